@@ -1,0 +1,171 @@
+"""Kernel-op API: the operators of ``chess_engine_4.kernels`` on the sm_100a library.
+
+Each function validates its arguments the way the reference does (``ValueError`` for
+device, dtype, rank and shape problems; src/chess_engine_4/kernels/dense.py:33-43,
+132-139, 366-382) and then calls the C ABI on the tensors' current CUDA stream.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _check_bf16_matrix(name: str, tensor: torch.Tensor) -> None:
+    if tensor.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if tensor.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must have dtype torch.bfloat16")
+    if tensor.ndim != 2 or not tensor.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous matrix")
+
+
+def _check_bf16_vector(name: str, tensor: torch.Tensor, size: int) -> None:
+    if tensor.device.type != "cuda" or tensor.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be a BF16 CUDA tensor")
+    if tuple(tensor.shape) != (size,) or not tensor.is_contiguous():
+        raise ValueError(f"{name} must be BF16 with shape [{size}]")
+
+
+def bf16_gemm(left: torch.Tensor, right: torch.Tensor) -> torch.Tensor:
+    """``left @ right.T`` in BF16 with FP32 accumulation (tcgen05 GEMM).
+
+    Mirrors ``_bf16_gemm`` (src/chess_engine_4/kernels/dense.py:116-129).
+    """
+
+    _check_bf16_matrix("left", left)
+    _check_bf16_matrix("right", right)
+    if left.shape[1] != right.shape[1]:
+        raise ValueError("BF16 GEMM reduction dimensions do not match")
+    if right.shape[0] % 16:
+        raise ValueError("BF16 GEMM output columns must be a multiple of 16")
+    if left.shape[1] % 8:
+        raise ValueError("BF16 GEMM reduction dimension must be a multiple of 8")
+    out = torch.empty(left.shape[0], right.shape[0], dtype=torch.bfloat16, device=left.device)
+    lib = _lib.library()
+    with torch.cuda.device(left.device):
+        _lib.check(
+            lib.ce4b_bf16_gemm(
+                left.data_ptr(),
+                right.data_ptr(),
+                out.data_ptr(),
+                left.shape[0],
+                right.shape[0],
+                left.shape[1],
+                _stream(left),
+            )
+        )
+    return out
+
+
+def rmsnorm_forward(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """Row RMSNorm, BF16 in/out, FP32 math (kernels/src/sm100/dense.cu:313-348)."""
+
+    _check_bf16_matrix("x", x)
+    _check_bf16_vector("weight", weight, x.shape[1])
+    out = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.check(
+            _lib.library().ce4b_rmsnorm_forward(
+                x.data_ptr(), weight.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1], eps,
+                _stream(x),
+            )
+        )
+    return out
+
+
+def swiglu_forward(gate_up: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` over a ``[rows, 2H]`` gate|up tensor (sm100/dense.cu:350-377)."""
+
+    _check_bf16_matrix("gate_up", gate_up)
+    if gate_up.shape[1] % 2:
+        raise ValueError("gate_up must have an even number of columns")
+    hidden_dim = gate_up.shape[1] // 2
+    hidden = torch.empty(gate_up.shape[0], hidden_dim, dtype=torch.bfloat16, device=gate_up.device)
+    with torch.cuda.device(gate_up.device):
+        _lib.check(
+            _lib.library().ce4b_swiglu_forward(
+                gate_up.data_ptr(), hidden.data_ptr(), gate_up.shape[0], hidden_dim,
+                _stream(gate_up),
+            )
+        )
+    return hidden
+
+
+def residual_add(out: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    """In place ``out = bf16(out + residual)`` (sm100/dense.cu:379-390)."""
+
+    _check_bf16_matrix("out", out)
+    _check_bf16_matrix("residual", residual)
+    if out.shape != residual.shape:
+        raise ValueError("residual must match out")
+    with torch.cuda.device(out.device):
+        _lib.check(
+            _lib.library().ce4b_residual_add(
+                out.data_ptr(), residual.data_ptr(), out.numel(), _stream(out)
+            )
+        )
+    return out
+
+
+def dense_block_forward(
+    x: torch.Tensor,
+    norm_weight: torch.Tensor,
+    gate_up_weight: torch.Tensor,
+    down_weight: torch.Tensor,
+    *,
+    precision: str,
+    eps: float = 1e-6,
+) -> torch.Tensor:
+    """One dense SwiGLU residual block: ``x + down(swiglu(gate_up(rmsnorm(x))))``.
+
+    Same arguments and checks as the reference operator
+    (src/chess_engine_4/kernels/dense.py:141-160, 357-392), except that any expansion
+    ratio whose hidden width is a multiple of 64 is accepted (the reference custom path
+    requires ratio 4).
+    """
+
+    _check_bf16_matrix("x", x)
+    d_model = x.shape[1]
+    if precision not in ("bf16", "mxfp8"):
+        raise ValueError(f"custom dense kernel does not support precision={precision!r}")
+    if precision != "bf16":
+        raise ValueError("dense_block_forward: only precision='bf16' is available")
+    _check_bf16_vector("norm_weight", norm_weight, d_model)
+    _check_bf16_matrix("gate_up_weight", gate_up_weight)
+    _check_bf16_matrix("down_weight", down_weight)
+    hidden_dim = down_weight.shape[1]
+    if tuple(gate_up_weight.shape) != (2 * hidden_dim, d_model):
+        raise ValueError(f"gate_up_weight must have shape [{2 * hidden_dim}, {d_model}]")
+    if tuple(down_weight.shape) != (d_model, hidden_dim):
+        raise ValueError(f"down_weight must have shape [{d_model}, {hidden_dim}]")
+    lib = _lib.library()
+    rows = x.shape[0]
+    ws_bytes = lib.ce4b_dense_block_workspace_size(rows, d_model, hidden_dim)
+    if ws_bytes < 0:
+        raise ValueError("invalid dense block extents")
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    out = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.check(
+            lib.ce4b_dense_block_forward(
+                x.data_ptr(),
+                norm_weight.data_ptr(),
+                gate_up_weight.data_ptr(),
+                down_weight.data_ptr(),
+                out.data_ptr(),
+                workspace.data_ptr(),
+                rows,
+                d_model,
+                hidden_dim,
+                eps,
+                _lib.PRECISION_BF16,
+                _stream(x),
+            )
+        )
+    return out

@@ -1,0 +1,280 @@
+// extern "C" entry points of libce4b200 (declared in include/ce4b200.h). Every entry point
+// converts exceptions to a status code and records the message for ce4b_last_error().
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+#include "model.h"
+
+namespace ce4b {
+
+namespace {
+
+thread_local std::string g_last_error;
+
+// Device error word written by bounded in-kernel waits (one per device context).
+__device__ int g_device_error_word;
+
+std::mutex g_mu;
+std::map<int, int*> g_error_words;
+std::map<int, int> g_sm_counts;
+
+int current_device() {
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  return dev;
+}
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    return CE4B_OK;
+  } catch (const Error& e) {
+    set_last_error(e.what());
+    return e.status;
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    return CE4B_ERR_INVALID_ARGUMENT;
+  } catch (...) {
+    set_last_error("unknown error");
+    return CE4B_ERR_INVALID_ARGUMENT;
+  }
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
+int* device_error_word() {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_error_words.find(dev);
+  if (it != g_error_words.end()) return it->second;
+  void* p = nullptr;
+  check_cuda(cudaGetSymbolAddress(&p, g_device_error_word), "cudaGetSymbolAddress(error word)");
+  g_error_words[dev] = static_cast<int*>(p);
+  return static_cast<int*>(p);
+}
+
+int sm_count() {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_mu);
+  auto it = g_sm_counts.find(dev);
+  if (it != g_sm_counts.end()) return it->second;
+  int n = 0;
+  check_cuda(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev), "SM count");
+  g_sm_counts[dev] = n;
+  return n;
+}
+
+}  // namespace ce4b
+
+using namespace ce4b;
+
+extern "C" {
+
+const char* ce4b_last_error(void) { return g_last_error.c_str(); }
+
+const char* ce4b_version(void) { return "ce4b200 0.1.0 (sm_100a)"; }
+
+int ce4b_check_device_error(int device, int* code_out) {
+  return guarded([&] {
+    require(code_out != nullptr, "code_out is null");
+    check_cuda(cudaSetDevice(device), "cudaSetDevice");
+    int* word = device_error_word();
+    check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    int code = 0;
+    check_cuda(cudaMemcpy(&code, word, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+    const int zero = 0;
+    check_cuda(cudaMemcpy(word, &zero, sizeof(int), cudaMemcpyHostToDevice), "clear error word");
+    *code_out = code;
+  });
+}
+
+// ------------------------------------------------------------------ model handle
+int ce4b_model_create(const ce4b_model_config* config, int device, int max_batch,
+                      ce4b_model** out) {
+  return guarded([&] {
+    require(config != nullptr && out != nullptr, "null argument");
+    *out = nullptr;
+    auto h = new ce4b_model;
+    try {
+      h->impl = std::make_unique<Model>();
+      h->impl->create(*config, device, max_batch);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int ce4b_model_set_tensor(ce4b_model* model, const char* name, const void* data, int dtype,
+                          int ndim, const int64_t* shape, int src_is_device) {
+  return guarded([&] {
+    require(model != nullptr && model->impl && name != nullptr, "null argument");
+    require(ndim >= 1 && ndim <= 4 && shape != nullptr, "bad tensor rank");
+    std::vector<int64_t> s(shape, shape + ndim);
+    model->impl->set_tensor(name, data, dtype, s, src_is_device != 0);
+  });
+}
+
+int ce4b_model_finalize(ce4b_model* model) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    model->impl->finalize();
+  });
+}
+
+int ce4b_model_load_safetensors(const char* path, int device, int max_batch, int precision,
+                                ce4b_model** out) {
+  return guarded([&] {
+    require(path != nullptr && out != nullptr, "null argument");
+    *out = nullptr;
+    auto h = new ce4b_model;
+    try {
+      h->impl = load_safetensors_model(path, device, max_batch, precision);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+  });
+}
+
+int ce4b_model_info_get(const ce4b_model* model, ce4b_model_info* info) {
+  return guarded([&] {
+    require(model != nullptr && model->impl && info != nullptr, "null argument");
+    const Model& m = *model->impl;
+    info->d_model = m.cfg.d_model;
+    info->depth = m.cfg.depth;
+    info->history_length = m.cfg.history_length;
+    info->policy_size = m.policy_size;
+    info->maximum_batch_size = m.max_batch;
+    info->hidden_dim = m.dense_hidden;
+    info->expert_hidden_dim = m.expert_hidden;
+    info->arch = m.cfg.arch;
+    info->weight_bytes = static_cast<int64_t>(m.arena_bytes);
+    info->workspace_bytes = static_cast<int64_t>(m.workspace_bytes);
+  });
+}
+
+int ce4b_model_forward(ce4b_model* model, int input_layout, void* input_dev,
+                       const void* scalars_dev, int batch, float* policy_dev, float* wdl_dev,
+                       float* moves_left_dev, int wdl_probs, int normalize_in_place,
+                       int32_t* tokens_per_expert_dev, void* stream) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    check_cuda(cudaSetDevice(model->impl->device), "cudaSetDevice");
+    model->impl->forward(input_layout, input_dev, scalars_dev, batch, policy_dev, wdl_dev,
+                         moves_left_dev, wdl_probs, normalize_in_place, tokens_per_expert_dev,
+                         as_stream(stream));
+  });
+}
+
+int ce4b_model_evaluate(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
+                        float* host_policy, float* host_wdl, float* host_moves_left) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    model->impl->evaluate(host_planes, batch, host_policy, host_wdl, host_moves_left);
+  });
+}
+
+void ce4b_model_destroy(ce4b_model* model) { delete model; }
+
+// ------------------------------------------------------------------ kernel-op API
+int ce4b_bf16_gemm(const void* a_dev, const void* b_dev, void* c_dev, int m, int n, int k,
+                   void* stream) {
+  return guarded([&] {
+    require(m >= 1 && n >= 1 && k >= 1, "GEMM extents must be positive");
+    require(n % 16 == 0, "GEMM N must be a multiple of 16");
+    require(k % 8 == 0, "GEMM K must be a multiple of 8");
+    require(c_dev != nullptr, "null output");
+    const CUtensorMap ta = make_tmap_bf16(a_dev, m, k, k, 128);
+    const CUtensorMap tb = make_tmap_bf16(b_dev, n, k, k, 128);
+    gemm_store_bf16(ta, tb, static_cast<bf16*>(c_dev), n, m, n, k, as_stream(stream));
+  });
+}
+
+int ce4b_rmsnorm_forward(const void* x_dev, const void* weight_dev, void* out_dev, int rows,
+                         int width, float eps, void* stream) {
+  return guarded([&] {
+    require(x_dev && weight_dev && out_dev, "null pointer");
+    require(rows >= 1 && width >= 1, "extents must be positive");
+    rmsnorm_rows(static_cast<const bf16*>(x_dev), static_cast<const bf16*>(weight_dev),
+                 static_cast<bf16*>(out_dev), rows, width, eps, as_stream(stream));
+  });
+}
+
+int ce4b_swiglu_forward(const void* gate_up_dev, void* hidden_dev, int rows, int hidden_dim,
+                        void* stream) {
+  return guarded([&] {
+    require(gate_up_dev && hidden_dev, "null pointer");
+    require(rows >= 1 && hidden_dim >= 1, "extents must be positive");
+    swiglu_rows(static_cast<const bf16*>(gate_up_dev), static_cast<bf16*>(hidden_dev), rows,
+                hidden_dim, as_stream(stream));
+  });
+}
+
+int ce4b_residual_add(void* out_dev, const void* residual_dev, int64_t elements, void* stream) {
+  return guarded([&] {
+    require(out_dev && residual_dev, "null pointer");
+    require(elements >= 0, "negative element count");
+    if (elements == 0) return;
+    residual_add(static_cast<bf16*>(out_dev), static_cast<const bf16*>(residual_dev), elements,
+                 as_stream(stream));
+  });
+}
+
+int64_t ce4b_dense_block_workspace_size(int rows, int d_model, int hidden_dim) {
+  if (rows < 1 || d_model < 1 || hidden_dim < 1) return -1;
+  const int64_t r = (static_cast<int64_t>(rows) + 127) / 128 * 128;
+  const int64_t a = (r * d_model * 2 + 255) / 256 * 256;
+  const int64_t b = (r * hidden_dim * 2 + 255) / 256 * 256;
+  return a + b;
+}
+
+int ce4b_dense_block_forward(const void* x_dev, const void* norm_weight_dev,
+                             const void* gate_up_weight_dev, const void* down_weight_dev,
+                             void* out_dev, void* workspace_dev, int rows, int d_model,
+                             int hidden_dim, float eps, int precision, void* stream) {
+  return guarded([&] {
+    require(x_dev && norm_weight_dev && gate_up_weight_dev && down_weight_dev && out_dev &&
+                workspace_dev,
+            "null pointer");
+    require(rows >= 1, "rows must be positive");
+    require(d_model >= 64 && d_model % 64 == 0, "d_model must be a multiple of 64");
+    require(hidden_dim >= 64 && hidden_dim % 64 == 0, "hidden_dim must be a multiple of 64");
+    if (precision != CE4B_PRECISION_BF16) {
+      fail(CE4B_ERR_UNSUPPORTED, "dense block: only BF16 precision is available");
+    }
+    require((reinterpret_cast<uintptr_t>(workspace_dev) & 255u) == 0,
+            "workspace must be 256-byte aligned");
+    cudaStream_t s = as_stream(stream);
+    const int64_t r = (static_cast<int64_t>(rows) + 127) / 128 * 128;
+    auto* normalized = static_cast<bf16*>(workspace_dev);
+    auto* hidden = reinterpret_cast<bf16*>(static_cast<uint8_t*>(workspace_dev) +
+                                           (r * d_model * 2 + 255) / 256 * 256);
+    rmsnorm_rows(static_cast<const bf16*>(x_dev), static_cast<const bf16*>(norm_weight_dev),
+                 normalized, rows, d_model, eps, s);
+    const CUtensorMap t_norm = make_tmap_bf16(normalized, rows, d_model, d_model, 128);
+    const CUtensorMap t_gu = make_tmap_bf16(gate_up_weight_dev, 2 * hidden_dim, d_model, d_model,
+                                            static_cast<uint32_t>(swiglu_chunk(hidden_dim)));
+    gemm_swiglu(t_norm, t_gu, hidden, rows, hidden_dim, d_model, s);
+    check_cuda(cudaMemcpyAsync(out_dev, x_dev, static_cast<size_t>(rows) * d_model * 2,
+                               cudaMemcpyDeviceToDevice, s),
+               "copy residual");
+    const CUtensorMap t_hidden = make_tmap_bf16(hidden, rows, hidden_dim, hidden_dim, 128);
+    const CUtensorMap t_down = make_tmap_bf16(down_weight_dev, d_model, hidden_dim, hidden_dim,
+                                              static_cast<uint32_t>(resnorm_bn(d_model)));
+    gemm_resnorm(t_hidden, t_down, static_cast<bf16*>(out_dev), nullptr, nullptr, nullptr, rows,
+                 d_model, hidden_dim, eps, s);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,239 @@
+// Memory-bound kernels around the GEMMs: input-plane expansion (three input layouts),
+// standalone RMSNorm / SwiGLU / residual add for the kernel-op API.
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace ce4b {
+
+namespace {
+
+// Source plane of selected plane `p` under history selection
+// (src/chess_engine_4/model/dense.py:45-51; kernels/src/inference/runtime.cu:197-200).
+__device__ __forceinline__ int source_plane(int p, int history_planes) {
+  return p < history_planes ? p : kHistoryPlanes + (p - history_planes);
+}
+
+// One thread = 8 squares (one 16-byte BF16 chunk) of one selected plane.
+__global__ void expand_lc0_kernel(const ce4b_input_plane* __restrict__ planes, bf16* __restrict__ out,
+                                  int batch, int history) {
+  const int sel = selected_planes(history);
+  const int hp = history * kPlanesPerHistory;
+  const int64_t chunks = static_cast<int64_t>(batch) * sel * 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int chunk = static_cast<int>(i % 8);
+    const int p = static_cast<int>((i / 8) % sel);
+    const int64_t b = i / (8 * sel);
+    const ce4b_input_plane pl = planes[b * kInputPlanes + source_plane(p, hp)];
+    float v = pl.value;
+    if (p == hp + 5) v = v / 99.0f;
+    const uint32_t bits = static_cast<uint32_t>(pl.mask >> (chunk * 8)) & 0xFFu;
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = ((bits >> j) & 1u) ? v : 0.0f;
+    uint4 o;
+    o.x = pack_bf16x2(f[0], f[1]);
+    o.y = pack_bf16x2(f[2], f[3]);
+    o.z = pack_bf16x2(f[4], f[5]);
+    o.w = pack_bf16x2(f[6], f[7]);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+// Dense planes [B, 112, 64] (f32 or bf16) -> BF16 [B, sel*64]; rule-50 plane / 99.
+template <typename T>
+__global__ void expand_dense_kernel(T* __restrict__ planes, bf16* __restrict__ out, int batch,
+                                    int history, int write_back) {
+  const int sel = selected_planes(history);
+  const int hp = history * kPlanesPerHistory;
+  const int64_t chunks = static_cast<int64_t>(batch) * sel * 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int chunk = static_cast<int>(i % 8);
+    const int p = static_cast<int>((i / 8) % sel);
+    const int64_t b = i / (8 * sel);
+    const int src = source_plane(p, hp);
+    T* in = planes + (b * kInputPlanes + src) * 64 + chunk * 8;
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if constexpr (sizeof(T) == 4) {
+        f[j] = in[j];
+      } else {
+        f[j] = __bfloat162float(in[j]);
+      }
+    }
+    if (p == hp + 5) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if constexpr (sizeof(T) == 4) {
+          f[j] = f[j] / 99.0f;
+          if (write_back) in[j] = f[j];
+        } else {
+          // BF16 input: the in-place division happens in BF16, as div_ on a BF16 tensor.
+          const T q = __float2bfloat16(f[j] / 99.0f);
+          f[j] = __bfloat162float(q);
+          if (write_back) in[j] = q;
+        }
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(f[0], f[1]);
+    o.y = pack_bf16x2(f[2], f[3]);
+    o.z = pack_bf16x2(f[4], f[5]);
+    o.w = pack_bf16x2(f[6], f[7]);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+// Packed training layout: u8 [B, 104, 8] (bit j of byte r, MSB first, is square r*8+j)
+// plus [B, 8] aux-plane scalars (src/chess_engine_4/training/packed_input.py:24-47).
+template <typename S>
+__global__ void expand_packed_kernel(const uint8_t* __restrict__ packed, const S* __restrict__ scalars,
+                                     bf16* __restrict__ out, int batch, int history) {
+  const int sel = selected_planes(history);
+  const int hp = history * kPlanesPerHistory;
+  const int64_t chunks = static_cast<int64_t>(batch) * sel * 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int chunk = static_cast<int>(i % 8);
+    const int p = static_cast<int>((i / 8) % sel);
+    const int64_t b = i / (8 * sel);
+    const int src = source_plane(p, hp);
+    float f[8];
+    if (src < kHistoryPlanes) {
+      const uint32_t byte = packed[(b * kHistoryPlanes + src) * 8 + chunk];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = ((byte >> (7 - j)) & 1u) ? 1.0f : 0.0f;
+    } else {
+      float v;
+      if constexpr (sizeof(S) == 4) {
+        v = scalars[b * 8 + (src - kHistoryPlanes)];
+      } else {
+        v = __bfloat162float(scalars[b * 8 + (src - kHistoryPlanes)]);
+      }
+      if (p == hp + 5) {
+        if constexpr (sizeof(S) == 4) {
+          v = v / 99.0f;
+        } else {
+          v = bf16_round(v / 99.0f);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = v;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(f[0], f[1]);
+    o.y = pack_bf16x2(f[2], f[3]);
+    o.z = pack_bf16x2(f[4], f[5]);
+    o.w = pack_bf16x2(f[6], f[7]);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+// One warp per row.
+__global__ void rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                               bf16* __restrict__ out, int rows, int width, float eps) {
+  const int warps = blockDim.x / 32;
+  const int row = blockIdx.x * warps + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const bf16* xr = x + static_cast<int64_t>(row) * width;
+  float ss = 0.0f;
+  for (int c = lane; c < width; c += 32) {
+    const float v = __bfloat162float(xr[c]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(width) + eps);
+  bf16* orow = out + static_cast<int64_t>(row) * width;
+  for (int c = lane; c < width; c += 32) {
+    orow[c] = __float2bfloat16((__bfloat162float(xr[c]) * inv) * __bfloat162float(w[c]));
+  }
+}
+
+__global__ void swiglu_kernel(const bf16* __restrict__ gate_up, bf16* __restrict__ hidden, int rows,
+                              int hidden_dim) {
+  const int64_t n = static_cast<int64_t>(rows) * hidden_dim;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / hidden_dim;
+    const int64_t c = i - r * hidden_dim;
+    const float g = __bfloat162float(gate_up[r * 2 * hidden_dim + c]);
+    const float u = __bfloat162float(gate_up[r * 2 * hidden_dim + hidden_dim + c]);
+    hidden[i] = __float2bfloat16(g / (1.0f + expf(-g)) * u);
+  }
+}
+
+__global__ void residual_add_kernel(bf16* __restrict__ out, const bf16* __restrict__ residual,
+                                    int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    out[i] = __float2bfloat16(__bfloat162float(out[i]) + __bfloat162float(residual[i]));
+  }
+}
+
+int grid_for(int64_t work, int threads) {
+  const int64_t blocks = (work + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+}  // namespace
+
+void expand_input(int layout, const void* input, const void* scalars, int batch, int history,
+                  bf16* out, int write_back_rule50, cudaStream_t s) {
+  const int64_t chunks = static_cast<int64_t>(batch) * selected_planes(history) * 8;
+  const int threads = 256;
+  const int grid = grid_for(chunks, threads);
+  switch (layout) {
+    case CE4B_INPUT_LC0:
+      expand_lc0_kernel<<<grid, threads, 0, s>>>(static_cast<const ce4b_input_plane*>(input), out,
+                                                 batch, history);
+      break;
+    case CE4B_INPUT_F32_PLANES:
+      expand_dense_kernel<float><<<grid, threads, 0, s>>>(
+          static_cast<float*>(const_cast<void*>(input)), out, batch, history, write_back_rule50);
+      break;
+    case CE4B_INPUT_BF16_PLANES:
+      expand_dense_kernel<bf16><<<grid, threads, 0, s>>>(
+          static_cast<bf16*>(const_cast<void*>(input)), out, batch, history, write_back_rule50);
+      break;
+    case CE4B_INPUT_PACKED_F32:
+      require(scalars != nullptr, "packed input needs scalars");
+      expand_packed_kernel<float><<<grid, threads, 0, s>>>(
+          static_cast<const uint8_t*>(input), static_cast<const float*>(scalars), out, batch,
+          history);
+      break;
+    case CE4B_INPUT_PACKED_BF16:
+      require(scalars != nullptr, "packed input needs scalars");
+      expand_packed_kernel<bf16><<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(input),
+                                                          static_cast<const bf16*>(scalars), out,
+                                                          batch, history);
+      break;
+    default:
+      fail(CE4B_ERR_INVALID_ARGUMENT, "unknown input layout " + std::to_string(layout));
+  }
+  check_cuda(cudaGetLastError(), "expand_input launch");
+}
+
+void rmsnorm_rows(const bf16* x, const bf16* w, bf16* out, int rows, int width, float eps,
+                  cudaStream_t s) {
+  const int warps = 8;
+  rmsnorm_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, s>>>(x, w, out, rows, width, eps);
+  check_cuda(cudaGetLastError(), "rmsnorm launch");
+}
+
+void swiglu_rows(const bf16* gate_up, bf16* hidden, int rows, int hidden_dim, cudaStream_t s) {
+  const int64_t n = static_cast<int64_t>(rows) * hidden_dim;
+  swiglu_kernel<<<grid_for(n, 256), 256, 0, s>>>(gate_up, hidden, rows, hidden_dim);
+  check_cuda(cudaGetLastError(), "swiglu launch");
+}
+
+void residual_add(bf16* out, const bf16* residual, int64_t elements, cudaStream_t s) {
+  residual_add_kernel<<<grid_for(elements, 256), 256, 0, s>>>(out, residual, elements);
+  check_cuda(cudaGetLastError(), "residual_add launch");
+}
+
+}  // namespace ce4b

@@ -1,0 +1,187 @@
+// Host launchers for the tcgen05 GEMM instantiations used by the forward path, plus the
+// TMA tensor-map helper.
+#include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "gemm.cuh"
+#include "internal.h"
+
+namespace ce4b {
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  if (fn == nullptr) fail(CE4B_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// Opt each kernel instantiation into the dynamic shared memory it needs, once per device.
+template <class K>
+void ensure_smem(K kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return;
+  check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+             "cudaFuncSetAttribute(max dynamic smem)");
+  done.insert(key);
+}
+
+template <class K, class... Args>
+void launch(K kernel, dim3 grid, int smem, int cluster_x, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (cluster_x > 0) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  check_cuda(cudaLaunchKernelEx(&cfg, kernel, args...), "gemm launch");
+}
+
+int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                           uint32_t box_rows) {
+  require(ptr != nullptr, "tensor map: null pointer");
+  require((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0, "tensor map: base not 16-byte aligned");
+  require((ld_elems * 2) % 16 == 0, "tensor map: row stride not a multiple of 16 bytes");
+  require(rows >= 1 && cols >= 1 && box_rows >= 1 && box_rows <= 256, "tensor map: bad extent");
+  CUtensorMap map;
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {ld_elems * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+                                 gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(CE4B_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return map;
+}
+
+// ------------------------------------------------------------------ plain store
+void gemm_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, bf16* c, int ldc, int m, int n,
+                     int k, cudaStream_t s) {
+  constexpr int BN = 128, NS = 6, NA = 2;
+  using Epi = EpiStoreBF16<BN>;
+  auto kernel = gemm_tc_kernel<BN, NS, NA, 1, false, DenseSched, Epi>;
+  constexpr int smem = GemmSmem<BN, NS, NA>::kBytes;
+  ensure_smem(kernel, smem);
+  DenseSched sched{m, ceil_div(n, BN), ceil_div(m, kBM) * ceil_div(n, BN), BN, 0};
+  typename Epi::Params ep{c, ldc, n};
+  const int grid = std::min(sched.num_tiles, sm_count());
+  launch(kernel, dim3(grid), smem, 0, s, tA, tB, sched, ep, ceil_div(k, kBK), device_error_word());
+}
+
+// ------------------------------------------------------------------ SwiGLU
+int swiglu_chunk(int hidden) { return hidden % 128 == 0 ? 128 : 64; }
+
+void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, bf16* hidden, int m, int hidden_dim,
+                 int k, cudaStream_t s) {
+  const int hc = swiglu_chunk(hidden_dim);
+  require(hidden_dim % hc == 0, "SwiGLU hidden dim must be a multiple of 64");
+  DenseSched sched{m, hidden_dim / hc, ceil_div(m, kBM) * (hidden_dim / hc), hc, hidden_dim};
+  const int grid = std::min(sched.num_tiles, sm_count());
+  if (hc == 128) {
+    constexpr int BN = 256, NS = 4, NA = 2;
+    using Epi = EpiSwiGLU<128>;
+    auto kernel = gemm_tc_kernel<BN, NS, NA, 2, false, DenseSched, Epi>;
+    constexpr int smem = GemmSmem<BN, NS, NA>::kBytes;
+    ensure_smem(kernel, smem);
+    typename Epi::Params ep{hidden, hidden_dim};
+    launch(kernel, dim3(grid), smem, 0, s, tA, tB, sched, ep, ceil_div(k, kBK), device_error_word());
+  } else {
+    constexpr int BN = 128, NS = 6, NA = 2;
+    using Epi = EpiSwiGLU<64>;
+    auto kernel = gemm_tc_kernel<BN, NS, NA, 2, false, DenseSched, Epi>;
+    constexpr int smem = GemmSmem<BN, NS, NA>::kBytes;
+    ensure_smem(kernel, smem);
+    typename Epi::Params ep{hidden, hidden_dim};
+    launch(kernel, dim3(grid), smem, 0, s, tA, tB, sched, ep, ceil_div(k, kBK), device_error_word());
+  }
+}
+
+// ------------------------------------------------------------------ residual + RMSNorm
+int resnorm_bn(int d) {
+  if (d % 128 == 0 && d / 128 <= kMaxClusterN) return 128;
+  if (d % 256 == 0 && d / 256 <= kMaxClusterN) return 256;
+  if (d % 64 == 0 && d / 64 <= kMaxClusterN) return 64;
+  fail(CE4B_ERR_UNSUPPORTED, "d_model " + std::to_string(d) +
+                                 " is not supported (multiple of 64, at most 2048)");
+}
+
+template <int BN, int NS>
+static void gemm_resnorm_bn(const CUtensorMap& tA, const CUtensorMap& tB, bf16* x,
+                            const bf16* bias, const bf16* norm_w, bf16* nout, int m, int d, int k,
+                            float eps, cudaStream_t s) {
+  using Epi = EpiResNorm<BN>;
+  auto kernel = gemm_tc_kernel<BN, NS, 1, 1, true, DenseSched, Epi>;
+  constexpr int smem = GemmSmem<BN, NS, 1>::kBytes;
+  ensure_smem(kernel, smem);
+  const int cn = d / BN;
+  DenseSched sched{m, cn, ceil_div(m, kBM) * cn, BN, 0};
+  typename Epi::Params ep{x,   bias, norm_w, nout, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
+                          cn, eps};
+  // One tile per CTA: the cluster's CTAs cover one 128-row block across the full width.
+  launch(kernel, dim3(sched.num_tiles), smem, cn, s, tA, tB, sched, ep, ceil_div(k, kBK),
+         device_error_word());
+}
+
+void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, bf16* x, const bf16* bias,
+                  const bf16* norm_w, bf16* nout, int m, int d, int k, float eps, cudaStream_t s) {
+  switch (resnorm_bn(d)) {
+    case 64: gemm_resnorm_bn<64, 8>(tA, tB, x, bias, norm_w, nout, m, d, k, eps, s); break;
+    case 128: gemm_resnorm_bn<128, 6>(tA, tB, x, bias, norm_w, nout, m, d, k, eps, s); break;
+    default: gemm_resnorm_bn<256, 4>(tA, tB, x, bias, norm_w, nout, m, d, k, eps, s); break;
+  }
+}
+
+// ------------------------------------------------------------------ heads
+void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, float* policy,
+                float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,
+                int wdl_probs, cudaStream_t s) {
+  constexpr int BN = 256, NS = 4, NA = 2;
+  using Epi = EpiHeads;
+  auto kernel = gemm_tc_kernel<BN, NS, NA, 1, false, DenseSched, Epi>;
+  constexpr int smem = GemmSmem<BN, NS, NA>::kBytes;
+  ensure_smem(kernel, smem);
+  const int n_total = policy_storage + 64;
+  DenseSched sched{m, ceil_div(n_total, BN), ceil_div(m, kBM) * ceil_div(n_total, BN), BN, 0};
+  typename Epi::Params ep{bias, policy, wdl, moves_left, policy_size, policy_storage, n_total,
+                          wdl_probs};
+  const int grid = std::min(sched.num_tiles, sm_count());
+  launch(kernel, dim3(grid), smem, 0, s, tA, tB, sched, ep, ceil_div(d, kBK), device_error_word());
+}
+
+}  // namespace ce4b

@@ -1,0 +1,86 @@
+// Internal host-side declarations shared by the translation units of libce4b200.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "../../include/ce4b200.h"
+
+#ifdef __CUDACC__
+#define CE4B_HD __host__ __device__
+#else
+#define CE4B_HD
+#endif
+
+namespace ce4b {
+
+using bf16 = __nv_bfloat16;
+
+// Error carrying a C-ABI status code; converted to a return value at the ABI edge.
+struct Error : std::runtime_error {
+  int status;
+  Error(int s, const std::string& msg) : std::runtime_error(msg), status(s) {}
+};
+
+[[noreturn]] inline void fail(int status, const std::string& msg) { throw Error(status, msg); }
+
+inline void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(CE4B_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+inline void require(bool cond, const std::string& msg) {
+  if (!cond) fail(CE4B_ERR_INVALID_ARGUMENT, msg);
+}
+
+// Per-thread message of the last failed ABI call.
+void set_last_error(const std::string& msg);
+
+// Device error word shared by all kernels of the current device (bounded-wait timeouts).
+int* device_error_word();
+
+int sm_count();
+
+// ---------------------------------------------------------------- tensor maps
+// 2-D BF16 tensor map, 128-byte swizzle, box = 64 (K) x box_rows. Throws on bad alignment.
+CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                           uint32_t box_rows);
+
+// ---------------------------------------------------------------- GEMM launchers
+// C[M,N] = A[M,K] . B[N,K]^T, BF16 out (row stride ldc), N % 16 == 0.
+void gemm_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB128, bf16* c, int ldc, int m,
+                     int n, int k, cudaStream_t s);
+// hidden[M,h] = SwiGLU over W_gu [2h, K] (gate rows first); tB box rows must equal hc.
+int swiglu_chunk(int hidden);  // 128 if hidden % 128 == 0, else 64
+void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, bf16* hidden, int m, int hidden_dim,
+                 int k, cudaStream_t s);
+// Residual/bias epilogue with optional fused RMSNorm; tB box rows must equal resnorm_bn(d).
+int resnorm_bn(int d);
+void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, bf16* x, const bf16* bias,
+                  const bf16* norm_w, bf16* nout, int m, int d, int k, float eps, cudaStream_t s);
+// Heads over the concatenated [policy | wdl | moves-left] matrix; tB box rows 256.
+void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, float* policy,
+                float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,
+                int wdl_probs, cudaStream_t s);
+
+// ---------------------------------------------------------------- elementwise
+// Expand an input batch into the BF16 GEMM operand [B, selected_planes * 64].
+void expand_input(int layout, const void* input, const void* scalars, int batch, int history,
+                  bf16* out, int write_back_rule50, cudaStream_t s);
+void rmsnorm_rows(const bf16* x, const bf16* w, bf16* out, int rows, int width, float eps,
+                  cudaStream_t s);
+void swiglu_rows(const bf16* gate_up, bf16* hidden, int rows, int hidden_dim, cudaStream_t s);
+void residual_add(bf16* out, const bf16* residual, int64_t elements, cudaStream_t s);
+
+constexpr int kInputPlanes = 112;
+constexpr int kHistoryPlanes = 104;
+constexpr int kPlanesPerHistory = 13;
+CE4B_HD inline int selected_planes(int history) {
+  return history * kPlanesPerHistory + (kInputPlanes - kHistoryPlanes);
+}
+
+}  // namespace ce4b

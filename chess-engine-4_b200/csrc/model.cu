@@ -1,0 +1,370 @@
+// Model handle: weight arena in the Safetensors v1 layout, activation workspace sized for
+// the maximum batch, TMA descriptors built once, and the per-layer forward schedule.
+//
+// Forward of a dense tower (B positions, width d, hidden h, L layers):
+//   expand planes -> A_in [B, 64*sel] BF16
+//   GEMM A_in . W_in^T, epilogue: x = bf16(acc + b_in), n = RMSNorm(x; block 0 weight)
+//   per layer: GEMM n . W_gu^T, epilogue SwiGLU -> hidden [B, h]
+//              GEMM hidden . W_d^T, epilogue: x = bf16(x + bf16(acc)), n = RMSNorm(x; next)
+//   GEMM n . [W_policy; W_wdl; W_ml]^T, epilogue: bias, BF16 round, FP32 outputs, WDL softmax
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+#include "model.h"
+#include "safetensors.h"
+
+namespace ce4b {
+
+namespace {
+
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+int64_t numel(const std::vector<int64_t>& s) {
+  int64_t n = 1;
+  for (auto v : s) n *= v;
+  return n;
+}
+
+std::string shape_str(const std::vector<int64_t>& s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); ++i) r += (i ? ", " : "") + std::to_string(s[i]);
+  return r + "]";
+}
+
+}  // namespace
+
+Model::~Model() {
+  if (device >= 0) cudaSetDevice(device);
+  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  if (stream) cudaStreamDestroy(stream);
+  if (arena) cudaFree(arena);
+  if (workspace) cudaFree(workspace);
+}
+
+void Model::add_slot(const std::string& name, std::vector<int64_t> shape, int dtype,
+                     size_t& cursor, bool pack) {
+  if (!pack) cursor = align256(cursor);
+  Slot s;
+  s.offset = cursor;
+  s.shape = std::move(shape);
+  s.dtype = dtype;
+  s.bytes = static_cast<size_t>(numel(s.shape)) * (dtype == CE4B_DTYPE_F32 ? 4 : 2);
+  cursor += s.bytes;
+  slots.emplace(name, s);
+}
+
+void Model::plan_weights() {
+  const int d = cfg.d_model;
+  size_t cur = 0;
+  add_slot("input.weight", {d, in_dim}, CE4B_DTYPE_BF16, cur);
+  add_slot("input.bias", {d}, CE4B_DTYPE_BF16, cur);
+  add_slot("final_norm.weight", {d}, CE4B_DTYPE_BF16, cur);
+  // The three head matrices (and their biases) are packed back to back so the heads run
+  // as one GEMM over [policy_storage + 64, d].
+  add_slot("policy.weight", {policy_storage, d}, CE4B_DTYPE_BF16, cur);
+  add_slot("wdl.weight", {32, d}, CE4B_DTYPE_BF16, cur, true);
+  add_slot("moves_left.weight", {32, d}, CE4B_DTYPE_BF16, cur, true);
+  add_slot("policy.bias", {policy_storage}, CE4B_DTYPE_BF16, cur);
+  add_slot("wdl.bias", {32}, CE4B_DTYPE_BF16, cur, true);
+  add_slot("moves_left.bias", {32}, CE4B_DTYPE_BF16, cur, true);
+  for (int l = 0; l < cfg.depth; ++l) {
+    const std::string p = "blocks." + std::to_string(l);
+    add_slot(p + ".norm.weight", {d}, CE4B_DTYPE_BF16, cur);
+    if (is_moe_layer(l)) {
+      add_slot(p + ".router.weight", {64, d}, CE4B_DTYPE_BF16, cur);
+      add_slot(p + ".router_qb_beta", {64}, CE4B_DTYPE_F32, cur);
+      add_slot(p + ".experts.gate_up.weight", {64, 2 * expert_hidden, d}, CE4B_DTYPE_BF16, cur);
+      add_slot(p + ".experts.down.weight", {64, d, expert_hidden}, CE4B_DTYPE_BF16, cur);
+    } else {
+      add_slot(p + ".gate_up.weight", {2 * dense_hidden, d}, CE4B_DTYPE_BF16, cur);
+      add_slot(p + ".down.weight", {d, dense_hidden}, CE4B_DTYPE_BF16, cur);
+    }
+  }
+  arena_bytes = align256(cur);
+}
+
+void Model::plan_workspace() {
+  const int d = cfg.d_model;
+  size_t cur = 0;
+  auto take = [&](size_t bytes) {
+    const size_t off = align256(cur);
+    cur = off + bytes;
+    return off;
+  };
+  const size_t r = static_cast<size_t>(rows_cap);
+  ws_off.planes = take(r * kInputPlanes * sizeof(ce4b_input_plane));
+  ws_off.a_in = take(r * in_dim * 2);
+  ws_off.x = take(r * d * 2);
+  ws_off.n = take(r * d * 2);
+  ws_off.hidden = take(r * std::max(dense_hidden, expert_hidden) * 2);
+  ws_off.policy = take(r * policy_size * 4);
+  ws_off.wdl = take(r * 3 * 4);
+  ws_off.moves_left = take(r * 4);
+  workspace_bytes = align256(cur);
+}
+
+bf16* Model::w(const std::string& name) const {
+  auto it = slots.find(name);
+  if (it == slots.end()) fail(CE4B_ERR_INVALID_ARGUMENT, "unknown tensor " + name);
+  return reinterpret_cast<bf16*>(arena + it->second.offset);
+}
+
+void Model::create(const ce4b_model_config& c, int dev, int maxb) {
+  cfg = c;
+  device = dev;
+  require(c.arch == CE4B_ARCH_DENSE || c.arch == CE4B_ARCH_MOE64A2, "unknown architecture");
+  require(c.d_model >= 64 && c.d_model % 64 == 0 && c.d_model <= 2048,
+          "d_model must be a multiple of 64 in [64, 2048]");
+  require(c.depth >= 1, "depth must be positive");
+  require(c.history_length >= 1 && c.history_length <= 8, "history_length must be in [1, 8]");
+  require(c.expansion_ratio > 0.0f, "expansion_ratio must be positive");
+  require(c.policy_size >= 1 && c.policy_storage_size >= c.policy_size,
+          "policy storage must hold the policy output");
+  require(c.policy_storage_size % 32 == 0, "policy storage size must be a multiple of 32");
+  require(maxb >= 1 && maxb <= (1 << 20), "max_batch must be in [1, 2^20]");
+  if (c.precision != CE4B_PRECISION_BF16) {
+    fail(CE4B_ERR_UNSUPPORTED, "only BF16 precision is available in this build");
+  }
+  if (c.arch == CE4B_ARCH_MOE64A2) {
+    require(c.depth % 2 == 0, "moe64a2 depth must be a positive even number");
+    fail(CE4B_ERR_UNSUPPORTED, "moe64a2 forward is not available in this build");
+  }
+  const int hid = static_cast<int>(static_cast<double>(c.d_model) * c.expansion_ratio);
+  dense_hidden = c.arch == CE4B_ARCH_DENSE ? hid : 4 * c.d_model;
+  expert_hidden = c.arch == CE4B_ARCH_MOE64A2 ? hid : 0;
+  require(dense_hidden % 64 == 0, "dense hidden dimension must be a multiple of 64");
+  require(expert_hidden % 64 == 0, "expert hidden dimension must be a multiple of 64");
+  sel = selected_planes(c.history_length);
+  in_dim = sel * 64;
+  policy_size = c.policy_size;
+  policy_storage = c.policy_storage_size;
+  max_batch = maxb;
+  rows_cap = (maxb + 127) / 128 * 128;
+  (void)resnorm_bn(c.d_model);  // validates width against the cluster limit
+
+  check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  plan_weights();
+  plan_workspace();
+  check_cuda(cudaMalloc(&arena, arena_bytes), "cudaMalloc weights");
+  check_cuda(cudaMemset(arena, 0, arena_bytes), "cudaMemset weights");
+  check_cuda(cudaMalloc(&workspace, workspace_bytes), "cudaMalloc workspace");
+  check_cuda(cudaMemset(workspace, 0, workspace_bytes), "cudaMemset workspace");
+  check_cuda(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "create stream");
+}
+
+void Model::set_tensor(const std::string& name, const void* data, int dtype,
+                       const std::vector<int64_t>& shape, bool src_device) {
+  auto it = slots.find(name);
+  if (it == slots.end()) fail(CE4B_ERR_INVALID_ARGUMENT, "model has no tensor named " + name);
+  Slot& s = it->second;
+  if (shape != s.shape) {
+    fail(CE4B_ERR_INVALID_ARGUMENT,
+         "tensor " + name + " has shape " + shape_str(shape) + ", expected " + shape_str(s.shape));
+  }
+  if (dtype != s.dtype) fail(CE4B_ERR_INVALID_ARGUMENT, "tensor " + name + " has the wrong dtype");
+  require(data != nullptr, "tensor data is null");
+  check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  check_cuda(cudaMemcpy(arena + s.offset, data, s.bytes,
+                        src_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice),
+             "copy tensor");
+  s.set = true;
+}
+
+void Model::finalize() {
+  for (const auto& kv : slots) {
+    if (!kv.second.set) fail(CE4B_ERR_NOT_READY, "model is missing tensor " + kv.first);
+  }
+  check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  const int d = cfg.d_model;
+  bf16* ws_a_in = reinterpret_cast<bf16*>(workspace + ws_off.a_in);
+  bf16* ws_n = reinterpret_cast<bf16*>(workspace + ws_off.n);
+  bf16* ws_hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);
+  tm_a_in = make_tmap_bf16(ws_a_in, rows_cap, in_dim, in_dim, 128);
+  tm_n = make_tmap_bf16(ws_n, rows_cap, d, d, 128);
+  tm_hidden = make_tmap_bf16(ws_hidden, rows_cap, dense_hidden, dense_hidden, 128);
+  const uint32_t bn = static_cast<uint32_t>(resnorm_bn(d));
+  tm_w_in = make_tmap_bf16(w("input.weight"), d, in_dim, in_dim, bn);
+  tm_heads = make_tmap_bf16(w("policy.weight"), policy_storage + 64, d, d, 256);
+  layers.clear();
+  for (int l = 0; l < cfg.depth; ++l) {
+    const std::string p = "blocks." + std::to_string(l);
+    Layer L;
+    L.moe = is_moe_layer(l);
+    L.norm = w(p + ".norm.weight");
+    if (!L.moe) {
+      const uint32_t hc = static_cast<uint32_t>(swiglu_chunk(dense_hidden));
+      L.tm_gate_up = make_tmap_bf16(w(p + ".gate_up.weight"), 2 * dense_hidden, d, d, hc);
+      L.tm_down = make_tmap_bf16(w(p + ".down.weight"), d, dense_hidden, dense_hidden, bn);
+    }
+    layers.push_back(L);
+  }
+  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  graphs.clear();
+  finalized = true;
+}
+
+void Model::forward(int layout, void* input, const void* scalars, int batch, float* policy,
+                    float* wdl, float* moves_left, int wdl_probs, int normalize_in_place,
+                    int32_t* tokens_per_expert, cudaStream_t s) {
+  (void)tokens_per_expert;
+  if (!finalized) fail(CE4B_ERR_NOT_READY, "model is not finalized");
+  require(batch >= 1 && batch <= max_batch,
+          "batch size " + std::to_string(batch) + " exceeds model capacity " +
+              std::to_string(max_batch));
+  require(input != nullptr && policy != nullptr && wdl != nullptr && moves_left != nullptr,
+          "null input or output pointer");
+  const int d = cfg.d_model;
+  const float eps = cfg.rms_norm_eps;
+  bf16* a_in = reinterpret_cast<bf16*>(workspace + ws_off.a_in);
+  bf16* x = reinterpret_cast<bf16*>(workspace + ws_off.x);
+  bf16* n = reinterpret_cast<bf16*>(workspace + ws_off.n);
+  bf16* hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);
+  const int write_back = normalize_in_place && cfg.history_length == 8;
+
+  expand_input(layout, input, scalars, batch, cfg.history_length, a_in, write_back, s);
+  const bf16* first_norm = cfg.depth > 0 ? layers[0].norm : w("final_norm.weight");
+  gemm_resnorm(tm_a_in, tm_w_in, x, w("input.bias"), first_norm, n, batch, d, in_dim, eps, s);
+  for (int l = 0; l < cfg.depth; ++l) {
+    const Layer& L = layers[l];
+    const bf16* next_norm = l + 1 < cfg.depth ? layers[l + 1].norm : w("final_norm.weight");
+    gemm_swiglu(tm_n, L.tm_gate_up, hidden, batch, dense_hidden, d, s);
+    gemm_resnorm(tm_hidden, L.tm_down, x, nullptr, next_norm, n, batch, d, dense_hidden, eps, s);
+  }
+  gemm_heads(tm_n, tm_heads, w("policy.bias"), policy, wdl, moves_left, batch, d, policy_size,
+             policy_storage, wdl_probs, s);
+}
+
+void Model::evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
+                     float* host_wdl, float* host_moves_left) {
+  if (!finalized) fail(CE4B_ERR_NOT_READY, "model is not finalized");
+  require(batch >= 1 && batch <= max_batch, "batch size exceeds model capacity");
+  require(host_planes && host_policy && host_wdl && host_moves_left, "null host buffer");
+  check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  auto* planes = reinterpret_cast<ce4b_input_plane*>(workspace + ws_off.planes);
+  float* pol = reinterpret_cast<float*>(workspace + ws_off.policy);
+  float* wdl = reinterpret_cast<float*>(workspace + ws_off.wdl);
+  float* ml = reinterpret_cast<float*>(workspace + ws_off.moves_left);
+  check_cuda(cudaMemcpyAsync(planes, host_planes,
+                             static_cast<size_t>(batch) * kInputPlanes * sizeof(ce4b_input_plane),
+                             cudaMemcpyHostToDevice, stream),
+             "copy input planes");
+  auto it = graphs.find(batch);
+  if (it == graphs.end()) {
+    // First use of this batch size: warm up (kernel attributes, descriptors) outside the
+    // capture, then capture the forward into a graph.
+    forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
+    check_cuda(cudaStreamSynchronize(stream), "warm-up forward");
+    check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
+    } catch (...) {
+      cudaGraph_t g = nullptr;
+      cudaStreamEndCapture(stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    cudaGraph_t graph = nullptr;
+    check_cuda(cudaStreamEndCapture(stream, &graph), "end capture");
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t st = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    check_cuda(st, "instantiate graph");
+    it = graphs.emplace(batch, exec).first;
+  }
+  check_cuda(cudaGraphLaunch(it->second, stream), "launch graph");
+  check_cuda(cudaMemcpyAsync(host_policy, pol, static_cast<size_t>(batch) * policy_size * 4,
+                             cudaMemcpyDeviceToHost, stream),
+             "copy policy");
+  check_cuda(cudaMemcpyAsync(host_wdl, wdl, static_cast<size_t>(batch) * 3 * 4,
+                             cudaMemcpyDeviceToHost, stream),
+             "copy wdl");
+  check_cuda(cudaMemcpyAsync(host_moves_left, ml, static_cast<size_t>(batch) * 4,
+                             cudaMemcpyDeviceToHost, stream),
+             "copy moves left");
+  check_cuda(cudaStreamSynchronize(stream), "synchronize evaluation");
+}
+
+// ------------------------------------------------------------------ Safetensors loading
+namespace {
+
+const std::string& meta(const SafetensorsFile& f, const std::string& key) {
+  auto it = f.metadata.find(key);
+  if (it == f.metadata.end()) fail(CE4B_ERR_IO, "model metadata is missing " + key);
+  return it->second;
+}
+
+int meta_int(const SafetensorsFile& f, const std::string& key) {
+  try {
+    return std::stoi(meta(f, key));
+  } catch (const Error&) {
+    throw;
+  } catch (...) {
+    fail(CE4B_ERR_IO, "model metadata " + key + " is not an integer");
+  }
+}
+
+float meta_float(const SafetensorsFile& f, const std::string& key) {
+  try {
+    return std::stof(meta(f, key));
+  } catch (const Error&) {
+    throw;
+  } catch (...) {
+    fail(CE4B_ERR_IO, "model metadata " + key + " is not a number");
+  }
+}
+
+}  // namespace
+
+std::unique_ptr<Model> load_safetensors_model(const std::string& path, int device, int max_batch,
+                                              int precision) {
+  const SafetensorsFile f = read_safetensors(path);
+  // Contract checks of kernels/src/inference/runtime.cu:348-396.
+  if (meta(f, "format") != "chess-engine-4" || meta(f, "format_version") != "1") {
+    fail(CE4B_ERR_UNSUPPORTED, "unsupported model format");
+  }
+  const std::string arch = meta(f, "architecture");
+  if (arch != "dense" && arch != "moe64a2") {
+    fail(CE4B_ERR_UNSUPPORTED, "unsupported model architecture: " + arch);
+  }
+  if (meta(f, "activation") != "swiglu" || meta(f, "input_format") != "lc0-classical-112" ||
+      meta(f, "input_normalization") != "history-select-rule50-div99-v1" ||
+      meta_int(f, "input_planes") != kInputPlanes || meta_int(f, "board_size") != 8) {
+    fail(CE4B_ERR_UNSUPPORTED, "unsupported model contract");
+  }
+  if (arch == "moe64a2" &&
+      (meta_int(f, "num_experts") != 64 || meta_int(f, "num_active_experts") != 2 ||
+       meta(f, "layer_pattern") != "alternating-moe-dense")) {
+    fail(CE4B_ERR_UNSUPPORTED, "unsupported MoE model contract");
+  }
+  ce4b_model_config c{};
+  c.arch = arch == "dense" ? CE4B_ARCH_DENSE : CE4B_ARCH_MOE64A2;
+  c.d_model = meta_int(f, "d_model");
+  c.depth = meta_int(f, "depth");
+  c.history_length = meta_int(f, "history_length");
+  c.expansion_ratio = meta_float(f, "expansion_ratio");
+  c.rms_norm_eps = meta_float(f, "rms_norm_eps");
+  c.policy_size = meta_int(f, "policy_size");
+  c.policy_storage_size = meta_int(f, "policy_storage_size");
+  c.precision = precision;
+  auto m = std::make_unique<Model>();
+  m->create(c, device, max_batch);
+  for (const auto& kv : m->slots) {
+    auto it = f.tensors.find(kv.first);
+    if (it == f.tensors.end()) fail(CE4B_ERR_IO, "model is missing tensor " + kv.first);
+    const SafetensorsTensor& t = it->second;
+    const int dtype = t.dtype == "BF16" ? CE4B_DTYPE_BF16 : (t.dtype == "F32" ? CE4B_DTYPE_F32 : -1);
+    if (dtype < 0) fail(CE4B_ERR_IO, "tensor " + kv.first + " has an unsupported dtype");
+    if (t.bytes != kv.second.bytes) fail(CE4B_ERR_IO, "tensor " + kv.first + " has a wrong size");
+    m->set_tensor(kv.first, t.data, dtype, t.shape, false);
+  }
+  m->finalize();
+  return m;
+}
+
+}  // namespace ce4b

@@ -1,0 +1,86 @@
+// Model handle behind the opaque ce4b_model of the C ABI.
+#pragma once
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+namespace ce4b {
+
+struct Model {
+  struct Slot {
+    size_t offset = 0;
+    size_t bytes = 0;
+    std::vector<int64_t> shape;
+    int dtype = CE4B_DTYPE_BF16;
+    bool set = false;
+  };
+  struct Layer {
+    bool moe = false;
+    const bf16* norm = nullptr;
+    CUtensorMap tm_gate_up{};
+    CUtensorMap tm_down{};
+  };
+  struct WorkspaceOffsets {
+    size_t planes = 0, a_in = 0, x = 0, n = 0, hidden = 0, policy = 0, wdl = 0, moves_left = 0;
+  };
+
+  ce4b_model_config cfg{};
+  int device = -1;
+  int max_batch = 0;
+  int rows_cap = 0;
+  int dense_hidden = 0;
+  int expert_hidden = 0;
+  int sel = 0;
+  int in_dim = 0;
+  int policy_size = 0;
+  int policy_storage = 0;
+
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::map<std::string, Slot> slots;
+  uint8_t* workspace = nullptr;
+  size_t workspace_bytes = 0;
+  WorkspaceOffsets ws_off;
+
+  CUtensorMap tm_a_in{}, tm_n{}, tm_hidden{}, tm_w_in{}, tm_heads{};
+  std::vector<Layer> layers;
+  bool finalized = false;
+  cudaStream_t stream = nullptr;
+  std::map<int, cudaGraphExec_t> graphs;
+
+  Model() = default;
+  Model(const Model&) = delete;
+  Model& operator=(const Model&) = delete;
+  ~Model();
+
+  bool is_moe_layer(int l) const { return cfg.arch == CE4B_ARCH_MOE64A2 && l % 2 == 0; }
+  void create(const ce4b_model_config& c, int device, int max_batch);
+  void set_tensor(const std::string& name, const void* data, int dtype,
+                  const std::vector<int64_t>& shape, bool src_device);
+  void finalize();
+  void forward(int layout, void* input, const void* scalars, int batch, float* policy, float* wdl,
+               float* moves_left, int wdl_probs, int normalize_in_place,
+               int32_t* tokens_per_expert, cudaStream_t s);
+  void evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
+                float* host_wdl, float* host_moves_left);
+
+ private:
+  void add_slot(const std::string& name, std::vector<int64_t> shape, int dtype, size_t& cursor,
+                bool pack = false);
+  void plan_weights();
+  void plan_workspace();
+  bf16* w(const std::string& name) const;
+};
+
+std::unique_ptr<Model> load_safetensors_model(const std::string& path, int device, int max_batch,
+                                              int precision);
+
+}  // namespace ce4b
+
+struct ce4b_model {
+  std::unique_ptr<ce4b::Model> impl;
+};

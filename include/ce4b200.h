@@ -1,0 +1,188 @@
+/*
+ * ce4b200 — C ABI of the B200 (sm_100a) forward path for the chess-engine-4
+ * position-evaluation networks (dense and moe64a2 SwiGLU towers).
+ *
+ * Conventions
+ *  - Every entry point returns an int status (CE4B_OK == 0). No exception crosses the
+ *    ABI. ce4b_last_error() returns the message of the calling thread's last failure.
+ *  - Pointers named *_dev are device pointers on the handle's (or current) device;
+ *    pointers named host_* are host pointers. BF16 tensors are raw uint16 storage.
+ *  - `stream` is a cudaStream_t passed as void*; NULL means the legacy default stream.
+ *    Work is enqueued asynchronously unless the function says it blocks.
+ *  - Matrices are row-major. "A . B^T" GEMMs take B as [N, K] (the nn.Linear weight
+ *    layout), K contiguous.
+ *  - One model handle belongs to one GPU. Calls on one handle must be serialised by
+ *    the caller; handles on different GPUs may be used concurrently.
+ */
+#ifndef CE4B200_H
+#define CE4B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CE4B_OK 0
+#define CE4B_ERR_INVALID_ARGUMENT 1
+#define CE4B_ERR_CUDA 2
+#define CE4B_ERR_UNSUPPORTED 3
+#define CE4B_ERR_IO 4
+#define CE4B_ERR_DEVICE_TIMEOUT 5
+#define CE4B_ERR_NOT_READY 6
+
+#define CE4B_ARCH_DENSE 0
+#define CE4B_ARCH_MOE64A2 1
+
+#define CE4B_PRECISION_BF16 0
+#define CE4B_PRECISION_MXFP8 1
+
+/* Input layouts accepted by ce4b_model_forward. */
+#define CE4B_INPUT_F32_PLANES 0  /* float  [B, 112, 8, 8]  (PyTorch model input)            */
+#define CE4B_INPUT_BF16_PLANES 1 /* bf16   [B, 112, 8, 8]                                    */
+#define CE4B_INPUT_LC0 2         /* ce4b_input_plane [B, 112] (lc0 engine input)             */
+#define CE4B_INPUT_PACKED_F32 3  /* uint8 [B, 104, 8] bit-packed MSB-first + float [B, 8]    */
+#define CE4B_INPUT_PACKED_BF16 4 /* uint8 [B, 104, 8] bit-packed MSB-first + bf16  [B, 8]    */
+
+#define CE4B_DTYPE_BF16 0
+#define CE4B_DTYPE_F32 1
+
+/* One lc0 input plane: square s (0..63) holds `value` if bit s of `mask` is set, else 0.
+ * Replaces chess_engine_4::inference::InputPlane
+ * (kernels/include/chess_engine_4/inference.h:10-13); same 16-byte size and layout. */
+typedef struct ce4b_input_plane {
+  uint64_t mask;
+  float value;
+  uint32_t reserved;
+} ce4b_input_plane;
+
+/* Model hyper-parameters; the fields of the Safetensors v1 metadata
+ * (src/chess_engine_4/release/export.py:199-219) and of DenseChessNetConfig /
+ * Moe64A2ChessNetConfig (src/chess_engine_4/model/dense.py:59-82, moe.py:74-102). */
+typedef struct ce4b_model_config {
+  int32_t arch;                /* CE4B_ARCH_*                                              */
+  int32_t d_model;             /* multiple of 64, <= 2048                                  */
+  int32_t depth;               /* layers; even for moe64a2                                 */
+  int32_t history_length;      /* 1..8                                                     */
+  float expansion_ratio;       /* dense hidden = int(d * ratio); moe: expert hidden        */
+  float rms_norm_eps;          /* 1e-6 in every reference config                           */
+  int32_t policy_size;         /* 1858                                                     */
+  int32_t policy_storage_size; /* 1888 (rows of policy.weight)                             */
+  int32_t precision;           /* CE4B_PRECISION_*                                         */
+} ce4b_model_config;
+
+typedef struct ce4b_model_info {
+  int32_t d_model;
+  int32_t depth;
+  int32_t history_length;
+  int32_t policy_size;
+  int32_t maximum_batch_size;
+  int32_t hidden_dim;       /* dense FFN hidden of dense layers                          */
+  int32_t expert_hidden_dim; /* 0 for dense models                                       */
+  int32_t arch;
+  int64_t weight_bytes;
+  int64_t workspace_bytes;
+} ce4b_model_info;
+
+typedef struct ce4b_model ce4b_model;
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* ce4b_last_error(void);
+
+/* Library version string. */
+const char* ce4b_version(void);
+
+/* Reads and clears the device error word written by bounded in-kernel waits that ran
+ * out (0 = no error). Blocks on `device` until prior work is done. */
+int ce4b_check_device_error(int device, int* code_out);
+
+/* ------------------------------------------------------------------ model handle
+ * Replaces chess_engine_4::inference::Model (kernels/include/chess_engine_4/inference.h:29-51,
+ * kernels/src/inference/runtime.cu:340-787) and the custom-kernel forward reached from
+ * DenseChessNet / Moe64A2ChessNet.forward (src/chess_engine_4/model/dense.py:188-199,
+ * moe.py:389-410). */
+
+/* Creates an empty model on `device` for batches up to `max_batch` positions. Weights
+ * are uploaded with ce4b_model_set_tensor and sealed with ce4b_model_finalize. */
+int ce4b_model_create(const ce4b_model_config* config, int device, int max_batch,
+                      ce4b_model** out);
+
+/* Copies one tensor into the model's weight arena. `name` and shape follow the
+ * Safetensors v1 contract (kernels/src/inference/runtime.cu:398-452), e.g.
+ * "input.weight" [d, 7168], "blocks.3.gate_up.weight" [2h, d]. `src_is_device` selects
+ * device-to-device or host-to-device copy. Blocks until the copy is done. */
+int ce4b_model_set_tensor(ce4b_model* model, const char* name, const void* data, int dtype,
+                          int ndim, const int64_t* shape, int src_is_device);
+
+/* Checks that every tensor is present and prepares derived data. Must be called after
+ * the last ce4b_model_set_tensor and before a forward. */
+int ce4b_model_finalize(ce4b_model* model);
+
+/* Loads a Safetensors v1 file (release/export.py format) and finalizes the model. */
+int ce4b_model_load_safetensors(const char* path, int device, int max_batch, int precision,
+                                ce4b_model** out);
+
+int ce4b_model_info_get(const ce4b_model* model, ce4b_model_info* info);
+
+/* Device-side forward on `stream`. `input_dev` is in layout `input_layout`;
+ * `scalars_dev` is the [B, 8] aux-plane scalars for the packed layouts (else NULL).
+ * Outputs: policy [B, policy_size] f32, wdl [B, 3] f32 (logits, or probabilities when
+ * wdl_probs != 0), moves_left [B] f32. For moe64a2, tokens_per_expert_dev receives
+ * [depth/2, 64] int32 counts (may be NULL). For CE4B_INPUT_F32_PLANES with
+ * `normalize_in_place` != 0 the rule-50 plane of the input is divided by 99 in place,
+ * as normalize_lc0_planes does (src/chess_engine_4/model/dense.py:34-42). */
+int ce4b_model_forward(ce4b_model* model, int input_layout, void* input_dev,
+                       const void* scalars_dev, int batch, float* policy_dev, float* wdl_dev,
+                       float* moves_left_dev, int wdl_probs, int normalize_in_place,
+                       int32_t* tokens_per_expert_dev, void* stream);
+
+/* Host-buffer evaluation, blocking: H2D of the planes, forward (CUDA graph per batch
+ * size), D2H of policy [B, policy_size], WDL probabilities [B, 3], moves-left [B].
+ * Mirrors Model::Evaluate (kernels/src/inference/runtime.cu:532-564). */
+int ce4b_model_evaluate(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
+                        float* host_policy, float* host_wdl, float* host_moves_left);
+
+void ce4b_model_destroy(ce4b_model* model);
+
+/* ------------------------------------------------------------------ kernel-op API
+ * Replaces the pybind operators of the reference extension (kernels/src/sm100/dense.cu:760-774)
+ * reached through src/chess_engine_4/kernels/dense.py. */
+
+/* C[M,N] = A[M,K] . B[N,K]^T in BF16 (FP32 accumulate). N % 16 == 0, K % 8 == 0.
+ * Replaces dense_bf16_gemm (src/chess_engine_4/kernels/dense.py:116-129). */
+int ce4b_bf16_gemm(const void* a_dev, const void* b_dev, void* c_dev, int m, int n, int k,
+                   void* stream);
+
+/* out = bf16(x * rsqrt(mean(x^2) + eps) * w) per row.
+ * Replaces dense_rmsnorm_forward (kernels/src/sm100/dense.cu:313-348). */
+int ce4b_rmsnorm_forward(const void* x_dev, const void* weight_dev, void* out_dev, int rows,
+                         int width, float eps, void* stream);
+
+/* hidden[r, j] = bf16(silu(gate_up[r, j]) * gate_up[r, H + j]).
+ * Replaces dense_swiglu_forward (kernels/src/sm100/dense.cu:350-377). */
+int ce4b_swiglu_forward(const void* gate_up_dev, void* hidden_dev, int rows, int hidden_dim,
+                        void* stream);
+
+/* out = bf16(out + residual), elementwise.
+ * Replaces dense_residual_add (kernels/src/sm100/dense.cu:379-390). */
+int ce4b_residual_add(void* out_dev, const void* residual_dev, int64_t elements, void* stream);
+
+/* Scratch bytes ce4b_dense_block_forward needs for `rows` rows. */
+int64_t ce4b_dense_block_workspace_size(int rows, int d_model, int hidden_dim);
+
+/* out = x + down(SwiGLU(gate_up(RMSNorm(x)))) for one dense block, BF16.
+ * gate_up_weight [2H, d] (gate rows first), down_weight [d, H]. `workspace_dev` holds
+ * ce4b_dense_block_workspace_size() bytes (256-byte aligned). precision must be
+ * CE4B_PRECISION_BF16. Replaces dense_block_forward
+ * (src/chess_engine_4/kernels/dense.py:141-160, 357-392). */
+int ce4b_dense_block_forward(const void* x_dev, const void* norm_weight_dev,
+                             const void* gate_up_weight_dev, const void* down_weight_dev,
+                             void* out_dev, void* workspace_dev, int rows, int d_model,
+                             int hidden_dim, float eps, int precision, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CE4B200_H */

@@ -1,0 +1,96 @@
+"""CPU oracle of the dense forward — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this module, as
+the checker; the product path (libce4b200) never calls it.
+
+Two restatements of the reference's dense tower on the same Safetensors-named weights:
+
+* ``mode="fp32"``: the reference's portable PyTorch model, ``PortableChessNet``
+  (src/chess_engine_4/model/reference.py:60-101, _DenseBlock :17-43), computed in FP32
+  with the BF16 weights upcast. History selection and the rule-50 / 99 normalisation
+  follow src/chess_engine_4/model/dense.py:34-51, 188-199. Pinned against outputs of the
+  reference itself (tests/golden/make_golden.py).
+* ``mode="bf16"``: the same network with the BF16 rounding points of the reference's
+  deployed forward (kernels/src/inference/runtime.cu:182-336, 578-645; TE's fused-bias
+  Linear for the input and head projections): inputs rounded to BF16; every GEMM
+  accumulates in FP32 and rounds its output to BF16; RMSNorm computes in FP32 and rounds
+  once; SwiGLU rounds gate and up, then the product; the residual add rounds the sum;
+  head logits are bf16(acc + bias).
+"""
+
+from __future__ import annotations
+
+import torch
+
+POLICY_SIZE = 1858
+HISTORY_PLANES = 104
+PLANES_PER_HISTORY = 13
+
+
+def _bf16(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.bfloat16).to(torch.float32)
+
+
+def select_and_normalize(planes: torch.Tensor, history_length: int) -> torch.Tensor:
+    """[B,112,8,8] -> [B, sel*64] float32 (dense.py:45-51 history select, :34-42 rule-50/99).
+    Does not modify ``planes``."""
+
+    x = planes.to(torch.float32)
+    hp = history_length * PLANES_PER_HISTORY
+    if hp != HISTORY_PLANES:
+        x = torch.cat((x[:, :hp], x[:, HISTORY_PLANES:]), dim=1)
+    else:
+        x = x.clone()
+    x[:, hp + 5] = x[:, hp + 5] / 99.0
+    return x.flatten(start_dim=1)
+
+
+def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    inv = torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + eps)
+    return x * inv * w
+
+
+def forward(
+    weights: dict[str, torch.Tensor],
+    planes: torch.Tensor,
+    *,
+    depth: int,
+    history_length: int = 8,
+    eps: float = 1e-6,
+    mode: str = "fp32",
+    moe_layers: frozenset[int] = frozenset(),
+    moe_forward=None,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (policy_logits [B,1858], wdl_logits [B,3], moves_left [B]) in float32.
+
+    ``moe_layers`` / ``moe_forward`` let oracle.moe reuse this tower for moe64a2."""
+
+    if mode not in ("fp32", "bf16"):
+        raise ValueError(mode)
+    rnd = _bf16 if mode == "bf16" else (lambda t: t)
+    f = {k: v.to(torch.float32) for k, v in weights.items()}
+    a = rnd(select_and_normalize(planes, history_length))
+    x = rnd(a @ f["input.weight"].T + f["input.bias"])
+    for layer in range(depth):
+        p = f"blocks.{layer}"
+        if layer in moe_layers:
+            assert moe_forward is not None
+            x = moe_forward(x, layer, mode)
+            continue
+        n = rnd(_rmsnorm(x, f[f"{p}.norm.weight"], eps))
+        gu = n @ f[f"{p}.gate_up.weight"].T
+        h = gu.shape[1] // 2
+        g, u = rnd(gu[:, :h]), rnd(gu[:, h:])
+        hidden = rnd(g / (1.0 + torch.exp(-g)) * u)
+        x = rnd(x + rnd(hidden @ f[f"{p}.down.weight"].T))
+    n = rnd(_rmsnorm(x, f["final_norm.weight"], eps))
+    policy = rnd(n @ f["policy.weight"][:POLICY_SIZE].T + f["policy.bias"][:POLICY_SIZE])
+    wdl = rnd(n @ f["wdl.weight"][:3].T + f["wdl.bias"][:3])
+    moves_left = rnd(n @ f["moves_left.weight"][:1].T + f["moves_left.bias"][:1])[:, 0]
+    return policy, wdl, moves_left
+
+
+def wdl_probabilities(wdl_logits: torch.Tensor) -> torch.Tensor:
+    """FP32 softmax of the three logits (kernels/src/inference/runtime.cu:309-328)."""
+
+    return torch.softmax(wdl_logits.to(torch.float32), dim=-1)
