@@ -103,6 +103,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _vp, _vp],
     ),
     "ce4b_model_evaluate": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
+    "ce4b_model_evaluate_async": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "ce4b_model_set_trace": (_i32, [_vp, _vp, _i32]),
+    "ce4b_model_trace_label": (_i32, [_vp, _i32, ctypes.c_char_p, _i32]),
     "ce4b_model_destroy": (None, [_vp]),
     "ce4b_bf16_gemm": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "ce4b_rmsnorm_forward": (_i32, [_vp, _vp, _vp, _i32, _i32, _f32, _vp]),

@@ -1,5 +1,6 @@
 // extern "C" entry points of libce4b200 (declared in include/ce4b200.h). Every entry point
 // converts exceptions to a status code and records the message for ce4b_last_error().
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <string>
@@ -185,6 +186,38 @@ int ce4b_model_evaluate(ce4b_model* model, const ce4b_input_plane* host_planes, 
   });
 }
 
+int ce4b_model_evaluate_async(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
+                              float* host_policy, float* host_wdl, float* host_moves_left,
+                              void* stream) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    model->impl->enqueue_evaluate(host_planes, batch, host_policy, host_wdl, host_moves_left,
+                                  as_stream(stream));
+  });
+}
+
+int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    require(count >= 0 && (count == 0 || events != nullptr), "bad trace event array");
+    model->impl->trace_events.assign(reinterpret_cast<const cudaEvent_t*>(events),
+                                     reinterpret_cast<const cudaEvent_t*>(events) + count);
+  });
+}
+
+int ce4b_model_trace_label(const ce4b_model* model, int index, char* buffer, int buffer_len) {
+  return guarded([&] {
+    require(model != nullptr && model->impl && buffer != nullptr && buffer_len > 0,
+            "null argument");
+    const auto& labels = model->impl->trace_labels;
+    require(index >= 0 && static_cast<size_t>(index) < labels.size(), "trace index out of range");
+    const std::string& l = labels[static_cast<size_t>(index)];
+    const size_t n = std::min(l.size(), static_cast<size_t>(buffer_len - 1));
+    l.copy(buffer, n);
+    buffer[n] = '\0';
+  });
+}
+
 void ce4b_model_destroy(ce4b_model* model) { delete model; }
 
 // ------------------------------------------------------------------ kernel-op API
@@ -197,7 +230,8 @@ int ce4b_bf16_gemm(const void* a_dev, const void* b_dev, void* c_dev, int m, int
     require(c_dev != nullptr, "null output");
     const CUtensorMap ta = make_tmap_bf16(a_dev, m, k, k, 128);
     const CUtensorMap tb = make_tmap_bf16(b_dev, n, k, k, 128);
-    gemm_store_bf16(ta, tb, static_cast<bf16*>(c_dev), n, m, n, k, as_stream(stream));
+    const CUtensorMap tc = make_tmap_bf16(c_dev, m, n, n, 128);
+    gemm_store_bf16(ta, tb, tc, m, n, k, as_stream(stream));
   });
 }
 
@@ -265,15 +299,15 @@ int ce4b_dense_block_forward(const void* x_dev, const void* norm_weight_dev,
     const CUtensorMap t_norm = make_tmap_bf16(normalized, rows, d_model, d_model, 128);
     const CUtensorMap t_gu = make_tmap_bf16(gate_up_weight_dev, 2 * hidden_dim, d_model, d_model,
                                             static_cast<uint32_t>(swiglu_chunk(hidden_dim)));
-    gemm_swiglu(t_norm, t_gu, hidden, rows, hidden_dim, d_model, s);
+    const CUtensorMap t_hidden = make_tmap_bf16(hidden, rows, hidden_dim, hidden_dim, 128);
+    gemm_swiglu(t_norm, t_gu, t_hidden, rows, hidden_dim, d_model, s);
     check_cuda(cudaMemcpyAsync(out_dev, x_dev, static_cast<size_t>(rows) * d_model * 2,
                                cudaMemcpyDeviceToDevice, s),
                "copy residual");
-    const CUtensorMap t_hidden = make_tmap_bf16(hidden, rows, hidden_dim, hidden_dim, 128);
     const CUtensorMap t_down = make_tmap_bf16(down_weight_dev, d_model, hidden_dim, hidden_dim,
                                               static_cast<uint32_t>(resnorm_bn(d_model)));
-    gemm_resnorm(t_hidden, t_down, static_cast<bf16*>(out_dev), nullptr, nullptr, nullptr, rows,
-                 d_model, hidden_dim, eps, s);
+    const CUtensorMap t_out = make_tmap_bf16(out_dev, rows, d_model, d_model, 128);
+    gemm_resnorm(t_hidden, t_down, t_out, t_out, nullptr, nullptr, rows, d_model, hidden_dim, eps, s);
   });
 }
 

@@ -2,12 +2,15 @@
 //
 //   C[M, N] = A[M, K] . B[N, K]^T      A, B: BF16, K-major (row-major with K contiguous)
 //
-// One CTA = 6 warps: warp 0 issues TMA tile loads into an NSTAGE ring of shared-memory
-// stages, warp 1 issues tcgen05.mma (M=128, N=BN, K=16) into a TMEM accumulator
-// (NACC buffers so the epilogue of one tile overlaps the main loop of the next), warps 2-5
-// drain the accumulator with tcgen05.ld (warp w owns TMEM lanes 32*(w%4) .. +31, i.e. one
-// output row per thread) and run the epilogue functor. Tiles are 128 x BN, k-blocks are
-// 64 BF16 (one 128-byte swizzle span). No TMA multicast is used anywhere.
+// One CTA = 2 + 4*G warps: warp 0 issues TMA tile loads into an NSTAGE ring of
+// shared-memory stages, warp 1 issues tcgen05.mma (M=128, N=BN, K=16) into a TMEM
+// accumulator (NACC buffers, so the epilogue of one tile overlaps the main loop of the
+// next), and 4*G epilogue warps drain the accumulator with tcgen05.ld. A warp can only
+// reach the TMEM lane quarter (warp id % 4), so warp w serves rows 32*(w%4) + lane and
+// column group (w-2)/4 of G; each thread owns one output row of its column group.
+// Epilogues stage BF16 results in 128-byte-swizzled shared memory and write them with
+// TMA bulk stores. Tiles are 128 x BN; k-blocks are 64 BF16 (one swizzle span).
+// No TMA multicast is used anywhere.
 #pragma once
 
 #include "ptx.cuh"
@@ -16,11 +19,14 @@ namespace ce4b {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 192;
 constexpr int kMaxClusterN = 8;
+constexpr int kMaxG = 4;
+constexpr uint32_t kEpiBarrierId = 1;  // named barrier of the epilogue warps
+
+__host__ __device__ constexpr int gemm_threads(int g) { return 64 + 128 * g; }
 
 struct TileCoord {
-  int a_row;    // first row of the A box (and of the output rows for dense GEMMs)
+  int a_row;    // first row of the A box
   int b_row;    // first row of the first B box
   int b_row2;   // first row of the second B box (SwiGLU "up" rows), unused otherwise
   int out_row;  // first output row of the tile
@@ -53,7 +59,8 @@ struct DenseSched {
 };
 
 // Grouped (MoE) tile order: the m-tile table is produced on the device by the routing
-// scan; entry i = {expert, first permuted row, valid rows, 0}.
+// scan; entry i = {expert, first permuted row, valid rows, 0}. Expert segments start on
+// 128-row boundaries, so a tile never spans two experts.
 struct GroupedSched {
   const int4* m_tiles;     // [max_m_tiles]
   const int* num_m_tiles;  // device scalar
@@ -77,36 +84,69 @@ struct GroupedSched {
   }
 };
 
-// Shared-memory block handed to epilogues that need cross-CTA exchange.
-struct EpiShared {
-  float recv[kMaxClusterN * kBM];
+// Where one epilogue thread sits in the tile.
+struct EpiThread {
+  int r;           // row within the tile (0..127)
+  int g;           // column group (0..G-1)
+  int tid;         // epilogue thread index (0..128*G-1)
+  uint32_t taddr;  // TMEM address of (row quarter, accumulator buffer column 0)
 };
 
-template <int BN, int NSTAGE, int NACC>
+// Shared resources handed to the epilogue of one tile.
+struct EpiCtx {
+  uint32_t smem;        // shared address of the epilogue region (1024-aligned)
+  uint8_t* smem_ptr;    // generic pointer to the same region
+  uint32_t ring;        // shared address of the stage ring (free after the last MMA of a
+                        // CTA's only tile)
+  uint32_t epi_bar;     // cluster exchange barrier
+  uint32_t x_bar;       // producer prefetch barrier
+  uint32_t tempty_bar;  // accumulator release barrier of this tile
+  int iter;             // tile iteration of this CTA (0, 1, ...)
+  const CUtensorMap* tmO1;
+  const CUtensorMap* tmO2;
+  int* err;
+};
+
+// Every epilogue thread calls this once per tile after its last tcgen05.ld completed.
+__device__ __forceinline__ void release_accumulator(const EpiCtx& ctx) {
+  tc_fence_before();
+  mbar_arrive(ctx.tempty_bar);
+}
+
+template <int G>
+__device__ __forceinline__ void epi_bar_sync() {
+  named_bar_sync(kEpiBarrierId, 128 * G);
+}
+
+template <int BN, int NSTAGE, int NACC, class Epi>
 struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kRingBytes = NSTAGE * kStageBytes;
-  static constexpr int kBarrierBytes = (2 * NSTAGE + 2 * NACC + 2) * 8 + 8;
-  static constexpr int kBytes = 1024 /*alignment slack*/ + kRingBytes + kBarrierBytes + 64 +
-                                static_cast<int>(sizeof(EpiShared));
+  static constexpr int kEpiBytes = (Epi::kSmemBytes + 1023) / 1024 * 1024;
+  static constexpr int kBarrierBytes = (2 * NSTAGE + 2 * NACC + 3) * 8 + 8;
+  static constexpr int kBytes = 1024 /*alignment slack*/ + kRingBytes + kEpiBytes + kBarrierBytes;
   static constexpr uint32_t kTmemCols = (NACC * BN <= 32)    ? 32
                                         : (NACC * BN <= 64)  ? 64
                                         : (NACC * BN <= 128) ? 128
                                         : (NACC * BN <= 256) ? 256
                                                              : 512;
+  static_assert(kBytes <= 232448, "shared memory budget exceeded");
 };
 
 // NBOX = number of TMA boxes that make up the B tile (2 for SwiGLU: gate rows, up rows).
-template <int BN, int NSTAGE, int NACC, int NBOX, bool CLUSTER, class Sched, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int BN, int NSTAGE, int NACC, int NBOX, int G, bool CLUSTER, class Sched, class Epi>
+__global__ void __launch_bounds__(gemm_threads(G), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO1, const __grid_constant__ CUtensorMap tmO2,
                    const Sched sched, const typename Epi::Params ep, const int kblocks, int* err) {
-  using L = GemmSmem<BN, NSTAGE, NACC>;
+  using L = GemmSmem<BN, NSTAGE, NACC, Epi>;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "invalid MMA N");
   static_assert(NACC * BN <= 512, "TMEM overflow");
+  static_assert(G >= 1 && G <= kMaxG, "invalid epilogue width");
   constexpr int kBoxRows = BN / NBOX;
+  constexpr uint32_t kEpiThreads = 128 * G;
 
   extern __shared__ uint8_t smem_raw[];
   uint32_t base = smem_u32(smem_raw);
@@ -114,16 +154,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + pad;
   base += pad;
 
-  const uint32_t bar_base = base + L::kRingBytes;
+  const uint32_t epi_base = base + L::kRingBytes;
+  const uint32_t bar_base = epi_base + L::kEpiBytes;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (NSTAGE + s); };
   auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * NSTAGE + a); };
   auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * NSTAGE + NACC + a); };
   const uint32_t drain_bar = bar_base + 8u * (2 * NSTAGE + 2 * NACC);
   const uint32_t epi_bar = drain_bar + 8u;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kRingBytes + L::kBarrierBytes);
-  EpiShared* epi_smem =
-      reinterpret_cast<EpiShared*>(smem + L::kRingBytes + L::kBarrierBytes + 64);
+  const uint32_t x_bar = drain_bar + 16u;
+  uint32_t* tmem_slot =
+      reinterpret_cast<uint32_t*>(smem + L::kRingBytes + L::kEpiBytes + L::kBarrierBytes - 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -135,16 +176,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 128);
+      mbar_init(tempty_bar(a), kEpiThreads);
     }
     mbar_init(drain_bar, 1);
-    mbar_init(epi_bar, Epi::bar_count(ep));
+    mbar_init(epi_bar, Epi::bar_count(ep, G));
+    mbar_init(x_bar, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
     tmem_relinquish();
   }
+  __syncwarp();
   tc_fence_before();
   if constexpr (CLUSTER) {
     cluster_sync_all();
@@ -162,6 +205,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       uint32_t issued_mask = 0, issued_phase = 0;
+      bool x_issued = false;
       const int ntiles = sched.count();
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         const TileCoord tc = sched.coord(t);
@@ -185,6 +229,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             stage = 0;
             phase ^= 1u;
           }
+          // Epilogue operand (e.g. the residual tile) behind the first k-block; only for
+          // kernels launched with one tile per CTA.
+          if (kb == 0 && !x_issued && Epi::prefetch(ep, tc, &tmO1, epi_base, x_bar)) x_issued = true;
         }
       }
       if (!ok) {
@@ -192,6 +239,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int s = 0; s < NSTAGE; ++s) {
           if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_phase >> s) & 1u);
         }
+        if (x_issued) mbar_wait(x_bar, 0);
       }
     }
     __syncwarp();
@@ -246,27 +294,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else {
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
+    EpiThread et;
+    et.r = quarter * 32 + lane;
+    et.g = (warp - 2) >> 2;
+    et.tid = threadIdx.x - 64;
+    EpiCtx ctx;
+    ctx.smem = epi_base;
+    ctx.smem_ptr = smem + L::kRingBytes;
+    ctx.ring = base;
+    ctx.epi_bar = epi_bar;
+    ctx.x_bar = x_bar;
+    ctx.tmO1 = &tmO1;
+    ctx.tmO2 = &tmO2;
+    ctx.err = err;
     int acc = 0;
     uint32_t acc_phase = 0;
+    int iter = 0;
     const int ntiles = sched.count();
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++iter) {
       const TileCoord tc = sched.coord(t);
       if (!mbar_wait(tfull_bar(acc), acc_phase)) {
         record_error(err, kErrTimeoutEpilogue);
         break;
       }
       tc_fence_after();
-      const uint32_t taddr =
+      et.taddr =
           tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
-      Epi::run(ep, tc, taddr, r, epi_smem, epi_bar, err);
-      tc_fence_before();
-      mbar_arrive(tempty_bar(acc));
+      ctx.iter = iter;
+      ctx.tempty_bar = tempty_bar(acc);
+      Epi::template run<G>(ep, tc, et, ctx);
       if (++acc == NACC) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
+    if (et.tid == 0) bulk_wait_all();  // bulk stores read shared memory until complete
   }
 
   __syncthreads();
@@ -276,184 +338,314 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// ------------------------------------------------------------------ epilogues
+// ------------------------------------------------------------------ epilogue helpers
 
-// Load 16 consecutive FP32 accumulator columns of this thread's row.
-__device__ __forceinline__ void load_acc16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  tmem_ld16(taddr, r);
+// Load 32 consecutive FP32 accumulator columns of this thread's row (one wait).
+__device__ __forceinline__ void load_acc32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
   tmem_ld_wait();
 #pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
-  uint4 lo, hi;
-  lo.x = pack_bf16x2(v[0], v[1]);
-  lo.y = pack_bf16x2(v[2], v[3]);
-  lo.z = pack_bf16x2(v[4], v[5]);
-  lo.w = pack_bf16x2(v[6], v[7]);
-  hi.x = pack_bf16x2(v[8], v[9]);
-  hi.y = pack_bf16x2(v[10], v[11]);
-  hi.z = pack_bf16x2(v[12], v[13]);
-  hi.w = pack_bf16x2(v[14], v[15]);
-  reinterpret_cast<uint4*>(dst)[0] = lo;
-  reinterpret_cast<uint4*>(dst)[1] = hi;
-}
-
-__device__ __forceinline__ void load_bf16x16(const __nv_bfloat16* src, float (&v)[16]) {
-  const uint4 lo = reinterpret_cast<const uint4*>(src)[0];
-  const uint4 hi = reinterpret_cast<const uint4*>(src)[1];
-  const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+// Two 32-column loads behind one wait.
+__device__ __forceinline__ void load_acc32x2(uint32_t ta, uint32_t tb, float (&a)[32], float (&b)[32]) {
+  uint32_t ra[32], rb[32];
+  tmem_ld32(ta, ra);
+  tmem_ld32(tb, rb);
+  tmem_ld_wait();
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float2 f = unpack_bf16x2(w[j]);
-    v[2 * j] = f.x;
-    v[2 * j + 1] = f.y;
+  for (int j = 0; j < 32; ++j) {
+    a[j] = __uint_as_float(ra[j]);
+    b[j] = __uint_as_float(rb[j]);
   }
 }
 
-// SiLU(g) * u with the reference's operation order: g / (1 + exp(-g)) * u.
-__device__ __forceinline__ float swiglu_f32(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+// Round pairs to BF16 (one cvt per pair) and back to FP32.
+__device__ __forceinline__ void round_bf16_inplace(float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float2 f = unpack_bf16x2(pack_bf16x2(v[j], v[j + 1]));
+    v[j] = f.x;
+    v[j + 1] = f.y;
+  }
+}
 
-// Plain BF16 store of C (N columns, row stride ldc). Requires N % 16 == 0.
+template <int N>
+__device__ __forceinline__ void load_bf16(const __nv_bfloat16* src, float* v) {
+  static_assert(N % 8 == 0, "16-byte chunks");
+#pragma unroll
+  for (int c = 0; c < N; c += 8) {
+    const uint4 q = reinterpret_cast<const uint4*>(src)[c / 8];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(w[j]);
+      v[c + 2 * j] = f.x;
+      v[c + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+// Write 32 BF16 values (columns col..col+31 of row r, col % 32 == 0) into a staging
+// tile made of [128 rows][64 cols] boxes with the 128-byte swizzle (the layout a TMA
+// store with SWIZZLE_128B reads).
+__device__ __forceinline__ void stage_bf16x32(uint32_t tile, int r, int col, const float (&v)[32]) {
+  const uint32_t box = tile + static_cast<uint32_t>(col / 64) * (kBM * 128);
+  const int chunk0 = (col % 64) / 8;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint4 o;
+    o.x = pack_bf16x2(v[8 * k + 0], v[8 * k + 1]);
+    o.y = pack_bf16x2(v[8 * k + 2], v[8 * k + 3]);
+    o.z = pack_bf16x2(v[8 * k + 4], v[8 * k + 5]);
+    o.w = pack_bf16x2(v[8 * k + 6], v[8 * k + 7]);
+    st_shared_v4(box + swz128(r, chunk0 + k), o);
+  }
+}
+
+// Read 32 BF16 values back from the same staging layout.
+__device__ __forceinline__ void unstage_bf16x32(uint32_t tile, int r, int col, float (&v)[32]) {
+  const uint32_t box = tile + static_cast<uint32_t>(col / 64) * (kBM * 128);
+  const int chunk0 = (col % 64) / 8;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint4 q = ld_shared_v4(box + swz128(r, chunk0 + k));
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(w[j]);
+      v[8 * k + 2 * j] = f.x;
+      v[8 * k + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+// TMA-store a staged [128 x cols] BF16 tile (cols / 64 boxes) at (x0, y0).
+__device__ __forceinline__ void store_staged(const CUtensorMap* map, uint32_t tile, int cols, int x0,
+                                             int y0) {
+  for (int b = 0; b < cols / 64; ++b) {
+    tma_store_2d(map, tile + static_cast<uint32_t>(b) * (kBM * 128), x0 + 64 * b, y0);
+  }
+  bulk_commit();
+}
+
+// SiLU(g) * u, evaluated as g / (1 + exp(-g)) * u with the special-function unit's exp2
+// and reciprocal (a few FP32 ulp; the result is rounded to BF16, whose ulp is 2^16 times
+// coarser, so the approximation changes the output only in rare rounding ties).
+__device__ __forceinline__ float swiglu_f32(float g, float u) {
+  const float e = ex2_approx(g * -1.4426950408889634f);
+  return g * rcp_approx(1.0f + e) * u;
+}
+
+// ------------------------------------------------------------------ epilogues
+
+// Plain BF16 C tile, staged and TMA-stored through tmO1 (box 64 x 128).
 template <int BN>
 struct EpiStoreBF16 {
+  static_assert(BN % 64 == 0, "64-column boxes");
+  static constexpr int kSmemBytes = kBM * BN * 2;
   struct Params {
-    __nv_bfloat16* c;
-    int ldc;
-    int n;
+    int n;  // logical columns (for the tail of the last tile)
   };
-  __device__ static uint32_t bar_count(const Params&) { return 1; }
-  __device__ static void run(const Params& p, const TileCoord& tc, uint32_t taddr, int r,
-                             EpiShared*, uint32_t, int*) {
-    const bool valid = r < tc.rows;
-    const int row = tc.out_row + r;
-    const int n0 = tc.n_tile * BN;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      if (n0 + c >= p.n) break;  // uniform across the warp
-      float v[16];
-      load_acc16(taddr + c, v);
-      if (valid) store_bf16x16(p.c + static_cast<size_t>(row) * p.ldc + n0 + c, v);
+  __device__ static uint32_t bar_count(const Params&, int) { return 1; }
+  __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
+                                  uint32_t) {
+    return false;
+  }
+  template <int G>
+  __device__ static void run(const Params& p, const TileCoord& tc, const EpiThread& et,
+                             const EpiCtx& ctx) {
+    if (ctx.iter > 0) {
+      if (et.tid == 0) bulk_wait_read_all();
+      epi_bar_sync<G>();
     }
+    const int n0 = tc.n_tile * BN;
+    for (int c = et.g * 32; c < BN; c += G * 32) {
+      float v[32];
+      load_acc32(et.taddr + c, v);
+      stage_bf16x32(ctx.smem, et.r, c, v);
+    }
+    release_accumulator(ctx);
+    fence_proxy_async_smem();
+    epi_bar_sync<G>();
+    if (et.tid == 0) store_staged(ctx.tmO1, ctx.smem, BN, n0, tc.out_row);
+    (void)p;
   }
 };
 
 // SwiGLU epilogue: accumulator columns [0, HC) are gate, [HC, 2*HC) are up for hidden
 // columns n_tile*HC + [0, HC). Gate and up are rounded to BF16 first (the reference
 // materialises the gate_up GEMM output in BF16), the product is rounded once more.
+// The hidden tile is TMA-stored through tmO1 (box 64 x 128 over [M, h]).
 template <int HC>
 struct EpiSwiGLU {
+  static_assert(HC % 64 == 0, "64-column boxes");
+  static constexpr int kSmemBytes = kBM * HC * 2;
   struct Params {
-    __nv_bfloat16* hidden;
-    int ldh;
+    int unused;
   };
-  __device__ static uint32_t bar_count(const Params&) { return 1; }
-  __device__ static void run(const Params& p, const TileCoord& tc, uint32_t taddr, int r,
-                             EpiShared*, uint32_t, int*) {
-    const bool valid = r < tc.rows;
-    __nv_bfloat16* dst =
-        p.hidden + static_cast<size_t>(tc.out_row + r) * p.ldh + tc.n_tile * HC;
-#pragma unroll 1
-    for (int c = 0; c < HC; c += 16) {
-      float g[16], u[16], h[16];
-      load_acc16(taddr + c, g);
-      load_acc16(taddr + HC + c, u);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) h[j] = swiglu_f32(bf16_round(g[j]), bf16_round(u[j]));
-      if (valid) store_bf16x16(dst + c, h);
+  __device__ static uint32_t bar_count(const Params&, int) { return 1; }
+  __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
+                                  uint32_t) {
+    return false;
+  }
+  template <int G>
+  __device__ static void run(const Params&, const TileCoord& tc, const EpiThread& et,
+                             const EpiCtx& ctx) {
+    if (ctx.iter > 0) {
+      if (et.tid == 0) bulk_wait_read_all();  // previous tile's store has read the staging
+      epi_bar_sync<G>();
     }
+    for (int c = et.g * 32; c < HC; c += G * 32) {
+      float g[32], u[32];
+      load_acc32x2(et.taddr + c, et.taddr + HC + c, g, u);
+      round_bf16_inplace(g);
+      round_bf16_inplace(u);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) g[j] = swiglu_f32(g[j], u[j]);
+      stage_bf16x32(ctx.smem, et.r, c, g);
+    }
+    release_accumulator(ctx);
+    fence_proxy_async_smem();
+    epi_bar_sync<G>();
+    if (et.tid == 0) store_staged(ctx.tmO1, ctx.smem, HC, tc.n_tile * HC, tc.out_row);
   }
 };
 
 // Residual / bias epilogue with an optional fused RMSNorm of the updated row.
 //   mode kBias:     x = bf16(acc + bias)                (input embedding, fused bias)
 //   mode kResidual: x = bf16(x + bf16(acc))             (block output + residual)
-// If norm_w is set, the CTAs of one cluster (one per BN-column slice of the row) exchange
-// per-row partial sums of squares through distributed shared memory, and each writes
-// nout = bf16((x * rsqrt(mean(x^2) + eps)) * norm_w) for its slice.
+// tmO1 is the x map (box 64 x 128): the producer prefetches the residual tile through it
+// and the epilogue stores the updated tile through it. If norm_w is set, every
+// (CTA, column group) of a cluster — one CTA per BN-column slice of the row — pushes its
+// per-row partial sum of squares to all CTAs through distributed shared memory; each CTA
+// then writes n = bf16((x * rsqrt(mean(x^2) + eps)) * norm_w) for its slice through tmO2.
+// Partials are summed in a fixed order, so results are deterministic. Launched with
+// exactly one tile per CTA (the stage ring is reused as the n staging buffer).
 template <int BN>
 struct EpiResNorm {
+  static_assert(BN % 64 == 0, "64-column boxes");
   enum Mode : int { kBias = 0, kResidual = 1 };
+  static constexpr int kXBytes = kBM * BN * 2;
+  static constexpr int kRecvFloats = kMaxClusterN * kMaxG * kBM;
+  static constexpr int kSmemBytes = kXBytes + kRecvFloats * 4;
   struct Params {
-    __nv_bfloat16* x;  // [M, d] residual stream (read for kResidual, always written)
     const __nv_bfloat16* bias;
     const __nv_bfloat16* norm_w;  // nullptr: no norm output
-    __nv_bfloat16* nout;
     int d;
     int mode;
     int cluster_n;  // CTAs per row = d / BN
     float eps;
   };
-  __device__ static uint32_t bar_count(const Params& p) {
-    return static_cast<uint32_t>(p.cluster_n * kBM);
+  __device__ static int groups(int G) { return G < BN / 32 ? G : BN / 32; }
+  __device__ static uint32_t bar_count(const Params& p, int G) {
+    return static_cast<uint32_t>(p.cluster_n * groups(G) * kBM);
+  }
+  __device__ static bool prefetch(const Params& p, const TileCoord& tc, const CUtensorMap* tm_x,
+                                  uint32_t dst, uint32_t bar) {
+    if (p.mode != kResidual) return false;
+    mbar_arrive_expect_tx(bar, kXBytes);
+    for (int b = 0; b < BN / 64; ++b) {
+      tma_load_2d(dst + static_cast<uint32_t>(b) * (kBM * 128), tm_x, bar, tc.n_tile * BN + 64 * b,
+                  tc.out_row);
+    }
+    return true;
   }
 
-  __device__ static void run(const Params& p, const TileCoord& tc, uint32_t taddr, int r,
-                             EpiShared* sh, uint32_t epi_bar, int* err) {
-    const bool valid = r < tc.rows;
-    const int row = tc.out_row + r;
+  template <int G>
+  __device__ static void run(const Params& p, const TileCoord& tc, const EpiThread& et,
+                             const EpiCtx& ctx) {
+    constexpr int kPer = BN / 32;  // 32-column chunks in this slice
+    constexpr int kGroups = G < kPer ? G : kPer;
+    constexpr int kChunks = kPer / kGroups;  // chunks per column group
+    static_assert(kPer % kGroups == 0, "chunks must split evenly");
+    const bool active = et.g < kGroups;
     const int n0 = tc.n_tile * BN;
-    __nv_bfloat16* xrow = p.x + static_cast<size_t>(row) * p.d + n0;
+    const uint32_t xs = ctx.smem;  // x tile (prefetched residual, then updated x)
+    float* recv = reinterpret_cast<float*>(ctx.smem_ptr + kXBytes);
+    bool ok = true;
+    if (p.mode == kResidual && !mbar_wait(ctx.x_bar, 0)) {
+      record_error(ctx.err, kErrTimeoutEpilogue);
+      ok = false;
+    }
     float ss = 0.0f;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      float v[16];
-      load_acc16(taddr + c, v);
-      if (p.mode == kBias) {
-        float b[16];
-        load_bf16x16(p.bias + n0 + c, b);
+    if (active) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = bf16_round(v[j] + b[j]);
-      } else {
-        float xo[16];
-        if (valid) {
-          load_bf16x16(xrow + c, xo);
+      for (int i = 0; i < kChunks; ++i) {
+        const int c = (et.g * kChunks + i) * 32;
+        float v[32];
+        load_acc32(et.taddr + c, v);
+        if (p.mode == kBias) {
+          float b[32];
+          load_bf16<32>(p.bias + n0 + c, b);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
+          round_bf16_inplace(v);
         } else {
+          float xo[32];
+          unstage_bf16x32(xs, et.r, c, xo);
+          round_bf16_inplace(v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) xo[j] = 0.0f;
+          for (int j = 0; j < 32; ++j) v[j] = xo[j] + v[j];
+          round_bf16_inplace(v);
         }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = bf16_round(xo[j] + bf16_round(v[j]));
+        for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+        stage_bf16x32(xs, et.r, c, v);
       }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) ss = fmaf(v[j], v[j], ss);
-      if (valid) store_bf16x16(xrow + c, v);
     }
-    if (p.norm_w == nullptr) return;
+    release_accumulator(ctx);
+    fence_proxy_async_smem();
+    epi_bar_sync<G>();
+    if (et.tid == 0) store_staged(ctx.tmO1, xs, BN, n0, tc.out_row);
+    if (p.norm_w == nullptr || !ok) return;
 
-    // Push this slice's partial sum to every CTA of the cluster, then collect.
-    const uint32_t rank = static_cast<uint32_t>(tc.n_tile);
-    const uint32_t slot = smem_u32(&sh->recv[rank * kBM + r]);
-    for (int k = 0; k < p.cluster_n; ++k) st_cluster_f32(mapa_shared(slot, k), ss);
-    for (int k = 0; k < p.cluster_n; ++k) mbar_arrive_remote(mapa_shared(epi_bar, k));
-    if (!mbar_wait_cluster(epi_bar, 0)) {
-      record_error(err, kErrTimeoutCluster);
+    // Push this (slice, group) partial to every CTA of the cluster, then collect.
+    if (active) {
+      const uint32_t rank = static_cast<uint32_t>(tc.n_tile);
+      const uint32_t slot = smem_u32(&recv[(rank * kGroups + et.g) * kBM + et.r]);
+      for (int k = 0; k < p.cluster_n; ++k) st_cluster_f32(mapa_shared(slot, k), ss);
+      for (int k = 0; k < p.cluster_n; ++k) mbar_arrive_remote(mapa_shared(ctx.epi_bar, k));
+    }
+    if (!mbar_wait_cluster(ctx.epi_bar, 0)) {
+      record_error(ctx.err, kErrTimeoutCluster);
       return;
     }
-    float total = 0.0f;
-    for (int k = 0; k < p.cluster_n; ++k) total += sh->recv[k * kBM + r];
-    const float inv = 1.0f / sqrtf(total / static_cast<float>(p.d) + p.eps);
-    if (!valid) return;
-    __nv_bfloat16* nrow = p.nout + static_cast<size_t>(row) * p.d + n0;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      float v[16], w[16];
-      load_bf16x16(xrow + c, v);
-      load_bf16x16(p.norm_w + n0 + c, w);
+    if (active) {
+      float total = 0.0f;
+      const int parts = p.cluster_n * kGroups;
+      for (int k = 0; k < parts; ++k) total += recv[k * kBM + et.r];
+      const float inv = 1.0f / sqrtf(total / static_cast<float>(p.d) + p.eps);
+      // The stage ring is idle after this CTA's only tile: stage n there.
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = (v[j] * inv) * w[j];
-      store_bf16x16(nrow + c, v);
+      for (int i = 0; i < kChunks; ++i) {
+        const int c = (et.g * kChunks + i) * 32;
+        float v[32], w[32];
+        unstage_bf16x32(xs, et.r, c, v);
+        load_bf16<32>(p.norm_w + n0 + c, w);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = (v[j] * inv) * w[j];
+        stage_bf16x32(ctx.ring, et.r, c, v);
+      }
     }
+    fence_proxy_async_smem();
+    epi_bar_sync<G>();
+    if (et.tid == 0) store_staged(ctx.tmO2, ctx.ring, BN, n0, tc.out_row);
   }
 };
 
 // Heads epilogue over the concatenated head matrix [policy (Ps) | wdl (32) | moves-left (32)]:
 // logits = bf16(acc + bias) (TE Linear fuses the bias before rounding); the policy block
 // is written as FP32 for columns < policy_size, WDL as logits or as an FP32 softmax of
-// the three rounded logits, moves-left as FP32.
+// the three rounded logits, moves-left as FP32. Each warp transposes its 32 x 32 block
+// through shared memory so that every store instruction writes 32 consecutive floats of
+// one row (the 7432-byte policy row stride rules out TMA stores).
 struct EpiHeads {
+  static constexpr int BN = 256;
+  static constexpr int kPitch = 33;  // floats per transposed row (bank-conflict free)
+  static constexpr int kSmemBytes = 16 * 32 * kPitch * 4;
   struct Params {
     const __nv_bfloat16* bias;  // [n_total]
     float* policy;              // [M, policy_size]
@@ -464,52 +656,61 @@ struct EpiHeads {
     int n_total;                // policy_storage + 64
     int wdl_probs;
   };
-  __device__ static uint32_t bar_count(const Params&) { return 1; }
-  static constexpr int BN = 256;
-  __device__ static void run(const Params& p, const TileCoord& tc, uint32_t taddr, int r,
-                             EpiShared*, uint32_t, int*) {
-    const bool valid = r < tc.rows;
-    const int row = tc.out_row + r;
+  __device__ static uint32_t bar_count(const Params&, int) { return 1; }
+  __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
+                                  uint32_t) {
+    return false;
+  }
+  template <int G>
+  __device__ static void run(const Params& p, const TileCoord& tc, const EpiThread& et,
+                             const EpiCtx& ctx) {
+    static_assert(G <= 4, "transpose buffers for 16 warps");
+    const int lane = et.r & 31;
+    const int row0 = tc.out_row + (et.r & ~31);  // first row of this warp's 32 rows
+    float* tbuf = reinterpret_cast<float*>(ctx.smem_ptr) + (et.tid >> 5) * 32 * kPitch;
     const int n0 = tc.n_tile * BN;
-    float* prow = p.policy + static_cast<size_t>(row) * p.policy_size;
-    float wdl[3] = {0.f, 0.f, 0.f};
-    bool has_wdl = false;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      if (n0 + c >= p.n_total) break;
-      float v[16];
-      load_acc16(taddr + c, v);
-      if (!valid) continue;
+    for (int c = et.g * 32; c < BN; c += G * 32) {
+      const int c0 = n0 + c;
+      if (c0 >= p.n_total) break;  // uniform across the warp
+      float v[32], b[32];
+      load_acc32(et.taddr + c, v);
+      load_bf16<32>(p.bias + c0, b);  // bias is padded to a multiple of 32 columns
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int col = n0 + c + j;
-        if (col >= p.n_total) break;
-        const float logit = bf16_round(v[j] + __bfloat162float(p.bias[col]));
-        if (col < p.policy_size) {
-          prow[col] = logit;
-        } else if (col >= p.policy_storage && col < p.policy_storage + 3) {
-          wdl[col - p.policy_storage] = logit;
-          has_wdl = true;
-        } else if (col == p.policy_storage + 32) {
-          p.moves_left[row] = logit;
+      for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
+      round_bf16_inplace(v);
+      const int row = tc.out_row + et.r;
+      const bool valid = et.r < tc.rows;
+      if (c0 < p.policy_size) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tbuf[lane * kPitch + j] = v[j];
+        __syncwarp();
+        const bool col_ok = c0 + lane < p.policy_size;
+        for (int rr = 0; rr < 32; ++rr) {
+          if (col_ok && (et.r & ~31) + rr < tc.rows) {
+            p.policy[static_cast<size_t>(row0 + rr) * p.policy_size + c0 + lane] =
+                tbuf[rr * kPitch + lane];
+          }
         }
+        __syncwarp();
+      } else if (c0 == p.policy_storage && valid) {
+        float* w = p.wdl + static_cast<size_t>(row) * 3;
+        if (p.wdl_probs) {
+          const float mx = fmaxf(fmaxf(v[0], v[1]), v[2]);
+          const float e0 = expf(v[0] - mx), e1 = expf(v[1] - mx), e2 = expf(v[2] - mx);
+          const float total = e0 + e1 + e2;
+          w[0] = e0 / total;
+          w[1] = e1 / total;
+          w[2] = e2 / total;
+        } else {
+          w[0] = v[0];
+          w[1] = v[1];
+          w[2] = v[2];
+        }
+      } else if (c0 == p.policy_storage + 32 && valid) {
+        p.moves_left[row] = v[0];
       }
     }
-    if (valid && has_wdl) {
-      float* w = p.wdl + static_cast<size_t>(row) * 3;
-      if (p.wdl_probs) {
-        const float mx = fmaxf(fmaxf(wdl[0], wdl[1]), wdl[2]);
-        const float e0 = expf(wdl[0] - mx), e1 = expf(wdl[1] - mx), e2 = expf(wdl[2] - mx);
-        const float total = e0 + e1 + e2;
-        w[0] = e0 / total;
-        w[1] = e1 / total;
-        w[2] = e2 / total;
-      } else {
-        w[0] = wdl[0];
-        w[1] = wdl[1];
-        w[2] = wdl[2];
-      }
-    }
+    release_accumulator(ctx);
   }
 };
 

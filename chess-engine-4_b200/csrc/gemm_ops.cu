@@ -49,10 +49,11 @@ void ensure_smem(K kernel, int bytes) {
 }
 
 template <class K, class... Args>
-void launch(K kernel, dim3 grid, int smem, int cluster_x, cudaStream_t s, Args... args) {
+void launch(K kernel, dim3 grid, int threads, int smem, int cluster_x, cudaStream_t s,
+            Args... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -68,6 +69,15 @@ void launch(K kernel, dim3 grid, int smem, int cluster_x, cudaStream_t s, Args..
 }
 
 int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// Epilogue column groups per TMEM lane quarter (4 * kG epilogue warps per CTA).
+constexpr int kG = 4;
+
+// Placeholder for unused tensor-map arguments.
+const CUtensorMap& null_map() {
+  static const CUtensorMap m{};
+  return m;
+}
 
 }  // namespace
 
@@ -91,24 +101,25 @@ CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64
 }
 
 // ------------------------------------------------------------------ plain store
-void gemm_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, bf16* c, int ldc, int m, int n,
-                     int k, cudaStream_t s) {
+void gemm_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC, int m,
+                     int n, int k, cudaStream_t s) {
   constexpr int BN = 128, NS = 6, NA = 2;
   using Epi = EpiStoreBF16<BN>;
-  auto kernel = gemm_tc_kernel<BN, NS, NA, 1, false, DenseSched, Epi>;
-  constexpr int smem = GemmSmem<BN, NS, NA>::kBytes;
+  auto kernel = gemm_tc_kernel<BN, NS, NA, 1, kG, false, DenseSched, Epi>;
+  constexpr int smem = GemmSmem<BN, NS, NA, Epi>::kBytes;
   ensure_smem(kernel, smem);
   DenseSched sched{m, ceil_div(n, BN), ceil_div(m, kBM) * ceil_div(n, BN), BN, 0};
-  typename Epi::Params ep{c, ldc, n};
+  typename Epi::Params ep{n};
   const int grid = std::min(sched.num_tiles, sm_count());
-  launch(kernel, dim3(grid), smem, 0, s, tA, tB, sched, ep, ceil_div(k, kBK), device_error_word());
+  launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tC, null_map(), sched, ep,
+         ceil_div(k, kBK), device_error_word());
 }
 
 // ------------------------------------------------------------------ SwiGLU
 int swiglu_chunk(int hidden) { return hidden % 128 == 0 ? 128 : 64; }
 
-void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, bf16* hidden, int m, int hidden_dim,
-                 int k, cudaStream_t s) {
+void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH, int m,
+                 int hidden_dim, int k, cudaStream_t s) {
   const int hc = swiglu_chunk(hidden_dim);
   require(hidden_dim % hc == 0, "SwiGLU hidden dim must be a multiple of 64");
   DenseSched sched{m, hidden_dim / hc, ceil_div(m, kBM) * (hidden_dim / hc), hc, hidden_dim};
@@ -116,19 +127,21 @@ void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, bf16* hidden, int
   if (hc == 128) {
     constexpr int BN = 256, NS = 4, NA = 2;
     using Epi = EpiSwiGLU<128>;
-    auto kernel = gemm_tc_kernel<BN, NS, NA, 2, false, DenseSched, Epi>;
-    constexpr int smem = GemmSmem<BN, NS, NA>::kBytes;
+    auto kernel = gemm_tc_kernel<BN, NS, NA, 2, kG, false, DenseSched, Epi>;
+    constexpr int smem = GemmSmem<BN, NS, NA, Epi>::kBytes;
     ensure_smem(kernel, smem);
-    typename Epi::Params ep{hidden, hidden_dim};
-    launch(kernel, dim3(grid), smem, 0, s, tA, tB, sched, ep, ceil_div(k, kBK), device_error_word());
+    typename Epi::Params ep{0};
+    launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tH, null_map(), sched, ep,
+           ceil_div(k, kBK), device_error_word());
   } else {
     constexpr int BN = 128, NS = 6, NA = 2;
     using Epi = EpiSwiGLU<64>;
-    auto kernel = gemm_tc_kernel<BN, NS, NA, 2, false, DenseSched, Epi>;
-    constexpr int smem = GemmSmem<BN, NS, NA>::kBytes;
+    auto kernel = gemm_tc_kernel<BN, NS, NA, 2, kG, false, DenseSched, Epi>;
+    constexpr int smem = GemmSmem<BN, NS, NA, Epi>::kBytes;
     ensure_smem(kernel, smem);
-    typename Epi::Params ep{hidden, hidden_dim};
-    launch(kernel, dim3(grid), smem, 0, s, tA, tB, sched, ep, ceil_div(k, kBK), device_error_word());
+    typename Epi::Params ep{0};
+    launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tH, null_map(), sched, ep,
+           ceil_div(k, kBK), device_error_word());
   }
 }
 
@@ -142,28 +155,28 @@ int resnorm_bn(int d) {
 }
 
 template <int BN, int NS>
-static void gemm_resnorm_bn(const CUtensorMap& tA, const CUtensorMap& tB, bf16* x,
-                            const bf16* bias, const bf16* norm_w, bf16* nout, int m, int d, int k,
-                            float eps, cudaStream_t s) {
+static void gemm_resnorm_bn(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
+                            const CUtensorMap& tN, const bf16* bias, const bf16* norm_w, int m,
+                            int d, int k, float eps, cudaStream_t s) {
   using Epi = EpiResNorm<BN>;
-  auto kernel = gemm_tc_kernel<BN, NS, 1, 1, true, DenseSched, Epi>;
-  constexpr int smem = GemmSmem<BN, NS, 1>::kBytes;
+  auto kernel = gemm_tc_kernel<BN, NS, 1, 1, kG, true, DenseSched, Epi>;
+  constexpr int smem = GemmSmem<BN, NS, 1, Epi>::kBytes;
   ensure_smem(kernel, smem);
   const int cn = d / BN;
   DenseSched sched{m, cn, ceil_div(m, kBM) * cn, BN, 0};
-  typename Epi::Params ep{x,   bias, norm_w, nout, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
-                          cn, eps};
+  typename Epi::Params ep{bias, norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual, cn, eps};
   // One tile per CTA: the cluster's CTAs cover one 128-row block across the full width.
-  launch(kernel, dim3(sched.num_tiles), smem, cn, s, tA, tB, sched, ep, ceil_div(k, kBK),
-         device_error_word());
+  launch(kernel, dim3(sched.num_tiles), gemm_threads(kG), smem, cn, s, tA, tB, tX, tN, sched, ep,
+         ceil_div(k, kBK), device_error_word());
 }
 
-void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, bf16* x, const bf16* bias,
-                  const bf16* norm_w, bf16* nout, int m, int d, int k, float eps, cudaStream_t s) {
+void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
+                  const CUtensorMap& tN, const bf16* bias, const bf16* norm_w, int m, int d, int k,
+                  float eps, cudaStream_t s) {
   switch (resnorm_bn(d)) {
-    case 64: gemm_resnorm_bn<64, 8>(tA, tB, x, bias, norm_w, nout, m, d, k, eps, s); break;
-    case 128: gemm_resnorm_bn<128, 6>(tA, tB, x, bias, norm_w, nout, m, d, k, eps, s); break;
-    default: gemm_resnorm_bn<256, 4>(tA, tB, x, bias, norm_w, nout, m, d, k, eps, s); break;
+    case 64: gemm_resnorm_bn<64, 7>(tA, tB, tX, tN, bias, norm_w, m, d, k, eps, s); break;
+    case 128: gemm_resnorm_bn<128, 5>(tA, tB, tX, tN, bias, norm_w, m, d, k, eps, s); break;
+    default: gemm_resnorm_bn<256, 3>(tA, tB, tX, tN, bias, norm_w, m, d, k, eps, s); break;
   }
 }
 
@@ -171,17 +184,18 @@ void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, bf16* x, const b
 void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, float* policy,
                 float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,
                 int wdl_probs, cudaStream_t s) {
-  constexpr int BN = 256, NS = 4, NA = 2;
+  constexpr int BN = 256, NS = 3, NA = 2;
   using Epi = EpiHeads;
-  auto kernel = gemm_tc_kernel<BN, NS, NA, 1, false, DenseSched, Epi>;
-  constexpr int smem = GemmSmem<BN, NS, NA>::kBytes;
+  auto kernel = gemm_tc_kernel<BN, NS, NA, 1, kG, false, DenseSched, Epi>;
+  constexpr int smem = GemmSmem<BN, NS, NA, Epi>::kBytes;
   ensure_smem(kernel, smem);
   const int n_total = policy_storage + 64;
   DenseSched sched{m, ceil_div(n_total, BN), ceil_div(m, kBM) * ceil_div(n_total, BN), BN, 0};
   typename Epi::Params ep{bias, policy, wdl, moves_left, policy_size, policy_storage, n_total,
                           wdl_probs};
   const int grid = std::min(sched.num_tiles, sm_count());
-  launch(kernel, dim3(grid), smem, 0, s, tA, tB, sched, ep, ceil_div(d, kBK), device_error_word());
+  launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, null_map(), null_map(), sched,
+         ep, ceil_div(d, kBK), device_error_word());
 }
 
 }  // namespace ce4b

@@ -51,17 +51,22 @@ CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64
                            uint32_t box_rows);
 
 // ---------------------------------------------------------------- GEMM launchers
-// C[M,N] = A[M,K] . B[N,K]^T, BF16 out (row stride ldc), N % 16 == 0.
-void gemm_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB128, bf16* c, int ldc, int m,
+// Every map is a BF16 map from make_tmap_bf16 (box 64 columns x box_rows rows); output
+// maps (tC, tH, tX, tN) use 128-row boxes and the exact row count of the output.
+// C[M,N] = A[M,K] . B[N,K]^T, BF16 out, N % 16 == 0 (B box 128 rows).
+void gemm_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC, int m,
                      int n, int k, cudaStream_t s);
 // hidden[M,h] = SwiGLU over W_gu [2h, K] (gate rows first); tB box rows must equal hc.
 int swiglu_chunk(int hidden);  // 128 if hidden % 128 == 0, else 64
-void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, bf16* hidden, int m, int hidden_dim,
-                 int k, cudaStream_t s);
+void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH, int m,
+                 int hidden_dim, int k, cudaStream_t s);
 // Residual/bias epilogue with optional fused RMSNorm; tB box rows must equal resnorm_bn(d).
+// tX is the residual stream x [M, d] (read for the residual mode, written), tN the
+// normalised output [M, d] (used when norm_w is set).
 int resnorm_bn(int d);
-void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, bf16* x, const bf16* bias,
-                  const bf16* norm_w, bf16* nout, int m, int d, int k, float eps, cudaStream_t s);
+void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
+                  const CUtensorMap& tN, const bf16* bias, const bf16* norm_w, int m, int d, int k,
+                  float eps, cudaStream_t s);
 // Heads over the concatenated [policy | wdl | moves-left] matrix; tB box rows 256.
 void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, float* policy,
                 float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,

@@ -187,6 +187,7 @@ void Model::finalize() {
   bf16* ws_hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);
   tm_a_in = make_tmap_bf16(ws_a_in, rows_cap, in_dim, in_dim, 128);
   tm_n = make_tmap_bf16(ws_n, rows_cap, d, d, 128);
+  tm_x = make_tmap_bf16(workspace + ws_off.x, rows_cap, d, d, 128);
   tm_hidden = make_tmap_bf16(ws_hidden, rows_cap, dense_hidden, dense_hidden, 128);
   const uint32_t bn = static_cast<uint32_t>(resnorm_bn(d));
   tm_w_in = make_tmap_bf16(w("input.weight"), d, in_dim, in_dim, bn);
@@ -222,26 +223,37 @@ void Model::forward(int layout, void* input, const void* scalars, int batch, flo
   const int d = cfg.d_model;
   const float eps = cfg.rms_norm_eps;
   bf16* a_in = reinterpret_cast<bf16*>(workspace + ws_off.a_in);
-  bf16* x = reinterpret_cast<bf16*>(workspace + ws_off.x);
-  bf16* n = reinterpret_cast<bf16*>(workspace + ws_off.n);
-  bf16* hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);
   const int write_back = normalize_in_place && cfg.history_length == 8;
 
+  trace_next = 0;
+  trace_labels.clear();
   expand_input(layout, input, scalars, batch, cfg.history_length, a_in, write_back, s);
+  trace("expand_planes", s);
   const bf16* first_norm = cfg.depth > 0 ? layers[0].norm : w("final_norm.weight");
-  gemm_resnorm(tm_a_in, tm_w_in, x, w("input.bias"), first_norm, n, batch, d, in_dim, eps, s);
+  gemm_resnorm(tm_a_in, tm_w_in, tm_x, tm_n, w("input.bias"), first_norm, batch, d, in_dim, eps, s);
+  trace("input_gemm_bias_rmsnorm", s);
   for (int l = 0; l < cfg.depth; ++l) {
     const Layer& L = layers[l];
     const bf16* next_norm = l + 1 < cfg.depth ? layers[l + 1].norm : w("final_norm.weight");
-    gemm_swiglu(tm_n, L.tm_gate_up, hidden, batch, dense_hidden, d, s);
-    gemm_resnorm(tm_hidden, L.tm_down, x, nullptr, next_norm, n, batch, d, dense_hidden, eps, s);
+    gemm_swiglu(tm_n, L.tm_gate_up, tm_hidden, batch, dense_hidden, d, s);
+    trace("gate_up_swiglu", s);
+    gemm_resnorm(tm_hidden, L.tm_down, tm_x, tm_n, nullptr, next_norm, batch, d, dense_hidden, eps,
+                 s);
+    trace("down_residual_rmsnorm", s);
   }
   gemm_heads(tm_n, tm_heads, w("policy.bias"), policy, wdl, moves_left, batch, d, policy_size,
              policy_storage, wdl_probs, s);
+  trace("heads", s);
 }
 
-void Model::evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
-                     float* host_wdl, float* host_moves_left) {
+void Model::trace(const char* label, cudaStream_t s) {
+  if (trace_next >= trace_events.size()) return;
+  check_cuda(cudaEventRecord(trace_events[trace_next++], s), "record trace event");
+  trace_labels.emplace_back(label);
+}
+
+void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
+                             float* host_wdl, float* host_moves_left, cudaStream_t s) {
   if (!finalized) fail(CE4B_ERR_NOT_READY, "model is not finalized");
   require(batch >= 1 && batch <= max_batch, "batch size exceeds model capacity");
   require(host_planes && host_policy && host_wdl && host_moves_left, "null host buffer");
@@ -250,43 +262,57 @@ void Model::evaluate(const ce4b_input_plane* host_planes, int batch, float* host
   float* pol = reinterpret_cast<float*>(workspace + ws_off.policy);
   float* wdl = reinterpret_cast<float*>(workspace + ws_off.wdl);
   float* ml = reinterpret_cast<float*>(workspace + ws_off.moves_left);
-  check_cuda(cudaMemcpyAsync(planes, host_planes,
-                             static_cast<size_t>(batch) * kInputPlanes * sizeof(ce4b_input_plane),
-                             cudaMemcpyHostToDevice, stream),
-             "copy input planes");
-  auto it = graphs.find(batch);
+  const int key = batch * 2 + 1;
+  auto it = graphs.find(key);
   if (it == graphs.end()) {
-    // First use of this batch size: warm up (kernel attributes, descriptors) outside the
-    // capture, then capture the forward into a graph.
-    forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
-    check_cuda(cudaStreamSynchronize(stream), "warm-up forward");
-    check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    // First use of this batch size: run once outside a capture (kernel attributes), then
+    // capture the forward into a graph on the internal stream. Blocks.
+    const std::vector<cudaEvent_t> saved = std::move(trace_events);
+    trace_events.clear();
     try {
       forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
+      check_cuda(cudaStreamSynchronize(stream), "warm-up forward");
+      check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+      try {
+        forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
+      } catch (...) {
+        cudaGraph_t g = nullptr;
+        cudaStreamEndCapture(stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      cudaGraph_t graph = nullptr;
+      check_cuda(cudaStreamEndCapture(stream, &graph), "end capture");
+      cudaGraphExec_t exec = nullptr;
+      const cudaError_t st = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      check_cuda(st, "instantiate graph");
+      it = graphs.emplace(key, exec).first;
     } catch (...) {
-      cudaGraph_t g = nullptr;
-      cudaStreamEndCapture(stream, &g);
-      if (g) cudaGraphDestroy(g);
+      trace_events = saved;
       throw;
     }
-    cudaGraph_t graph = nullptr;
-    check_cuda(cudaStreamEndCapture(stream, &graph), "end capture");
-    cudaGraphExec_t exec = nullptr;
-    const cudaError_t st = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    check_cuda(st, "instantiate graph");
-    it = graphs.emplace(batch, exec).first;
+    trace_events = saved;
   }
-  check_cuda(cudaGraphLaunch(it->second, stream), "launch graph");
+  check_cuda(cudaMemcpyAsync(planes, host_planes,
+                             static_cast<size_t>(batch) * kInputPlanes * sizeof(ce4b_input_plane),
+                             cudaMemcpyHostToDevice, s),
+             "copy input planes");
+  check_cuda(cudaGraphLaunch(it->second, s), "launch graph");
   check_cuda(cudaMemcpyAsync(host_policy, pol, static_cast<size_t>(batch) * policy_size * 4,
-                             cudaMemcpyDeviceToHost, stream),
+                             cudaMemcpyDeviceToHost, s),
              "copy policy");
   check_cuda(cudaMemcpyAsync(host_wdl, wdl, static_cast<size_t>(batch) * 3 * 4,
-                             cudaMemcpyDeviceToHost, stream),
+                             cudaMemcpyDeviceToHost, s),
              "copy wdl");
   check_cuda(cudaMemcpyAsync(host_moves_left, ml, static_cast<size_t>(batch) * 4,
-                             cudaMemcpyDeviceToHost, stream),
+                             cudaMemcpyDeviceToHost, s),
              "copy moves left");
+}
+
+void Model::evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
+                     float* host_wdl, float* host_moves_left) {
+  enqueue_evaluate(host_planes, batch, host_policy, host_wdl, host_moves_left, stream);
   check_cuda(cudaStreamSynchronize(stream), "synchronize evaluation");
 }
 

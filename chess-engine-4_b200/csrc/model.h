@@ -46,11 +46,15 @@ struct Model {
   size_t workspace_bytes = 0;
   WorkspaceOffsets ws_off;
 
-  CUtensorMap tm_a_in{}, tm_n{}, tm_hidden{}, tm_w_in{}, tm_heads{};
+  CUtensorMap tm_a_in{}, tm_x{}, tm_n{}, tm_hidden{}, tm_w_in{}, tm_heads{};
   std::vector<Layer> layers;
   bool finalized = false;
   cudaStream_t stream = nullptr;
-  std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, cudaGraphExec_t> graphs;  // key: batch * 2 + wdl_probs
+  // Optional per-kernel trace: an event is recorded after each kernel of forward().
+  std::vector<cudaEvent_t> trace_events;
+  std::vector<std::string> trace_labels;
+  size_t trace_next = 0;
 
   Model() = default;
   Model(const Model&) = delete;
@@ -67,6 +71,9 @@ struct Model {
                int32_t* tokens_per_expert, cudaStream_t s);
   void evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
                 float* host_wdl, float* host_moves_left);
+  void enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
+                        float* host_wdl, float* host_moves_left, cudaStream_t s);
+  void trace(const char* label, cudaStream_t s);
 
  private:
   void add_slot(const std::string& name, std::vector<int64_t> shape, int dtype, size_t& cursor,

@@ -143,6 +143,20 @@ int ce4b_model_forward(ce4b_model* model, int input_layout, void* input_dev,
 int ce4b_model_evaluate(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
                         float* host_policy, float* host_wdl, float* host_moves_left);
 
+/* Asynchronous form of ce4b_model_evaluate on `stream`: enqueues the H2D copy, the
+ * graph and the D2H copies and returns. Host buffers must stay valid (and should be
+ * pinned) until the stream reaches that point. The first call for a batch size builds
+ * its graph and blocks. */
+int ce4b_model_evaluate_async(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
+                              float* host_policy, float* host_wdl, float* host_moves_left,
+                              void* stream);
+
+/* Per-kernel tracing of ce4b_model_forward: when `count` > 0, forward records
+ * events[i] (cudaEvent_t) on its stream after its i-th kernel; count 0 disables.
+ * ce4b_model_trace_label names kernel i of the last traced forward. */
+int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count);
+int ce4b_model_trace_label(const ce4b_model* model, int index, char* buffer, int buffer_len);
+
 void ce4b_model_destroy(ce4b_model* model);
 
 /* ------------------------------------------------------------------ kernel-op API
