@@ -116,6 +116,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, _i32, _vp],
     ),
+    "ce4b_dense_block_forward_static": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, _i32, _vp],
+    ),
 }
 
 _LIB: ctypes.CDLL | None = None

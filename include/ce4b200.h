@@ -195,6 +195,21 @@ int ce4b_dense_block_forward(const void* x_dev, const void* norm_weight_dev,
                              void* out_dev, void* workspace_dev, int rows, int d_model,
                              int hidden_dim, float eps, int precision, void* stream);
 
+/* ce4b_dense_block_forward for callers that cannot allocate device memory (an engine
+ * thread whose process freezes its allocator after start-up, a plugin that is handed only
+ * its input and output buffers, code under a no-allocation budget). Same arguments and
+ * result, without the workspace: the scratch lives in a fixed 8 MiB __device__ array of
+ * the library (held on every GPU that loads it), so rows * (d_model + hidden_dim) * 2
+ * bytes, each part rounded up to 128 rows and 256 bytes, must fit in 8 MiB; larger calls
+ * fail with CE4B_ERR_INVALID_ARGUMENT. The first call on a device looks up the array's
+ * device address and should come before any stream capture. All calls on a device share
+ * the array: calls whose GPU work overlaps race and must be serialised by the caller.
+ * Allocates nothing. This entry point has no counterpart in the reference. */
+int ce4b_dense_block_forward_static(const void* x_dev, const void* norm_weight_dev,
+                                    const void* gate_up_weight_dev, const void* down_weight_dev,
+                                    void* out_dev, int rows, int d_model, int hidden_dim,
+                                    float eps, int precision, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
