@@ -116,6 +116,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, _i32, _vp],
     ),
+    "ce4b_moe_route": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp]),
+    "ce4b_moe_workspace_size": (_i64, [_i32, _i32, _i32]),
+    "ce4b_moe_forward": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp],
+    ),
     "ce4b_dense_block_forward_static": (
         _i32,
         [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, _i32, _vp],

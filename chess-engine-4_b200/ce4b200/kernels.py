@@ -169,3 +169,84 @@ def dense_block_forward(
             )
         )
     return out
+
+
+EXPERT_COUNT = 64
+MOE_ROW_ALIGNMENT = 128
+
+
+def moe_forward(
+    x: torch.Tensor,
+    gate_up_weight: torch.Tensor,
+    down_weight: torch.Tensor,
+    route_probs: torch.Tensor,
+    expert_offsets: torch.Tensor,
+) -> torch.Tensor:
+    """Expert SwiGLU MLP over rows sorted and padded by expert.
+
+    Mirrors ``moe_forward`` (src/chess_engine_4/kernels/moe.py:24-46): rows
+    ``expert_offsets[e]:expert_offsets[e+1]`` of ``x`` go through expert ``e`` and are
+    scaled by ``route_probs``. Segments must start on multiples of 128 rows (the reference's
+    static dispatch pads to 128, src/chess_engine_4/model/moe.py:239-251); rows past
+    ``expert_offsets[64]`` are left unwritten.
+    """
+
+    _check_bf16_matrix("x", x)
+    rows, d_model = x.shape
+    if gate_up_weight.ndim != 3 or gate_up_weight.shape[0] != EXPERT_COUNT:
+        raise ValueError("gate_up_weight must be [64, 2H, d]")
+    hidden_dim = gate_up_weight.shape[1] // 2
+    if tuple(gate_up_weight.shape) != (EXPERT_COUNT, 2 * hidden_dim, d_model):
+        raise ValueError(f"gate_up_weight must have shape [64, {2 * hidden_dim}, {d_model}]")
+    if tuple(down_weight.shape) != (EXPERT_COUNT, d_model, hidden_dim):
+        raise ValueError(f"down_weight must have shape [64, {d_model}, {hidden_dim}]")
+    for name, t in (("gate_up_weight", gate_up_weight), ("down_weight", down_weight)):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.device != x.device:
+            raise ValueError(f"{name} must be a contiguous BF16 tensor on x's device")
+    if route_probs.dtype != torch.bfloat16 or tuple(route_probs.shape) != (rows,):
+        raise ValueError("route_probs must be BF16 with one entry per row")
+    if expert_offsets.dtype != torch.int32 or tuple(expert_offsets.shape) != (EXPERT_COUNT + 1,):
+        raise ValueError("expert_offsets must be int32 [65]")
+    lib = _lib.library()
+    ws = torch.empty(lib.ce4b_moe_workspace_size(rows, d_model, hidden_dim), dtype=torch.uint8, device=x.device)
+    out = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.check(
+            lib.ce4b_moe_forward(
+                x.data_ptr(), gate_up_weight.data_ptr(), down_weight.data_ptr(),
+                route_probs.contiguous().data_ptr(), expert_offsets.contiguous().data_ptr(),
+                out.data_ptr(), ws.data_ptr(), rows, d_model, hidden_dim, _stream(x),
+            )
+        )
+    return out
+
+
+def moe_route(
+    logits: torch.Tensor, qb_beta: torch.Tensor
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Quantile-balanced top-2 selection of the reference's eval path
+    (src/chess_engine_4/model/moe.py:50-63, 160-177): experts = top-2 of (logits - beta)
+    with the lower index winning ties, weights = softmax(logits)[experts] rounded to BF16.
+
+    Returns (experts int32 [T, 2], weights float32 [T, 2], tokens_per_expert int32 [64]).
+    """
+
+    if logits.device.type != "cuda" or logits.dtype != torch.bfloat16:
+        raise ValueError("logits must be a BF16 CUDA tensor")
+    if logits.ndim != 2 or logits.shape[1] != EXPERT_COUNT or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous [T, 64] matrix")
+    beta = qb_beta.to(device=logits.device, dtype=torch.float32).contiguous()
+    if tuple(beta.shape) != (EXPERT_COUNT,):
+        raise ValueError("qb_beta must have 64 entries")
+    tokens = logits.shape[0]
+    experts = torch.empty(tokens, 2, dtype=torch.int32, device=logits.device)
+    probs = torch.empty(tokens, 2, dtype=torch.float32, device=logits.device)
+    counts = torch.zeros(EXPERT_COUNT, dtype=torch.int32, device=logits.device)
+    with torch.cuda.device(logits.device):
+        _lib.check(
+            _lib.library().ce4b_moe_route(
+                logits.data_ptr(), beta.data_ptr(), experts.data_ptr(), probs.data_ptr(),
+                counts.data_ptr(), tokens, _stream(logits),
+            )
+        )
+    return experts, probs, counts

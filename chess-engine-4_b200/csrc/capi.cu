@@ -311,4 +311,60 @@ int ce4b_dense_block_forward(const void* x_dev, const void* norm_weight_dev,
   });
 }
 
+// ------------------------------------------------------------------ MoE kernel ops
+int ce4b_moe_route(const void* logits_dev, const float* beta_dev, int32_t* experts_dev,
+                   float* probs_dev, int32_t* counts_dev, int tokens, void* stream) {
+  return guarded([&] {
+    require(logits_dev && beta_dev && experts_dev && probs_dev, "null pointer");
+    require(tokens >= 1, "tokens must be positive");
+    moe_route_logits(static_cast<const bf16*>(logits_dev), beta_dev,
+                     reinterpret_cast<int2*>(experts_dev), reinterpret_cast<float2*>(probs_dev),
+                     counts_dev, tokens, as_stream(stream));
+  });
+}
+
+int64_t ce4b_moe_workspace_size(int rows, int d_model, int hidden_dim) {
+  if (rows < 1 || d_model < 1 || hidden_dim < 1) return -1;
+  const int64_t tiles = (static_cast<int64_t>(rows) + 127) / 128 + 64;
+  const int64_t r = (static_cast<int64_t>(rows) + 127) / 128 * 128;
+  auto a = [](int64_t v) { return (v + 255) / 256 * 256; };
+  return a(tiles * 16) + a(4) + a(r * 4) + a(r * hidden_dim * 2);
+}
+
+int ce4b_moe_forward(const void* x_dev, const void* gate_up_weight_dev,
+                     const void* down_weight_dev, const void* route_probs_dev,
+                     const int32_t* expert_offsets_dev, void* out_dev, void* workspace_dev,
+                     int rows, int d_model, int hidden_dim, void* stream) {
+  return guarded([&] {
+    require(x_dev && gate_up_weight_dev && down_weight_dev && route_probs_dev &&
+                expert_offsets_dev && out_dev && workspace_dev,
+            "null pointer");
+    require(rows >= 1, "rows must be positive");
+    require(d_model >= 64 && d_model % 64 == 0, "d_model must be a multiple of 64");
+    require(hidden_dim >= 64 && hidden_dim % 64 == 0, "hidden_dim must be a multiple of 64");
+    require((reinterpret_cast<uintptr_t>(workspace_dev) & 255u) == 0,
+            "workspace must be 256-byte aligned");
+    cudaStream_t s = as_stream(stream);
+    auto a = [](int64_t v) { return (v + 255) / 256 * 256; };
+    const int64_t tiles = (static_cast<int64_t>(rows) + 127) / 128 + 64;
+    const int64_t r = (static_cast<int64_t>(rows) + 127) / 128 * 128;
+    auto* base = static_cast<uint8_t*>(workspace_dev);
+    auto* m_tiles = reinterpret_cast<int4*>(base);
+    auto* num_m_tiles = reinterpret_cast<int*>(base + a(tiles * 16));
+    auto* scale = reinterpret_cast<float*>(base + a(tiles * 16) + a(4));
+    auto* hidden = reinterpret_cast<bf16*>(base + a(tiles * 16) + a(4) + a(r * 4));
+    moe_tiles_from_offsets(expert_offsets_dev, m_tiles, num_m_tiles, s);
+    bf16_to_f32(static_cast<const bf16*>(route_probs_dev), scale, rows, s);
+    const CUtensorMap t_x = make_tmap_bf16(x_dev, rows, d_model, d_model, 128);
+    const CUtensorMap t_gu = make_tmap_bf16(gate_up_weight_dev, 64ull * 2 * hidden_dim, d_model,
+                                            d_model, static_cast<uint32_t>(swiglu_chunk(hidden_dim)));
+    const CUtensorMap t_h = make_tmap_bf16(hidden, rows, hidden_dim, hidden_dim, 128);
+    gemm_grouped_swiglu(t_x, t_gu, t_h, m_tiles, num_m_tiles, hidden_dim, d_model, s);
+    const CUtensorMap t_dn = make_tmap_bf16(down_weight_dev, 64ull * d_model, hidden_dim, hidden_dim,
+                                            static_cast<uint32_t>(grouped_bn(d_model)));
+    const CUtensorMap t_y = make_tmap_bf16(out_dev, rows, d_model, d_model, 128);
+    gemm_grouped_scale(t_h, t_dn, t_y, m_tiles, num_m_tiles, scale, d_model, hidden_dim, s);
+  });
+}
+
 }  // extern "C"

@@ -714,4 +714,123 @@ struct EpiHeads {
   }
 };
 
+// ------------------------------------------------------------------ MoE epilogues
+
+// Top-2 routing of one token from its 64 router logits (BF16 values held as FP32):
+// experts = the two largest (logit - beta), the lower expert index winning ties;
+// weights = FP32 softmax over all 64 raw logits at those experts, rounded to BF16
+// (src/chess_engine_4/model/moe.py:160-177; tie rule of the reference runtime's router).
+__device__ __forceinline__ void route_top2(const float (&lo)[32], const float (&hi)[32],
+                                           const float* __restrict__ beta, int& e0, int& e1,
+                                           float& p0, float& p1) {
+  float mx = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fmaxf(lo[e], hi[e]));
+  float denom = 0.0f, s0 = -INFINITY, s1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  e0 = 0;
+  e1 = 1;
+#pragma unroll
+  for (int e = 0; e < 64; ++e) {
+    const float l = e < 32 ? lo[e] : hi[e - 32];
+    const float s = l - __ldg(beta + e);
+    denom += expf(l - mx);
+    if (s > s0) {
+      s1 = s0;
+      e1 = e0;
+      l1 = l0;
+      s0 = s;
+      e0 = e;
+      l0 = l;
+    } else if (s > s1) {
+      s1 = s;
+      e1 = e;
+      l1 = l;
+    }
+  }
+  p0 = bf16_round(expf(l0 - mx) / denom);
+  p1 = bf16_round(expf(l1 - mx) / denom);
+}
+
+// Router epilogue over a [tokens, 64] logit tile (BN = 64). One thread per token routes it;
+// each CTA writes the expert histogram of its 128 tokens to block_hist[tile] so that the
+// scan can place every route deterministically (stable by token).
+struct EpiRouter {
+  static constexpr int kSmemBytes = 64 * 4;
+  struct Params {
+    const float* beta;   // [64]
+    int2* route_expert;  // [T]
+    float2* route_prob;  // [T] (BF16-rounded values)
+    int* block_hist;     // [T/128 tiles][64]
+  };
+  __device__ static uint32_t bar_count(const Params&, int) { return 1; }
+  __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
+                                  uint32_t) {
+    return false;
+  }
+  template <int G>
+  __device__ static void run(const Params& p, const TileCoord& tc, const EpiThread& et,
+                             const EpiCtx& ctx) {
+    int* hist = reinterpret_cast<int*>(ctx.smem_ptr);
+    if (ctx.iter > 0) epi_bar_sync<G>();  // previous tile's histogram has been written out
+    if (et.tid < 64) hist[et.tid] = 0;
+    epi_bar_sync<G>();
+    if (et.g == 0) {
+      float lo[32], hi[32];
+      load_acc32x2(et.taddr, et.taddr + 32, lo, hi);
+      round_bf16_inplace(lo);
+      round_bf16_inplace(hi);
+      int e0, e1;
+      float p0, p1;
+      route_top2(lo, hi, p.beta, e0, e1, p0, p1);
+      if (et.r < tc.rows) {
+        const int row = tc.out_row + et.r;
+        p.route_expert[row] = make_int2(e0, e1);
+        p.route_prob[row] = make_float2(p0, p1);
+        atomicAdd(&hist[e0], 1);
+        atomicAdd(&hist[e1], 1);
+      }
+    }
+    release_accumulator(ctx);
+    epi_bar_sync<G>();
+    if (et.tid < 64) p.block_hist[(tc.a_row / kBM) * 64 + et.tid] = hist[et.tid];
+  }
+};
+
+// Expert down-projection epilogue: y = bf16(acc * prob[row]) for the permuted rows of one
+// expert segment, staged and TMA-stored through tmO1 (the probability scales the FP32
+// accumulator, as the reference's expert kernels do).
+template <int BN>
+struct EpiScaleStore {
+  static_assert(BN % 64 == 0, "64-column boxes");
+  static constexpr int kSmemBytes = kBM * BN * 2;
+  struct Params {
+    const float* row_scale;  // [rows] per permuted row
+  };
+  __device__ static uint32_t bar_count(const Params&, int) { return 1; }
+  __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
+                                  uint32_t) {
+    return false;
+  }
+  template <int G>
+  __device__ static void run(const Params& p, const TileCoord& tc, const EpiThread& et,
+                             const EpiCtx& ctx) {
+    if (ctx.iter > 0) {
+      if (et.tid == 0) bulk_wait_read_all();
+      epi_bar_sync<G>();
+    }
+    const float scale = et.r < tc.rows ? __ldg(p.row_scale + tc.out_row + et.r) : 0.0f;
+    for (int c = et.g * 32; c < BN; c += G * 32) {
+      float v[32];
+      load_acc32(et.taddr + c, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= scale;
+      stage_bf16x32(ctx.smem, et.r, c, v);
+    }
+    release_accumulator(ctx);
+    fence_proxy_async_smem();
+    epi_bar_sync<G>();
+    if (et.tid == 0) store_staged(ctx.tmO1, ctx.smem, BN, tc.n_tile * BN, tc.out_row);
+  }
+};
+
 }  // namespace ce4b

@@ -198,4 +198,80 @@ void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, 
          ep, ceil_div(d, kBK), device_error_word());
 }
 
+// ------------------------------------------------------------------ MoE GEMMs
+void moe_router_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const float* beta,
+                     int2* route_expert, float2* route_prob, int* block_hist, int tokens, int d,
+                     cudaStream_t s) {
+  constexpr int BN = 64, NS = 8, NA = 1;
+  using Epi = EpiRouter;
+  auto kernel = gemm_tc_kernel<BN, NS, NA, 1, kG, false, DenseSched, Epi>;
+  constexpr int smem = GemmSmem<BN, NS, NA, Epi>::kBytes;
+  ensure_smem(kernel, smem);
+  DenseSched sched{tokens, 1, ceil_div(tokens, kBM), BN, 0};
+  typename Epi::Params ep{beta, route_expert, route_prob, block_hist};
+  // One tile (128 tokens) per CTA: block_hist row = tile index.
+  launch(kernel, dim3(sched.num_tiles), gemm_threads(kG), smem, 0, s, tA, tB, null_map(),
+         null_map(), sched, ep, ceil_div(d, kBK), device_error_word());
+}
+
+void gemm_grouped_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH,
+                         const int4* m_tiles, const int* num_m_tiles, int hidden, int k,
+                         cudaStream_t s) {
+  const int hc = swiglu_chunk(hidden);
+  require(hidden % hc == 0, "expert hidden dim must be a multiple of 64");
+  GroupedSched sched{m_tiles, num_m_tiles, hidden / hc, hc, 2 * hidden, hidden};
+  const int grid = sm_count();
+  if (hc == 128) {
+    constexpr int BN = 256, NS = 4, NA = 2;
+    using Epi = EpiSwiGLU<128>;
+    auto kernel = gemm_tc_kernel<BN, NS, NA, 2, kG, false, GroupedSched, Epi>;
+    constexpr int smem = GemmSmem<BN, NS, NA, Epi>::kBytes;
+    ensure_smem(kernel, smem);
+    typename Epi::Params ep{0};
+    launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tH, null_map(), sched, ep,
+           ceil_div(k, kBK), device_error_word());
+  } else {
+    constexpr int BN = 128, NS = 6, NA = 2;
+    using Epi = EpiSwiGLU<64>;
+    auto kernel = gemm_tc_kernel<BN, NS, NA, 2, kG, false, GroupedSched, Epi>;
+    constexpr int smem = GemmSmem<BN, NS, NA, Epi>::kBytes;
+    ensure_smem(kernel, smem);
+    typename Epi::Params ep{0};
+    launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tH, null_map(), sched, ep,
+           ceil_div(k, kBK), device_error_word());
+  }
+}
+
+int grouped_bn(int n) {
+  if (n % 256 == 0) return 256;
+  if (n % 128 == 0) return 128;
+  require(n % 64 == 0, "expert output width must be a multiple of 64");
+  return 64;
+}
+
+template <int BN, int NS>
+static void gemm_grouped_scale_bn(const CUtensorMap& tA, const CUtensorMap& tB,
+                                  const CUtensorMap& tY, const int4* m_tiles,
+                                  const int* num_m_tiles, const float* row_scale, int n, int k,
+                                  cudaStream_t s) {
+  using Epi = EpiScaleStore<BN>;
+  auto kernel = gemm_tc_kernel<BN, NS, 2, 1, kG, false, GroupedSched, Epi>;
+  constexpr int smem = GemmSmem<BN, NS, 2, Epi>::kBytes;
+  ensure_smem(kernel, smem);
+  GroupedSched sched{m_tiles, num_m_tiles, n / BN, BN, n, 0};
+  typename Epi::Params ep{row_scale};
+  launch(kernel, dim3(sm_count()), gemm_threads(kG), smem, 0, s, tA, tB, tY, null_map(), sched, ep,
+         ceil_div(k, kBK), device_error_word());
+}
+
+void gemm_grouped_scale(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tY,
+                        const int4* m_tiles, const int* num_m_tiles, const float* row_scale, int n,
+                        int k, cudaStream_t s) {
+  switch (grouped_bn(n)) {
+    case 256: gemm_grouped_scale_bn<256, 3>(tA, tB, tY, m_tiles, num_m_tiles, row_scale, n, k, s); break;
+    case 128: gemm_grouped_scale_bn<128, 5>(tA, tB, tY, m_tiles, num_m_tiles, row_scale, n, k, s); break;
+    default: gemm_grouped_scale_bn<64, 7>(tA, tB, tY, m_tiles, num_m_tiles, row_scale, n, k, s); break;
+  }
+}
+
 }  // namespace ce4b

@@ -72,6 +72,33 @@ void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, 
                 float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,
                 int wdl_probs, cudaStream_t s);
 
+// ---------------------------------------------------------------- MoE
+// Router GEMM (A = normalised rows [T, d], B = router weight [64, d] with 64-row boxes)
+// with the top-2 routing epilogue; block_hist receives [ceil(T/128)][64] counts.
+void moe_router_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const float* beta,
+                     int2* route_expert, float2* route_prob, int* block_hist, int tokens, int d,
+                     cudaStream_t s);
+void moe_scan(const int* block_hist, int ntiles, int* expert_start, int* block_off,
+              int4* m_tiles, int* num_m_tiles, int* counts_out, cudaStream_t s);
+void moe_dispatch(const bf16* n, const int2* route_expert, const float2* route_prob,
+                  const int* expert_start, const int* block_off, bf16* xperm, float* pprob,
+                  int* route_pos, int tokens, int d, cudaStream_t s);
+// Grouped expert GEMMs over the device-side m-tile table. B rows per expert: 2*hidden for
+// gate_up (box rows = swiglu_chunk(hidden)), n for down (box rows = grouped_bn(n)).
+void gemm_grouped_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH,
+                         const int4* m_tiles, const int* num_m_tiles, int hidden, int k,
+                         cudaStream_t s);
+int grouped_bn(int n);
+void gemm_grouped_scale(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tY,
+                        const int4* m_tiles, const int* num_m_tiles, const float* row_scale, int n,
+                        int k, cudaStream_t s);
+void moe_combine_norm(bf16* x, const bf16* yperm, const int* route_pos, const bf16* norm_w,
+                      bf16* nout, int tokens, int d, float eps, cudaStream_t s);
+void moe_tiles_from_offsets(const int* offsets, int4* m_tiles, int* num_m_tiles, cudaStream_t s);
+void moe_route_logits(const bf16* logits, const float* beta, int2* experts, float2* probs,
+                      int* counts, int tokens, cudaStream_t s);
+void bf16_to_f32(const bf16* in, float* out, int n, cudaStream_t s);
+
 // ---------------------------------------------------------------- elementwise
 // Expand an input batch into the BF16 GEMM operand [B, selected_planes * 64].
 void expand_input(int layout, const void* input, const void* scalars, int batch, int history,

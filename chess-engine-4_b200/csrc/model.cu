@@ -106,6 +106,24 @@ void Model::plan_workspace() {
   ws_off.policy = take(r * policy_size * 4);
   ws_off.wdl = take(r * 3 * 4);
   ws_off.moves_left = take(r * 4);
+  if (cfg.arch == CE4B_ARCH_MOE64A2) {
+    // Expert rows: 2 routes per token, each expert segment padded to 128 rows.
+    perm_rows = static_cast<int>((2 * r + 64 * 127 + 127) / 128 * 128);
+    const size_t p = static_cast<size_t>(perm_rows);
+    const size_t tiles = r / 128;
+    ws_off.route_expert = take(r * 8);
+    ws_off.route_prob = take(r * 8);
+    ws_off.route_pos = take(r * 8);
+    ws_off.block_hist = take(tiles * 64 * 4);
+    ws_off.block_off = take(tiles * 64 * 4);
+    ws_off.expert_start = take(64 * 4);
+    ws_off.m_tiles = take((p / 128) * 16);
+    ws_off.num_m_tiles = take(4);
+    ws_off.xperm = take(p * d * 2);
+    ws_off.pprob = take(p * 4);
+    ws_off.hperm = take(p * expert_hidden * 2);
+    ws_off.yperm = take(p * d * 2);
+  }
   workspace_bytes = align256(cur);
 }
 
@@ -133,7 +151,6 @@ void Model::create(const ce4b_model_config& c, int dev, int maxb) {
   }
   if (c.arch == CE4B_ARCH_MOE64A2) {
     require(c.depth % 2 == 0, "moe64a2 depth must be a positive even number");
-    fail(CE4B_ERR_UNSUPPORTED, "moe64a2 forward is not available in this build");
   }
   const int hid = static_cast<int>(static_cast<double>(c.d_model) * c.expansion_ratio);
   dense_hidden = c.arch == CE4B_ARCH_DENSE ? hid : 4 * c.d_model;
@@ -202,8 +219,21 @@ void Model::finalize() {
       const uint32_t hc = static_cast<uint32_t>(swiglu_chunk(dense_hidden));
       L.tm_gate_up = make_tmap_bf16(w(p + ".gate_up.weight"), 2 * dense_hidden, d, d, hc);
       L.tm_down = make_tmap_bf16(w(p + ".down.weight"), d, dense_hidden, dense_hidden, bn);
+    } else {
+      const int he = expert_hidden;
+      L.tm_router = make_tmap_bf16(w(p + ".router.weight"), 64, d, d, 64);
+      L.beta = reinterpret_cast<const float*>(w(p + ".router_qb_beta"));
+      L.tm_gate_up = make_tmap_bf16(w(p + ".experts.gate_up.weight"), 64ull * 2 * he, d, d,
+                                    static_cast<uint32_t>(swiglu_chunk(he)));
+      L.tm_down = make_tmap_bf16(w(p + ".experts.down.weight"), 64ull * d, he, he,
+                                 static_cast<uint32_t>(grouped_bn(d)));
     }
     layers.push_back(L);
+  }
+  if (cfg.arch == CE4B_ARCH_MOE64A2) {
+    tm_xperm = make_tmap_bf16(workspace + ws_off.xperm, perm_rows, d, d, 128);
+    tm_hperm = make_tmap_bf16(workspace + ws_off.hperm, perm_rows, expert_hidden, expert_hidden, 128);
+    tm_yperm = make_tmap_bf16(workspace + ws_off.yperm, perm_rows, d, d, 128);
   }
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   graphs.clear();
@@ -213,7 +243,6 @@ void Model::finalize() {
 void Model::forward(int layout, void* input, const void* scalars, int batch, float* policy,
                     float* wdl, float* moves_left, int wdl_probs, int normalize_in_place,
                     int32_t* tokens_per_expert, cudaStream_t s) {
-  (void)tokens_per_expert;
   if (!finalized) fail(CE4B_ERR_NOT_READY, "model is not finalized");
   require(batch >= 1 && batch <= max_batch,
           "batch size " + std::to_string(batch) + " exceeds model capacity " +
@@ -235,6 +264,10 @@ void Model::forward(int layout, void* input, const void* scalars, int batch, flo
   for (int l = 0; l < cfg.depth; ++l) {
     const Layer& L = layers[l];
     const bf16* next_norm = l + 1 < cfg.depth ? layers[l + 1].norm : w("final_norm.weight");
+    if (L.moe) {
+      moe_layer(L, l / 2, next_norm, batch, tokens_per_expert, s);
+      continue;
+    }
     gemm_swiglu(tm_n, L.tm_gate_up, tm_hidden, batch, dense_hidden, d, s);
     trace("gate_up_swiglu", s);
     gemm_resnorm(tm_hidden, L.tm_down, tm_x, tm_n, nullptr, next_norm, batch, d, dense_hidden, eps,
@@ -244,6 +277,43 @@ void Model::forward(int layout, void* input, const void* scalars, int batch, flo
   gemm_heads(tm_n, tm_heads, w("policy.bias"), policy, wdl, moves_left, batch, d, policy_size,
              policy_storage, wdl_probs, s);
   trace("heads", s);
+}
+
+// One moe64a2 expert layer (src/chess_engine_4/model/moe.py:160-180, static dispatch path
+// :226-287): router GEMM with the top-2 epilogue, scan, dispatch, grouped gate_up+SwiGLU,
+// grouped down scaled by the route weight, combine + residual + next layer's RMSNorm.
+void Model::moe_layer(const Layer& L, int moe_index, const bf16* next_norm, int batch,
+                      int32_t* tokens_per_expert, cudaStream_t s) {
+  const int d = cfg.d_model;
+  const int he = expert_hidden;
+  auto at = [&](size_t off) { return workspace + off; };
+  auto* route_expert = reinterpret_cast<int2*>(at(ws_off.route_expert));
+  auto* route_prob = reinterpret_cast<float2*>(at(ws_off.route_prob));
+  auto* route_pos = reinterpret_cast<int*>(at(ws_off.route_pos));
+  auto* block_hist = reinterpret_cast<int*>(at(ws_off.block_hist));
+  auto* block_off = reinterpret_cast<int*>(at(ws_off.block_off));
+  auto* expert_start = reinterpret_cast<int*>(at(ws_off.expert_start));
+  auto* m_tiles = reinterpret_cast<int4*>(at(ws_off.m_tiles));
+  auto* num_m_tiles = reinterpret_cast<int*>(at(ws_off.num_m_tiles));
+  auto* xperm = reinterpret_cast<bf16*>(at(ws_off.xperm));
+  auto* pprob = reinterpret_cast<float*>(at(ws_off.pprob));
+  auto* yperm = reinterpret_cast<bf16*>(at(ws_off.yperm));
+  auto* x = reinterpret_cast<bf16*>(at(ws_off.x));
+  auto* n = reinterpret_cast<bf16*>(at(ws_off.n));
+  moe_router_gemm(tm_n, L.tm_router, L.beta, route_expert, route_prob, block_hist, batch, d, s);
+  trace("moe_router", s);
+  moe_scan(block_hist, (batch + 127) / 128, expert_start, block_off, m_tiles, num_m_tiles,
+           tokens_per_expert != nullptr ? tokens_per_expert + 64 * moe_index : nullptr, s);
+  trace("moe_scan", s);
+  moe_dispatch(n, route_expert, route_prob, expert_start, block_off, xperm, pprob, route_pos,
+               batch, d, s);
+  trace("moe_dispatch", s);
+  gemm_grouped_swiglu(tm_xperm, L.tm_gate_up, tm_hperm, m_tiles, num_m_tiles, he, d, s);
+  trace("moe_experts_gate_up_swiglu", s);
+  gemm_grouped_scale(tm_hperm, L.tm_down, tm_yperm, m_tiles, num_m_tiles, pprob, d, he, s);
+  trace("moe_experts_down", s);
+  moe_combine_norm(x, yperm, route_pos, next_norm, n, batch, d, cfg.rms_norm_eps, s);
+  trace("moe_combine_rmsnorm", s);
 }
 
 void Model::trace(const char* label, cudaStream_t s) {

@@ -21,11 +21,16 @@ struct Model {
   struct Layer {
     bool moe = false;
     const bf16* norm = nullptr;
-    CUtensorMap tm_gate_up{};
-    CUtensorMap tm_down{};
+    CUtensorMap tm_gate_up{};  // dense gate_up, or stacked expert gate_up [64*2h_e, d]
+    CUtensorMap tm_down{};     // dense down, or stacked expert down [64*d, h_e]
+    CUtensorMap tm_router{};   // MoE router [64, d]
+    const float* beta = nullptr;  // MoE router_qb_beta [64]
   };
   struct WorkspaceOffsets {
     size_t planes = 0, a_in = 0, x = 0, n = 0, hidden = 0, policy = 0, wdl = 0, moves_left = 0;
+    size_t route_expert = 0, route_prob = 0, route_pos = 0, block_hist = 0, block_off = 0;
+    size_t expert_start = 0, m_tiles = 0, num_m_tiles = 0, xperm = 0, pprob = 0, hperm = 0;
+    size_t yperm = 0;
   };
 
   ce4b_model_config cfg{};
@@ -38,6 +43,7 @@ struct Model {
   int in_dim = 0;
   int policy_size = 0;
   int policy_storage = 0;
+  int perm_rows = 0;  // MoE permuted-row capacity
 
   uint8_t* arena = nullptr;
   size_t arena_bytes = 0;
@@ -47,6 +53,7 @@ struct Model {
   WorkspaceOffsets ws_off;
 
   CUtensorMap tm_a_in{}, tm_x{}, tm_n{}, tm_hidden{}, tm_w_in{}, tm_heads{};
+  CUtensorMap tm_xperm{}, tm_hperm{}, tm_yperm{};
   std::vector<Layer> layers;
   bool finalized = false;
   cudaStream_t stream = nullptr;
@@ -74,6 +81,8 @@ struct Model {
   void enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
                         float* host_wdl, float* host_moves_left, cudaStream_t s);
   void trace(const char* label, cudaStream_t s);
+  void moe_layer(const Layer& L, int moe_index, const bf16* next_norm, int batch,
+                 int32_t* tokens_per_expert, cudaStream_t s);
 
  private:
   void add_slot(const std::string& name, std::vector<int64_t> shape, int dtype, size_t& cursor,

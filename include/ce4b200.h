@@ -195,6 +195,30 @@ int ce4b_dense_block_forward(const void* x_dev, const void* norm_weight_dev,
                              void* out_dev, void* workspace_dev, int rows, int d_model,
                              int hidden_dim, float eps, int precision, void* stream);
 
+/* Top-2 routing of BF16 router logits [tokens, 64] with the quantile-balancing offsets
+ * beta [64] (FP32): experts [tokens, 2] int32 (best first; the lower index wins ties),
+ * probs [tokens, 2] FP32 holding the BF16-rounded softmax weights over all 64 logits,
+ * counts [64] int32 incremented per route (may be NULL; zero it first). Replaces the
+ * selection in MoeBlock.forward (src/chess_engine_4/model/moe.py:160-177) and the
+ * runtime's RouteKernel (kernels/src/inference/moe_bf16_impl.cuh:18-68). */
+int ce4b_moe_route(const void* logits_dev, const float* beta_dev, int32_t* experts_dev,
+                   float* probs_dev, int32_t* counts_dev, int tokens, void* stream);
+
+/* Scratch bytes ce4b_moe_forward needs. */
+int64_t ce4b_moe_workspace_size(int rows, int d_model, int hidden_dim);
+
+/* Expert MLP over rows already sorted by expert: rows [offsets[e], offsets[e+1]) of x
+ * [rows, d] go through expert e: out = ((silu(x.Wg^T) * (x.Wu^T)) . Wd^T) * route_probs
+ * per row (BF16, FP32 accumulate). gate_up [64, 2H, d] (gate rows first), down [64, d, H],
+ * route_probs [rows] BF16, expert_offsets [65] int32 on the device, each a multiple of 128
+ * (the reference's static path pads segments to 128 rows); a misaligned offset sets the
+ * device error word and that expert is skipped. Rows past offsets[64] are not written.
+ * Replaces moe_forward (src/chess_engine_4/kernels/moe.py:24-46). */
+int ce4b_moe_forward(const void* x_dev, const void* gate_up_weight_dev,
+                     const void* down_weight_dev, const void* route_probs_dev,
+                     const int32_t* expert_offsets_dev, void* out_dev, void* workspace_dev,
+                     int rows, int d_model, int hidden_dim, void* stream);
+
 /* ce4b_dense_block_forward for callers that cannot allocate device memory (an engine
  * thread whose process freezes its allocator after start-up, a plugin that is handed only
  * its input and output buffers, code under a no-allocation budget). Same arguments and
