@@ -7,6 +7,8 @@ device, dtype, rank and shape problems; src/chess_engine_4/kernels/dense.py:33-4
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 
 from . import _lib
@@ -166,6 +168,63 @@ def dense_block_forward(
                 eps,
                 _lib.PRECISION_BF16,
                 _stream(x),
+            )
+        )
+    return out
+
+
+MXFP8_TILE_SIZE = 128
+
+
+@dataclass(frozen=True, slots=True)
+class Mxfp8Tensor:
+    """E4M3 codes and their E8M0 scale tiles (src/chess_engine_4/kernels/dense.py:27-30)."""
+
+    values: torch.Tensor  # float8_e4m3fn [rows, cols]
+    scales: torch.Tensor  # uint8 [rows/128, cols/128, 32, 16]
+
+
+def _check_mx_matrix(name: str, tensor: torch.Tensor) -> None:
+    _check_bf16_matrix(name, tensor)
+    if any(size % MXFP8_TILE_SIZE for size in tensor.shape):
+        raise ValueError(f"{name} dimensions must be multiples of {MXFP8_TILE_SIZE}")
+
+
+def quantize_mxfp8(tensor: torch.Tensor) -> Mxfp8Tensor:
+    """MXFP8 quantisation, bit-exact to the reference recipe (kernels/dense.py:46-60)."""
+
+    _check_mx_matrix("tensor", tensor)
+    rows, cols = tensor.shape
+    values = torch.empty_like(tensor, dtype=torch.float8_e4m3fn)
+    scales = torch.empty(rows // 128, cols // 128, 32, 16, dtype=torch.uint8, device=tensor.device)
+    with torch.cuda.device(tensor.device):
+        _lib.check(
+            _lib.library().ce4b_quantize_mxfp8(
+                tensor.data_ptr(), values.data_ptr(), scales.data_ptr(), rows, cols, _stream(tensor)
+            )
+        )
+    return Mxfp8Tensor(values=values, scales=scales)
+
+
+def mxfp8_gemm(left: Mxfp8Tensor, right: Mxfp8Tensor) -> torch.Tensor:
+    """``dequant(left) @ dequant(right).T`` in BF16 on block-scaled tcgen05 MMAs
+    (replaces kernels/dense.py:87-113; any output width divisible by 128)."""
+
+    rows, reduction = left.values.shape
+    out_cols, right_reduction = right.values.shape
+    if reduction != right_reduction:
+        raise ValueError("MXFP8 GEMM reduction dimensions do not match")
+    for t in (left.values, right.values):
+        if t.device.type != "cuda" or t.dtype != torch.float8_e4m3fn or not t.is_contiguous():
+            raise ValueError("MXFP8 values must be contiguous float8_e4m3fn CUDA tensors")
+    if rows % 128 or out_cols % 128 or reduction % 128:
+        raise ValueError("MXFP8 GEMM dimensions must be multiples of 128")
+    out = torch.empty(rows, out_cols, dtype=torch.bfloat16, device=left.values.device)
+    with torch.cuda.device(out.device):
+        _lib.check(
+            _lib.library().ce4b_mxfp8_gemm(
+                left.values.data_ptr(), left.scales.data_ptr(), right.values.data_ptr(),
+                right.scales.data_ptr(), out.data_ptr(), rows, out_cols, reduction, _stream(out),
             )
         )
     return out

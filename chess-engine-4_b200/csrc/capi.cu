@@ -367,4 +367,30 @@ int ce4b_moe_forward(const void* x_dev, const void* gate_up_weight_dev,
   });
 }
 
+// ------------------------------------------------------------------ MXFP8 kernel ops
+int ce4b_quantize_mxfp8(const void* x_dev, void* codes_dev, void* scales_dev, int rows, int cols,
+                        void* stream) {
+  return guarded([&] {
+    require(x_dev && codes_dev && scales_dev, "null pointer");
+    require(rows >= 128 && cols >= 128, "MXFP8 tensors need at least 128 rows and columns");
+    mx_quantize(static_cast<const bf16*>(x_dev), static_cast<uint8_t*>(codes_dev),
+                static_cast<uint8_t*>(scales_dev), rows, cols, as_stream(stream));
+  });
+}
+
+int ce4b_mxfp8_gemm(const void* a_codes_dev, const void* a_scales_dev, const void* b_codes_dev,
+                    const void* b_scales_dev, void* c_dev, int m, int n, int k, void* stream) {
+  return guarded([&] {
+    require(a_codes_dev && a_scales_dev && b_codes_dev && b_scales_dev && c_dev, "null pointer");
+    require(m >= 128 && n >= 128 && k >= 128, "MXFP8 GEMM extents must be at least 128");
+    require(m % 128 == 0 && n % 128 == 0 && k % 128 == 0,
+            "MXFP8 GEMM extents must be multiples of 128");
+    const CUtensorMap ta = make_tmap_u8(a_codes_dev, m, k, k, 128);
+    const CUtensorMap tb = make_tmap_u8(b_codes_dev, n, k, k, 128);
+    const CUtensorMap tc = make_tmap_bf16(c_dev, m, n, n, 128);
+    gemm_mx_store_bf16(ta, tb, tc, static_cast<const uint8_t*>(a_scales_dev),
+                       static_cast<const uint8_t*>(b_scales_dev), m, n, k, as_stream(stream));
+  });
+}
+
 }  // extern "C"

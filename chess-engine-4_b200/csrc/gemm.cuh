@@ -338,6 +338,256 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
   }
 }
 
+// ------------------------------------------------------------------ MXFP8 GEMM
+// Block-scaled variant: A, B are E4M3 codes (K-major, one k-block = 128 codes = one
+// 128-byte swizzle span), with E8M0 scales per row per 32 codes stored as 512-byte
+// [32][16] tiles per (128 rows, 128 codes) (the tcgen05 scale-factor layout). Each stage
+// holds the A and B code tiles plus their scale tiles; the MMA thread copies the scale
+// tiles into a per-stage tensor-memory region (tcgen05.cp ... 32x128b.warpx4) and issues
+// four K=32 block-scaled MMAs per k-block. Every MMA is N=128; a BN=256 tile issues two
+// (one per 128-row half of B, each with its own B scale tile).
+struct MxScales {
+  const uint8_t* sfa;  // [M/128][K/128][512]
+  const uint8_t* sfb;  // [N/128][K/128][512]
+  int k_tiles;         // K / 128
+};
+
+template <int BN, int NSTAGE, int NACC, class Epi>
+struct GemmMxSmem {
+  static constexpr int kNSub = BN / 128;
+  static constexpr int kABytes = kBM * 128;
+  static constexpr int kBBytes = BN * 128;
+  static constexpr int kLoadBytes = kABytes + kBBytes + 512 * (1 + kNSub);  // per stage
+  static constexpr int kSfBytes = (512 * (1 + kNSub) + 1023) / 1024 * 1024;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfBytes;
+  static constexpr int kRingBytes = NSTAGE * kStageBytes;
+  static constexpr int kEpiBytes = (Epi::kSmemBytes + 1023) / 1024 * 1024;
+  static constexpr int kBarrierBytes = (2 * NSTAGE + 2 * NACC + 3) * 8 + 8;
+  static constexpr int kBytes = 1024 + kRingBytes + kEpiBytes + kBarrierBytes;
+  static constexpr int kSfCols = 4 * (1 + kNSub);  // TMEM columns of one stage's scales
+  static constexpr int kUsedCols = NACC * BN + NSTAGE * kSfCols;
+  static constexpr uint32_t kTmemCols = kUsedCols <= 128 ? 128 : (kUsedCols <= 256 ? 256 : 512);
+  static_assert(kUsedCols <= 512, "TMEM overflow");
+  static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
+  static_assert(kBytes <= 232448, "shared memory budget exceeded");
+};
+
+template <int BN, int NSTAGE, int NACC, int NBOX, int G, class Sched, class Epi>
+__global__ void __launch_bounds__(gemm_threads(G), 1)
+    gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO1, const __grid_constant__ CUtensorMap tmO2,
+                   const Sched sched, const typename Epi::Params ep, const MxScales sf,
+                   const int kblocks, int* err) {
+  using L = GemmMxSmem<BN, NSTAGE, NACC, Epi>;
+  constexpr int kNSub = L::kNSub;
+  constexpr int kBoxRows = BN / NBOX;
+  static_assert(BN == 128 || BN == 256, "MXFP8 tiles are 128 or 256 columns");
+  constexpr uint32_t kEpiThreads = 128 * G;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint32_t base = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  base += pad;
+
+  const uint32_t epi_base = base + L::kRingBytes;
+  const uint32_t bar_base = epi_base + L::kEpiBytes;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (NSTAGE + s); };
+  auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * NSTAGE + a); };
+  auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * NSTAGE + NACC + a); };
+  const uint32_t drain_bar = bar_base + 8u * (2 * NSTAGE + 2 * NACC);
+  const uint32_t epi_bar = drain_bar + 8u;
+  const uint32_t x_bar = drain_bar + 16u;
+  uint32_t* tmem_slot =
+      reinterpret_cast<uint32_t*>(smem + L::kRingBytes + L::kEpiBytes + L::kBarrierBytes - 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < NACC; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), kEpiThreads);
+    }
+    mbar_init(drain_bar, 1);
+    mbar_init(epi_bar, Epi::bar_count(ep, G));
+    mbar_init(x_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+    tmem_relinquish();
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool x_issued = false;
+      const int ntiles = sched.count();
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const TileCoord tc = sched.coord(t);
+        const int a_tile = tc.a_row / kBM;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
+            record_error(err, kErrTimeoutProducer);
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + stage * L::kStageBytes;
+          const uint32_t sb = sa + L::kABytes;
+          const uint32_t ssf = sb + L::kBBytes;
+          mbar_arrive_expect_tx(full_bar(stage), L::kLoadBytes);
+          tma_load_2d(sa, &tmA, full_bar(stage), kb * 128, tc.a_row);
+          tma_load_2d(sb, &tmB, full_bar(stage), kb * 128, tc.b_row);
+          if constexpr (NBOX == 2) {
+            tma_load_2d(sb + kBoxRows * 128, &tmB, full_bar(stage), kb * 128, tc.b_row2);
+          }
+          bulk_load(ssf, sf.sfa + (static_cast<size_t>(a_tile) * sf.k_tiles + kb) * 512, 512,
+                    full_bar(stage));
+#pragma unroll
+          for (int j = 0; j < kNSub; ++j) {
+            const int brow = (NBOX == 2 && j == 1) ? tc.b_row2 : tc.b_row + 128 * j;
+            bulk_load(ssf + 512u * (1 + j),
+                      sf.sfb + (static_cast<size_t>(brow / 128) * sf.k_tiles + kb) * 512, 512,
+                      full_bar(stage));
+          }
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (kb == 0 && !x_issued && Epi::prefetch(ep, tc, &tmO1, epi_base, x_bar)) x_issued = true;
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < NSTAGE; ++s) {
+          if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_phase >> s) & 1u);
+        }
+        if (x_issued) mbar_wait(x_bar, 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      const int ntiles = sched.count();
+      const uint32_t sf_base = tmem_base + static_cast<uint32_t>(NACC * BN);
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u)) {
+          record_error(err, kErrTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase)) {
+            record_error(err, kErrTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * L::kStageBytes;
+          const uint32_t sb = sa + L::kABytes;
+          const uint32_t ssf = sb + L::kBBytes;
+          const uint32_t sfa_t = sf_base + static_cast<uint32_t>(stage * L::kSfCols);
+          tmem_cp_32x128b_x4(sfa_t, sdesc_sf32x16(ssf));
+#pragma unroll
+          for (int j = 0; j < kNSub; ++j) {
+            tmem_cp_32x128b_x4(sfa_t + 4u * (1 + j), sdesc_sf32x16(ssf + 512u * (1 + j)));
+          }
+          const uint64_t adesc = sdesc_k128(sa);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+#pragma unroll
+            for (int j = 0; j < kNSub; ++j) {
+              const uint64_t bdesc = sdesc_k128(sb + static_cast<uint32_t>(j) * (128u * 128u));
+              umma_mxf8(d_tmem + 128u * j, adesc + 2u * k, bdesc + 2u * k, idesc_mxf8(kBM, 128, k),
+                        sfa_t, sfa_t + 4u * (1 + j), (kb | k) != 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        if (++acc == NACC) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      umma_commit(drain_bar);
+      if (!mbar_wait(drain_bar, 0)) record_error(err, kErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    EpiThread et;
+    et.r = quarter * 32 + lane;
+    et.g = (warp - 2) >> 2;
+    et.tid = threadIdx.x - 64;
+    EpiCtx ctx;
+    ctx.smem = epi_base;
+    ctx.smem_ptr = smem + L::kRingBytes;
+    ctx.ring = base;
+    ctx.epi_bar = epi_bar;
+    ctx.x_bar = x_bar;
+    ctx.tmO1 = &tmO1;
+    ctx.tmO2 = &tmO2;
+    ctx.err = err;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int iter = 0;
+    const int ntiles = sched.count();
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++iter) {
+      const TileCoord tc = sched.coord(t);
+      if (!mbar_wait(tfull_bar(acc), acc_phase)) {
+        record_error(err, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      et.taddr =
+          tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      ctx.iter = iter;
+      ctx.tempty_bar = tempty_bar(acc);
+      Epi::template run<G>(ep, tc, et, ctx);
+      if (++acc == NACC) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (et.tid == 0) bulk_wait_all();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ epilogue helpers
 
 // Load 32 consecutive FP32 accumulator columns of this thread's row (one wait).

@@ -100,6 +100,44 @@ CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64
   return map;
 }
 
+CUtensorMap make_tmap_u8(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
+                         uint32_t box_rows) {
+  require(ptr != nullptr, "tensor map: null pointer");
+  require((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0, "tensor map: base not 16-byte aligned");
+  require(ld_bytes % 16 == 0, "tensor map: row stride not a multiple of 16 bytes");
+  require(rows >= 1 && cols >= 1 && box_rows >= 1 && box_rows <= 256, "tensor map: bad extent");
+  CUtensorMap map;
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {ld_bytes};
+  const cuuint32_t box[2] = {128, box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr),
+                                 gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(CE4B_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return map;
+}
+
+// ------------------------------------------------------------------ MXFP8 GEMMs
+void gemm_mx_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
+                        const uint8_t* sfa, const uint8_t* sfb, int m, int n, int k,
+                        cudaStream_t s) {
+  require(m % 128 == 0 && n % 128 == 0 && k % 128 == 0,
+          "MXFP8 GEMM extents must be multiples of 128");
+  constexpr int BN = 128, NS = 5, NA = 2;
+  using Epi = EpiStoreBF16<BN>;
+  auto kernel = gemm_mx_kernel<BN, NS, NA, 1, kG, DenseSched, Epi>;
+  constexpr int smem = GemmMxSmem<BN, NS, NA, Epi>::kBytes;
+  ensure_smem(kernel, smem);
+  DenseSched sched{m, n / BN, (m / kBM) * (n / BN), BN, 0};
+  typename Epi::Params ep{n};
+  const MxScales sf{sfa, sfb, k / 128};
+  const int grid = std::min(sched.num_tiles, sm_count());
+  launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tC, null_map(), sched, ep, sf,
+         k / 128, device_error_word());
+}
+
 // ------------------------------------------------------------------ plain store
 void gemm_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC, int m,
                      int n, int k, cudaStream_t s) {

@@ -99,6 +99,19 @@ void moe_route_logits(const bf16* logits, const float* beta, int2* experts, floa
                       int* counts, int tokens, cudaStream_t s);
 void bf16_to_f32(const bf16* in, float* out, int n, cudaStream_t s);
 
+// ---------------------------------------------------------------- MXFP8
+// BF16 [rows, cols] -> E4M3 codes [rows, cols] + E8M0 scales [rows/128][cols/128][512].
+void mx_quantize(const bf16* x, uint8_t* codes, uint8_t* scales, int rows, int cols,
+                 cudaStream_t s);
+// 2-D byte (E4M3 code) tensor map, 128-byte swizzle, box = 128 codes x box_rows.
+CUtensorMap make_tmap_u8(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
+                         uint32_t box_rows);
+// C[M,N] BF16 = block-scaled E4M3 A[M,K] . B[N,K]^T (M, N, K multiples of 128; maps with
+// 128-row boxes; C map BF16 with 128-row boxes).
+void gemm_mx_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
+                        const uint8_t* sfa, const uint8_t* sfb, int m, int n, int k,
+                        cudaStream_t s);
+
 // ---------------------------------------------------------------- elementwise
 // Expand an input batch into the BF16 GEMM operand [B, selected_planes * 64].
 void expand_input(int layout, const void* input, const void* scalars, int batch, int history,

@@ -220,6 +220,55 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// D[tmem] (+)= (A * 2^SFA)[smem] * (B * 2^SFB)[smem]^T with E4M3 operands, E8M0 scales
+// (one per row per 32-element K chunk) read from tensor memory.
+__device__ __forceinline__ void umma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale.scale_vec::1X [%0], %1, %2, %3, [%4], "
+      "[%5], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      : "memory");
+}
+
+// Copy a 32-row x 128-bit shared-memory matrix into tensor memory, replicated into all
+// four 32-lane quarters (the scale-factor layout of block-scaled MMAs).
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// Descriptor of a contiguous [32 rows][16 bytes] shared-memory matrix without swizzling:
+// 8-row core matrices of 128 bytes, 128 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_sf32x16(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(128u >> 4) << 16;
+  d |= static_cast<uint64_t>(128u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  return d;
+}
+
+// Instruction descriptor, kind::mxf8f6f4 with block scaling: A = B = E4M3 (format 0),
+// K-major, N>>3 at bits 17-22, scale format UE8M0 (bit 23), M>>4 at bits 24-28, the
+// scale-factor byte selectors for B (bits 4-5) and A (bits 29-30).
+__host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n, int sf_id) {
+  return (static_cast<uint32_t>(sf_id) << 4) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (1u << 23) | (static_cast<uint32_t>(m >> 4) << 24) |
+         (static_cast<uint32_t>(sf_id) << 29);
+}
+
+// 1-D bulk copy global -> shared, completing on an mbarrier (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // Arrive (once) on an mbarrier when all previously issued tcgen05 ops of this thread finish.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile(

@@ -219,6 +219,22 @@ int ce4b_moe_forward(const void* x_dev, const void* gate_up_weight_dev,
                      const int32_t* expert_offsets_dev, void* out_dev, void* workspace_dev,
                      int rows, int d_model, int hidden_dim, void* stream);
 
+/* MXFP8 quantisation of a BF16 [rows, cols] matrix (rows, cols multiples of 128):
+ * E4M3 codes [rows, cols] and E8M0 scales [rows/128, cols/128, 32, 16] (one per row and
+ * 32 columns; byte (r%32)*16 + (r/32)*4 + kb of each 128x128 tile). Bit-exact to the
+ * reference's quantiser recipe: scale = E8M0 round-up of max(amax * 0.002232142857, 1e-12),
+ * codes = E4M3 round-to-nearest-even satfinite of x / scale. Replaces quantize_mxfp8
+ * (src/chess_engine_4/kernels/dense.py:46-60). */
+int ce4b_quantize_mxfp8(const void* x_dev, void* codes_dev, void* scales_dev, int rows, int cols,
+                        void* stream);
+
+/* C[M,N] BF16 = sum over 32-element K blocks of (A codes * 2^(sa-127)) (B codes *
+ * 2^(sb-127)), FP32 accumulate: A, B E4M3 codes [M,K], [N,K] with scales in the
+ * ce4b_quantize_mxfp8 layout; M, N, K multiples of 128. Block-scaled tcgen05 MMA
+ * (kind::mxf8f6f4). Replaces mxfp8_gemm (src/chess_engine_4/kernels/dense.py:87-113). */
+int ce4b_mxfp8_gemm(const void* a_codes_dev, const void* a_scales_dev, const void* b_codes_dev,
+                    const void* b_scales_dev, void* c_dev, int m, int n, int k, void* stream);
+
 /* ce4b_dense_block_forward for callers that cannot allocate device memory (an engine
  * thread whose process freezes its allocator after start-up, a plugin that is handed only
  * its input and output buffers, code under a no-allocation budget). Same arguments and
