@@ -1,6 +1,7 @@
 // Memory-bound kernels around the GEMMs: input-plane expansion (three input layouts),
 // standalone RMSNorm / SwiGLU / residual add for the kernel-op API.
 #include "internal.h"
+#include "mxfp8.cuh"
 #include "ptx.cuh"
 
 namespace ce4b {
@@ -131,6 +132,82 @@ __global__ void expand_packed_kernel(const uint8_t* __restrict__ packed, const S
   }
 }
 
+// MXFP8 operand of the input projection straight from any input layout: one thread = one
+// 32-square half of one selected plane of one position (= one MX scale block). The values
+// are formed exactly as in the BF16 path (rule-50 / 99, BF16 rounding), then quantised.
+__global__ void expand_mx_kernel(int layout, const void* __restrict__ input,
+                                 const void* __restrict__ scalars, uint8_t* __restrict__ codes,
+                                 uint8_t* __restrict__ scales, int batch, int history,
+                                 int write_back) {
+  const int sel = selected_planes(history);
+  const int hp = history * kPlanesPerHistory;
+  const int in_dim = sel * 64;
+  const int64_t blocks = static_cast<int64_t>(batch) * sel * 2;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < blocks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int half = static_cast<int>(i % 2);
+    const int p = static_cast<int>((i / 2) % sel);
+    const int64_t b = i / (2 * sel);
+    const int src = source_plane(p, hp);
+    const bool rule50 = p == hp + 5;
+    float f[32];
+    if (layout == CE4B_INPUT_LC0) {
+      const ce4b_input_plane pl = static_cast<const ce4b_input_plane*>(input)[b * kInputPlanes + src];
+      const float v = rule50 ? pl.value / 99.0f : pl.value;
+      const uint32_t bits = static_cast<uint32_t>(pl.mask >> (32 * half));
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] = ((bits >> j) & 1u) ? v : 0.0f;
+    } else if (layout == CE4B_INPUT_F32_PLANES) {
+      float* in = static_cast<float*>(const_cast<void*>(input)) + (b * kInputPlanes + src) * 64 + half * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        f[j] = rule50 ? in[j] / 99.0f : in[j];
+        if (rule50 && write_back) in[j] = f[j];
+      }
+    } else if (layout == CE4B_INPUT_BF16_PLANES) {
+      bf16* in = static_cast<bf16*>(const_cast<void*>(input)) + (b * kInputPlanes + src) * 64 + half * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        f[j] = __bfloat162float(in[j]);
+        if (rule50) {
+          const bf16 q = __float2bfloat16(f[j] / 99.0f);
+          f[j] = __bfloat162float(q);
+          if (write_back) in[j] = q;
+        }
+      }
+    } else {
+      if (src < kHistoryPlanes) {
+        const uint8_t* bytes = static_cast<const uint8_t*>(input) + (b * kHistoryPlanes + src) * 8 + half * 4;
+#pragma unroll
+        for (int jb = 0; jb < 4; ++jb) {
+          const uint32_t byte = bytes[jb];
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) f[jb * 8 + jj] = ((byte >> (7 - jj)) & 1u) ? 1.0f : 0.0f;
+        }
+      } else {
+        float v;
+        if (layout == CE4B_INPUT_PACKED_F32) {
+          v = static_cast<const float*>(scalars)[b * 8 + (src - kHistoryPlanes)];
+          if (rule50) v = v / 99.0f;
+        } else {
+          v = __bfloat162float(static_cast<const bf16*>(scalars)[b * 8 + (src - kHistoryPlanes)]);
+          if (rule50) v = bf16_round(v / 99.0f);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = v;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = bf16_round(f[j]);
+    uint32_t q[8];
+    const uint8_t sc = mx_quantize32(f, q);
+    uint4* dst = reinterpret_cast<uint4*>(codes + b * in_dim + p * 64 + half * 32);
+    dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+    dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+    scales[mx_scale_offset(static_cast<int>(b), p * 2 + half, in_dim / 128)] = sc;
+  }
+}
+
 // One warp per row.
 __global__ void rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
                                bf16* __restrict__ out, int rows, int width, float eps) {
@@ -216,6 +293,20 @@ void expand_input(int layout, const void* input, const void* scalars, int batch,
       fail(CE4B_ERR_INVALID_ARGUMENT, "unknown input layout " + std::to_string(layout));
   }
   check_cuda(cudaGetLastError(), "expand_input launch");
+}
+
+void expand_input_mx(int layout, const void* input, const void* scalars, int batch, int history,
+                     uint8_t* codes, uint8_t* scales, int write_back_rule50, cudaStream_t s) {
+  require(layout >= CE4B_INPUT_F32_PLANES && layout <= CE4B_INPUT_PACKED_BF16,
+          "unknown input layout " + std::to_string(layout));
+  require((layout != CE4B_INPUT_PACKED_F32 && layout != CE4B_INPUT_PACKED_BF16) || scalars != nullptr,
+          "packed input needs scalars");
+  require(selected_planes(history) % 2 == 0, "MXFP8 input needs an even number of planes");
+  const int64_t blocks = static_cast<int64_t>(batch) * selected_planes(history) * 2;
+  const int threads = 256;
+  expand_mx_kernel<<<grid_for(blocks, threads), threads, 0, s>>>(
+      layout, input, scalars, codes, scales, batch, history, write_back_rule50);
+  check_cuda(cudaGetLastError(), "expand_input_mx launch");
 }
 
 void rmsnorm_rows(const bf16* x, const bf16* w, bf16* out, int rows, int width, float eps,

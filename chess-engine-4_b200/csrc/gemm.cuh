@@ -13,6 +13,7 @@
 // No TMA multicast is used anywhere.
 #pragma once
 
+#include "mxfp8.cuh"
 #include "ptx.cuh"
 
 namespace ce4b {
@@ -372,7 +373,7 @@ struct GemmMxSmem {
   static_assert(kBytes <= 232448, "shared memory budget exceeded");
 };
 
-template <int BN, int NSTAGE, int NACC, int NBOX, int G, class Sched, class Epi>
+template <int BN, int NSTAGE, int NACC, int NBOX, int G, bool CLUSTER, class Sched, class Epi>
 __global__ void __launch_bounds__(gemm_threads(G), 1)
     gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO1, const __grid_constant__ CUtensorMap tmO2,
@@ -425,7 +426,11 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
   }
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CLUSTER) {
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
@@ -672,6 +677,24 @@ __device__ __forceinline__ void unstage_bf16x32(uint32_t tile, int r, int col, f
   }
 }
 
+// Write 32 E4M3 codes (columns col..col+31 of row r, col % 32 == 0) into a staging tile
+// of [128 rows][128 codes] boxes with the 128-byte swizzle.
+__device__ __forceinline__ void stage_u8x32(uint32_t tile, int r, int col, const uint32_t (&q)[8]) {
+  const uint32_t box = tile + static_cast<uint32_t>(col / 128) * (kBM * 128);
+  const int chunk0 = (col % 128) / 16;
+  st_shared_v4(box + swz128(r, chunk0), make_uint4(q[0], q[1], q[2], q[3]));
+  st_shared_v4(box + swz128(r, chunk0 + 1), make_uint4(q[4], q[5], q[6], q[7]));
+}
+
+// TMA-store a staged [128 x cols] code tile (cols / 128 boxes) at (x0, y0).
+__device__ __forceinline__ void store_staged_u8(const CUtensorMap* map, uint32_t tile, int cols,
+                                                int x0, int y0) {
+  for (int b = 0; b < cols / 128; ++b) {
+    tma_store_2d(map, tile + static_cast<uint32_t>(b) * (kBM * 128), x0 + 128 * b, y0);
+  }
+  bulk_commit();
+}
+
 // TMA-store a staged [128 x cols] BF16 tile (cols / 64 boxes) at (x0, y0).
 __device__ __forceinline__ void store_staged(const CUtensorMap* map, uint32_t tile, int cols, int x0,
                                              int y0) {
@@ -729,12 +752,18 @@ struct EpiStoreBF16 {
 // columns n_tile*HC + [0, HC). Gate and up are rounded to BF16 first (the reference
 // materialises the gate_up GEMM output in BF16), the product is rounded once more.
 // The hidden tile is TMA-stored through tmO1 (box 64 x 128 over [M, h]).
-template <int HC>
+// With MX, the hidden tile is written as MXFP8 instead: the BF16-rounded values (the
+// reference quantises the BF16 hidden tensor) become E4M3 codes TMA-stored through tmO1
+// (a byte map over [M, h], 128-code boxes) and one E8M0 scale per row and 32 columns,
+// each thread's 32-column group being exactly one scale block.
+template <int HC, bool MX = false>
 struct EpiSwiGLU {
   static_assert(HC % 64 == 0, "64-column boxes");
-  static constexpr int kSmemBytes = kBM * HC * 2;
+  static_assert(!MX || HC == 128, "MXFP8 output needs 128-column chunks");
+  static constexpr int kSmemBytes = MX ? kBM * HC : kBM * HC * 2;
   struct Params {
-    int unused;
+    uint8_t* scales;  // MX: [M/128][h/128][512] scale tiles of the hidden codes
+    int col_tiles;    // MX: h / 128
   };
   __device__ static uint32_t bar_count(const Params&, int) { return 1; }
   __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
@@ -742,7 +771,7 @@ struct EpiSwiGLU {
     return false;
   }
   template <int G>
-  __device__ static void run(const Params&, const TileCoord& tc, const EpiThread& et,
+  __device__ static void run(const Params& p, const TileCoord& tc, const EpiThread& et,
                              const EpiCtx& ctx) {
     if (ctx.iter > 0) {
       if (et.tid == 0) bulk_wait_read_all();  // previous tile's store has read the staging
@@ -755,12 +784,28 @@ struct EpiSwiGLU {
       round_bf16_inplace(u);
 #pragma unroll
       for (int j = 0; j < 32; ++j) g[j] = swiglu_f32(g[j], u[j]);
-      stage_bf16x32(ctx.smem, et.r, c, g);
+      if constexpr (MX) {
+        round_bf16_inplace(g);
+        uint32_t q[8];
+        const uint8_t sc = mx_quantize32(g, q);
+        stage_u8x32(ctx.smem, et.r, c, q);
+        if (et.r < tc.rows) {
+          p.scales[mx_scale_offset(tc.out_row + et.r, (tc.n_tile * HC + c) / 32, p.col_tiles)] = sc;
+        }
+      } else {
+        stage_bf16x32(ctx.smem, et.r, c, g);
+      }
     }
     release_accumulator(ctx);
     fence_proxy_async_smem();
     epi_bar_sync<G>();
-    if (et.tid == 0) store_staged(ctx.tmO1, ctx.smem, HC, tc.n_tile * HC, tc.out_row);
+    if (et.tid == 0) {
+      if constexpr (MX) {
+        store_staged_u8(ctx.tmO1, ctx.smem, HC, tc.n_tile * HC, tc.out_row);
+      } else {
+        store_staged(ctx.tmO1, ctx.smem, HC, tc.n_tile * HC, tc.out_row);
+      }
+    }
   }
 };
 
@@ -774,9 +819,12 @@ struct EpiSwiGLU {
 // then writes n = bf16((x * rsqrt(mean(x^2) + eps)) * norm_w) for its slice through tmO2.
 // Partials are summed in a fixed order, so results are deterministic. Launched with
 // exactly one tile per CTA (the stage ring is reused as the n staging buffer).
-template <int BN>
+// With MX, n is written as MXFP8 (BF16-rounded, then E4M3 codes through tmO2 as a byte
+// map with 128-code boxes, one E8M0 scale per row and 32 columns into n_scales).
+template <int BN, bool MX = false>
 struct EpiResNorm {
   static_assert(BN % 64 == 0, "64-column boxes");
+  static_assert(!MX || BN % 128 == 0, "MXFP8 output needs 128-column slices");
   enum Mode : int { kBias = 0, kResidual = 1 };
   static constexpr int kXBytes = kBM * BN * 2;
   static constexpr int kRecvFloats = kMaxClusterN * kMaxG * kBM;
@@ -788,6 +836,7 @@ struct EpiResNorm {
     int mode;
     int cluster_n;  // CTAs per row = d / BN
     float eps;
+    uint8_t* n_scales;  // MX: [M/128][d/128][512]
   };
   __device__ static int groups(int G) { return G < BN / 32 ? G : BN / 32; }
   __device__ static uint32_t bar_count(const Params& p, int G) {
@@ -877,12 +926,28 @@ struct EpiResNorm {
         load_bf16<32>(p.norm_w + n0 + c, w);
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = (v[j] * inv) * w[j];
-        stage_bf16x32(ctx.ring, et.r, c, v);
+        if constexpr (MX) {
+          round_bf16_inplace(v);
+          uint32_t q[8];
+          const uint8_t sc = mx_quantize32(v, q);
+          stage_u8x32(ctx.ring, et.r, c, q);
+          if (et.r < tc.rows) {
+            p.n_scales[mx_scale_offset(tc.out_row + et.r, (n0 + c) / 32, p.d / 128)] = sc;
+          }
+        } else {
+          stage_bf16x32(ctx.ring, et.r, c, v);
+        }
       }
     }
     fence_proxy_async_smem();
     epi_bar_sync<G>();
-    if (et.tid == 0) store_staged(ctx.tmO2, ctx.ring, BN, n0, tc.out_row);
+    if (et.tid == 0) {
+      if constexpr (MX) {
+        store_staged_u8(ctx.tmO2, ctx.ring, BN, n0, tc.out_row);
+      } else {
+        store_staged(ctx.tmO2, ctx.ring, BN, n0, tc.out_row);
+      }
+    }
   }
 };
 

@@ -127,7 +127,7 @@ void gemm_mx_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUte
           "MXFP8 GEMM extents must be multiples of 128");
   constexpr int BN = 128, NS = 5, NA = 2;
   using Epi = EpiStoreBF16<BN>;
-  auto kernel = gemm_mx_kernel<BN, NS, NA, 1, kG, DenseSched, Epi>;
+  auto kernel = gemm_mx_kernel<BN, NS, NA, 1, kG, false, DenseSched, Epi>;
   constexpr int smem = GemmMxSmem<BN, NS, NA, Epi>::kBytes;
   ensure_smem(kernel, smem);
   DenseSched sched{m, n / BN, (m / kBM) * (n / BN), BN, 0};
@@ -136,6 +136,62 @@ void gemm_mx_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUte
   const int grid = std::min(sched.num_tiles, sm_count());
   launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tC, null_map(), sched, ep, sf,
          k / 128, device_error_word());
+}
+
+void gemm_mx_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH,
+                    const uint8_t* sfa, const uint8_t* sfb, uint8_t* h_scales, int m,
+                    int hidden_dim, int k, cudaStream_t s) {
+  require(hidden_dim % 128 == 0 && k % 128 == 0, "MXFP8 SwiGLU needs multiples of 128");
+  constexpr int BN = 256, NS = 4, NA = 1;
+  using Epi = EpiSwiGLU<128, true>;
+  auto kernel = gemm_mx_kernel<BN, NS, NA, 2, kG, false, DenseSched, Epi>;
+  constexpr int smem = GemmMxSmem<BN, NS, NA, Epi>::kBytes;
+  ensure_smem(kernel, smem);
+  DenseSched sched{m, hidden_dim / 128, ceil_div(m, kBM) * (hidden_dim / 128), 128, hidden_dim};
+  typename Epi::Params ep{h_scales, hidden_dim / 128};
+  const MxScales sf{sfa, sfb, k / 128};
+  const int grid = std::min(sched.num_tiles, sm_count());
+  launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tH, null_map(), sched, ep, sf,
+         k / 128, device_error_word());
+}
+
+void gemm_mx_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
+                     const CUtensorMap& tN, const uint8_t* sfa, const uint8_t* sfb,
+                     uint8_t* n_scales, const bf16* bias, const bf16* norm_w, int m, int d, int k,
+                     float eps, cudaStream_t s) {
+  require(d % 128 == 0 && d / 128 <= kMaxClusterN && k % 128 == 0,
+          "MXFP8 residual GEMM needs d a multiple of 128 up to 1024 and K a multiple of 128");
+  constexpr int BN = 128, NS = 5, NA = 1;
+  using Epi = EpiResNorm<BN, true>;
+  auto kernel = gemm_mx_kernel<BN, NS, NA, 1, kG, true, DenseSched, Epi>;
+  constexpr int smem = GemmMxSmem<BN, NS, NA, Epi>::kBytes;
+  ensure_smem(kernel, smem);
+  const int cn = d / BN;
+  DenseSched sched{m, cn, ceil_div(m, kBM) * cn, BN, 0};
+  typename Epi::Params ep{bias,     norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
+                          cn,       eps,    n_scales};
+  const MxScales sf{sfa, sfb, k / 128};
+  launch(kernel, dim3(sched.num_tiles), gemm_threads(kG), smem, cn, s, tA, tB, tX, tN, sched, ep,
+         sf, k / 128, device_error_word());
+}
+
+void gemm_mx_heads(const CUtensorMap& tA, const CUtensorMap& tB, const uint8_t* sfa,
+                   const uint8_t* sfb, const bf16* bias, float* policy, float* wdl,
+                   float* moves_left, int m, int d, int policy_size, int policy_storage,
+                   int wdl_probs, cudaStream_t s) {
+  constexpr int BN = 256, NS = 3, NA = 1;
+  using Epi = EpiHeads;
+  auto kernel = gemm_mx_kernel<BN, NS, NA, 1, kG, false, DenseSched, Epi>;
+  constexpr int smem = GemmMxSmem<BN, NS, NA, Epi>::kBytes;
+  ensure_smem(kernel, smem);
+  const int n_total = policy_storage + 64;
+  DenseSched sched{m, ceil_div(n_total, BN), ceil_div(m, kBM) * ceil_div(n_total, BN), BN, 0};
+  typename Epi::Params ep{bias, policy, wdl, moves_left, policy_size, policy_storage, n_total,
+                          wdl_probs};
+  const MxScales sf{sfa, sfb, d / 128};
+  const int grid = std::min(sched.num_tiles, sm_count());
+  launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, null_map(), null_map(), sched,
+         ep, sf, d / 128, device_error_word());
 }
 
 // ------------------------------------------------------------------ plain store

@@ -111,6 +111,22 @@ CUtensorMap make_tmap_u8(const void* ptr, uint64_t rows, uint64_t cols, uint64_t
 void gemm_mx_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC,
                         const uint8_t* sfa, const uint8_t* sfb, int m, int n, int k,
                         cudaStream_t s);
+// MXFP8 forms of the forward's GEMMs (code maps from make_tmap_u8 with 128-row boxes; the
+// x map of the residual GEMM stays BF16). sfa/sfb are the A/B scale tiles.
+void gemm_mx_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH,
+                    const uint8_t* sfa, const uint8_t* sfb, uint8_t* h_scales, int m,
+                    int hidden_dim, int k, cudaStream_t s);
+void gemm_mx_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
+                     const CUtensorMap& tN, const uint8_t* sfa, const uint8_t* sfb,
+                     uint8_t* n_scales, const bf16* bias, const bf16* norm_w, int m, int d, int k,
+                     float eps, cudaStream_t s);
+void gemm_mx_heads(const CUtensorMap& tA, const CUtensorMap& tB, const uint8_t* sfa,
+                   const uint8_t* sfb, const bf16* bias, float* policy, float* wdl,
+                   float* moves_left, int m, int d, int policy_size, int policy_storage,
+                   int wdl_probs, cudaStream_t s);
+// Input planes -> MXFP8 codes [B, 64*sel] + scales (sel*64 a multiple of 128).
+void expand_input_mx(int layout, const void* input, const void* scalars, int batch, int history,
+                     uint8_t* codes, uint8_t* scales, int write_back_rule50, cudaStream_t s);
 
 // ---------------------------------------------------------------- elementwise
 // Expand an input batch into the BF16 GEMM operand [B, selected_planes * 64].

@@ -44,6 +44,7 @@ Model::~Model() {
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   if (stream) cudaStreamDestroy(stream);
   if (arena) cudaFree(arena);
+  if (mx_arena) cudaFree(mx_arena);
   if (workspace) cudaFree(workspace);
 }
 
@@ -106,6 +107,15 @@ void Model::plan_workspace() {
   ws_off.policy = take(r * policy_size * 4);
   ws_off.wdl = take(r * 3 * 4);
   ws_off.moves_left = take(r * 4);
+  if (mx) {
+    const size_t t = r / 128;
+    ws_off.a_codes = take(r * in_dim);
+    ws_off.a_scales = take(t * (in_dim / 128) * 512);
+    ws_off.n_codes = take(r * d);
+    ws_off.n_scales = take(t * (d / 128) * 512);
+    ws_off.h_codes = take(r * dense_hidden);
+    ws_off.h_scales = take(t * (dense_hidden / 128) * 512);
+  }
   if (cfg.arch == CE4B_ARCH_MOE64A2) {
     // Expert rows: 2 routes per token, each expert segment padded to 128 rows.
     perm_rows = static_cast<int>((2 * r + 64 * 127 + 127) / 128 * 128);
@@ -146,11 +156,12 @@ void Model::create(const ce4b_model_config& c, int dev, int maxb) {
           "policy storage must hold the policy output");
   require(c.policy_storage_size % 32 == 0, "policy storage size must be a multiple of 32");
   require(maxb >= 1 && maxb <= (1 << 20), "max_batch must be in [1, 2^20]");
-  if (c.precision != CE4B_PRECISION_BF16) {
-    fail(CE4B_ERR_UNSUPPORTED, "only BF16 precision is available in this build");
-  }
+  require(c.precision == CE4B_PRECISION_BF16 || c.precision == CE4B_PRECISION_MXFP8,
+          "unknown precision");
+  mx = c.precision == CE4B_PRECISION_MXFP8;
   if (c.arch == CE4B_ARCH_MOE64A2) {
     require(c.depth % 2 == 0, "moe64a2 depth must be a positive even number");
+    if (mx) fail(CE4B_ERR_UNSUPPORTED, "moe64a2 runs in BF16 (the reference's MoE kernels are BF16)");
   }
   const int hid = static_cast<int>(static_cast<double>(c.d_model) * c.expansion_ratio);
   dense_hidden = c.arch == CE4B_ARCH_DENSE ? hid : 4 * c.d_model;
@@ -159,6 +170,12 @@ void Model::create(const ce4b_model_config& c, int dev, int maxb) {
   require(expert_hidden % 64 == 0, "expert hidden dimension must be a multiple of 64");
   sel = selected_planes(c.history_length);
   in_dim = sel * 64;
+  if (mx) {
+    require(c.d_model % 128 == 0 && c.d_model <= 1024,
+            "MXFP8 needs d_model a multiple of 128, at most 1024");
+    require(dense_hidden % 128 == 0, "MXFP8 needs a hidden width that is a multiple of 128");
+    require(in_dim % 128 == 0, "MXFP8 needs an even history_length (input width multiple of 128)");
+  }
   policy_size = c.policy_size;
   policy_storage = c.policy_storage_size;
   max_batch = maxb;
@@ -235,9 +252,96 @@ void Model::finalize() {
     tm_hperm = make_tmap_bf16(workspace + ws_off.hperm, perm_rows, expert_hidden, expert_hidden, 128);
     tm_yperm = make_tmap_bf16(workspace + ws_off.yperm, perm_rows, d, d, 128);
   }
+  if (mx) quantize_weights();
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   graphs.clear();
   finalized = true;
+}
+
+// MXFP8 weights: every linear's BF16 weight is quantised once (the reference re-quantises
+// its weights on every call, src/chess_engine_4/kernels/dense.py:395-406; the codes are
+// the same). The head matrix [policy_storage + 64, d] is padded with zero rows to a
+// multiple of 128.
+void Model::quantize_weights() {
+  const int d = cfg.d_model;
+  const int h = dense_hidden;
+  heads_rows_mx = (policy_storage + 64 + 127) / 128 * 128;
+  auto mx_size = [](size_t rows, size_t cols) {
+    return align256(rows * cols) + align256((rows / 128) * (cols / 128) * 512);
+  };
+  size_t total = mx_size(d, in_dim) + mx_size(heads_rows_mx, d);
+  for (int l = 0; l < cfg.depth; ++l) total += mx_size(2 * h, d) + mx_size(d, h);
+  if (mx_arena == nullptr) {
+    mx_arena_bytes = total;
+    check_cuda(cudaMalloc(&mx_arena, mx_arena_bytes), "cudaMalloc MXFP8 weights");
+  }
+  bf16* padded = nullptr;
+  check_cuda(cudaMalloc(&padded, static_cast<size_t>(heads_rows_mx) * d * 2), "cudaMalloc heads");
+  size_t cur = 0;
+  auto quant = [&](const bf16* src, int rows, int cols, const uint8_t** scales_out) {
+    uint8_t* codes = mx_arena + cur;
+    cur += align256(static_cast<size_t>(rows) * cols);
+    uint8_t* scales = mx_arena + cur;
+    cur += align256(static_cast<size_t>(rows / 128) * (cols / 128) * 512);
+    mx_quantize(src, codes, scales, rows, cols, stream);
+    *scales_out = scales;
+    return codes;
+  };
+  const uint8_t* w_in_codes = quant(w("input.weight"), d, in_dim, &w_in_scales);
+  tm_w_in = make_tmap_u8(w_in_codes, d, in_dim, in_dim, 128);
+  check_cuda(cudaMemsetAsync(padded, 0, static_cast<size_t>(heads_rows_mx) * d * 2, stream), "zero");
+  check_cuda(cudaMemcpyAsync(padded, w("policy.weight"),
+                             static_cast<size_t>(policy_storage + 64) * d * 2,
+                             cudaMemcpyDeviceToDevice, stream),
+             "copy heads");
+  const uint8_t* heads_codes = quant(padded, heads_rows_mx, d, &heads_scales);
+  tm_heads = make_tmap_u8(heads_codes, heads_rows_mx, d, d, 256);
+  for (int l = 0; l < cfg.depth; ++l) {
+    const std::string p = "blocks." + std::to_string(l);
+    Layer& L = layers[l];
+    const uint8_t* gu = quant(w(p + ".gate_up.weight"), 2 * h, d, &L.gu_scales);
+    const uint8_t* dn = quant(w(p + ".down.weight"), d, h, &L.down_scales);
+    L.tm_gate_up = make_tmap_u8(gu, 2 * h, d, d, 128);
+    L.tm_down = make_tmap_u8(dn, d, h, h, 128);
+  }
+  check_cuda(cudaStreamSynchronize(stream), "quantise weights");
+  cudaFree(padded);
+  tm_a_u8 = make_tmap_u8(workspace + ws_off.a_codes, rows_cap, in_dim, in_dim, 128);
+  tm_n_u8 = make_tmap_u8(workspace + ws_off.n_codes, rows_cap, d, d, 128);
+  tm_h_u8 = make_tmap_u8(workspace + ws_off.h_codes, rows_cap, h, h, 128);
+}
+
+// MXFP8 forward: the same schedule as the BF16 one on block-scaled GEMMs; each producing
+// epilogue quantises its output (n, hidden) for the next GEMM, x stays BF16.
+void Model::forward_mx(int layout, void* input, const void* scalars, int batch, float* policy,
+                       float* wdl, float* moves_left, int wdl_probs, int write_back,
+                       cudaStream_t s) {
+  const int d = cfg.d_model;
+  const int h = dense_hidden;
+  const float eps = cfg.rms_norm_eps;
+  auto* a_codes = workspace + ws_off.a_codes;
+  auto* a_scales = workspace + ws_off.a_scales;
+  auto* n_scales = workspace + ws_off.n_scales;
+  auto* h_scales = workspace + ws_off.h_scales;
+  expand_input_mx(layout, input, scalars, batch, cfg.history_length, a_codes, a_scales, write_back,
+                  s);
+  trace("expand_planes_mxfp8", s);
+  const bf16* first_norm = cfg.depth > 0 ? layers[0].norm : w("final_norm.weight");
+  gemm_mx_resnorm(tm_a_u8, tm_w_in, tm_x, tm_n_u8, a_scales, w_in_scales, n_scales,
+                  w("input.bias"), first_norm, batch, d, in_dim, eps, s);
+  trace("input_gemm_bias_rmsnorm", s);
+  for (int l = 0; l < cfg.depth; ++l) {
+    const Layer& L = layers[l];
+    const bf16* next_norm = l + 1 < cfg.depth ? layers[l + 1].norm : w("final_norm.weight");
+    gemm_mx_swiglu(tm_n_u8, L.tm_gate_up, tm_h_u8, n_scales, L.gu_scales, h_scales, batch, h, d, s);
+    trace("gate_up_swiglu", s);
+    gemm_mx_resnorm(tm_h_u8, L.tm_down, tm_x, tm_n_u8, h_scales, L.down_scales, n_scales, nullptr,
+                    next_norm, batch, d, h, eps, s);
+    trace("down_residual_rmsnorm", s);
+  }
+  gemm_mx_heads(tm_n_u8, tm_heads, n_scales, heads_scales, w("policy.bias"), policy, wdl,
+                moves_left, batch, d, policy_size, policy_storage, wdl_probs, s);
+  trace("heads", s);
 }
 
 void Model::forward(int layout, void* input, const void* scalars, int batch, float* policy,
@@ -256,6 +360,10 @@ void Model::forward(int layout, void* input, const void* scalars, int batch, flo
 
   trace_next = 0;
   trace_labels.clear();
+  if (mx) {
+    forward_mx(layout, input, scalars, batch, policy, wdl, moves_left, wdl_probs, write_back, s);
+    return;
+  }
   expand_input(layout, input, scalars, batch, cfg.history_length, a_in, write_back, s);
   trace("expand_planes", s);
   const bf16* first_norm = cfg.depth > 0 ? layers[0].norm : w("final_norm.weight");

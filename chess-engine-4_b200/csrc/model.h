@@ -25,12 +25,15 @@ struct Model {
     CUtensorMap tm_down{};     // dense down, or stacked expert down [64*d, h_e]
     CUtensorMap tm_router{};   // MoE router [64, d]
     const float* beta = nullptr;  // MoE router_qb_beta [64]
+    const uint8_t* gu_scales = nullptr;    // MXFP8 weight scales
+    const uint8_t* down_scales = nullptr;
   };
   struct WorkspaceOffsets {
     size_t planes = 0, a_in = 0, x = 0, n = 0, hidden = 0, policy = 0, wdl = 0, moves_left = 0;
     size_t route_expert = 0, route_prob = 0, route_pos = 0, block_hist = 0, block_off = 0;
     size_t expert_start = 0, m_tiles = 0, num_m_tiles = 0, xperm = 0, pprob = 0, hperm = 0;
     size_t yperm = 0;
+    size_t a_codes = 0, a_scales = 0, n_codes = 0, n_scales = 0, h_codes = 0, h_scales = 0;
   };
 
   ce4b_model_config cfg{};
@@ -49,11 +52,18 @@ struct Model {
   size_t arena_bytes = 0;
   std::map<std::string, Slot> slots;
   uint8_t* workspace = nullptr;
+  bool mx = false;                // precision MXFP8
+  uint8_t* mx_arena = nullptr;    // quantised weights (codes + scales)
+  size_t mx_arena_bytes = 0;
+  const uint8_t* w_in_scales = nullptr;
+  const uint8_t* heads_scales = nullptr;
+  int heads_rows_mx = 0;          // head rows padded to a multiple of 128
   size_t workspace_bytes = 0;
   WorkspaceOffsets ws_off;
 
   CUtensorMap tm_a_in{}, tm_x{}, tm_n{}, tm_hidden{}, tm_w_in{}, tm_heads{};
   CUtensorMap tm_xperm{}, tm_hperm{}, tm_yperm{};
+  CUtensorMap tm_a_u8{}, tm_n_u8{}, tm_h_u8{};  // MXFP8 activation codes
   std::vector<Layer> layers;
   bool finalized = false;
   cudaStream_t stream = nullptr;
@@ -81,6 +91,9 @@ struct Model {
   void enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
                         float* host_wdl, float* host_moves_left, cudaStream_t s);
   void trace(const char* label, cudaStream_t s);
+  void quantize_weights();
+  void forward_mx(int layout, void* input, const void* scalars, int batch, float* policy,
+                  float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s);
   void moe_layer(const Layer& L, int moe_index, const bf16* next_norm, int batch,
                  int32_t* tokens_per_expert, cudaStream_t s);
 

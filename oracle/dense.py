@@ -45,6 +45,19 @@ def select_and_normalize(planes: torch.Tensor, history_length: int) -> torch.Ten
     return x.flatten(start_dim=1)
 
 
+def mx_dequant(t: torch.Tensor) -> torch.Tensor:
+    """MXFP8 round trip of a BF16-valued matrix (quantise with the C restatement of the
+    reference's recipe, oracle/mxfp8.c, then dequantise); rows are padded to 128."""
+
+    from . import mxfp8
+
+    rows, cols = t.shape
+    pad = (-rows) % 128
+    tb = torch.cat([t, t.new_zeros(pad, cols)]) if pad else t
+    codes, scales = mxfp8.quantize(tb.to(torch.bfloat16))
+    return mxfp8.dequantize(codes, scales)[:rows]
+
+
 def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     inv = torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + eps)
     return x * inv * w
@@ -65,12 +78,15 @@ def forward(
 
     ``moe_layers`` / ``moe_forward`` let oracle.moe reuse this tower for moe64a2."""
 
-    if mode not in ("fp32", "bf16"):
+    if mode not in ("fp32", "bf16", "mxfp8"):
         raise ValueError(mode)
-    rnd = _bf16 if mode == "bf16" else (lambda t: t)
+    rnd = _bf16 if mode in ("bf16", "mxfp8") else (lambda t: t)
+    # MXFP8 (all linears, recipe of the reference's custom path): both GEMM operands are
+    # MXFP8 round trips of their BF16 values; everything else is the BF16 forward.
+    q = mx_dequant if mode == "mxfp8" else (lambda t: t)
     f = {k: v.to(torch.float32) for k, v in weights.items()}
     a = rnd(select_and_normalize(planes, history_length))
-    x = rnd(a @ f["input.weight"].T + f["input.bias"])
+    x = rnd(q(a) @ q(f["input.weight"]).T + f["input.bias"])
     for layer in range(depth):
         p = f"blocks.{layer}"
         if layer in moe_layers:
@@ -78,15 +94,18 @@ def forward(
             x = moe_forward(x, layer, mode)
             continue
         n = rnd(_rmsnorm(x, f[f"{p}.norm.weight"], eps))
-        gu = n @ f[f"{p}.gate_up.weight"].T
+        gu = q(n) @ q(f[f"{p}.gate_up.weight"]).T
         h = gu.shape[1] // 2
         g, u = rnd(gu[:, :h]), rnd(gu[:, h:])
         hidden = rnd(g / (1.0 + torch.exp(-g)) * u)
-        x = rnd(x + rnd(hidden @ f[f"{p}.down.weight"].T))
-    n = rnd(_rmsnorm(x, f["final_norm.weight"], eps))
-    policy = rnd(n @ f["policy.weight"][:POLICY_SIZE].T + f["policy.bias"][:POLICY_SIZE])
-    wdl = rnd(n @ f["wdl.weight"][:3].T + f["wdl.bias"][:3])
-    moves_left = rnd(n @ f["moves_left.weight"][:1].T + f["moves_left.bias"][:1])[:, 0]
+        x = rnd(x + rnd(q(hidden) @ q(f[f"{p}.down.weight"]).T))
+    n = q(rnd(_rmsnorm(x, f["final_norm.weight"], eps)))
+    heads = torch.cat([f["policy.weight"], f["wdl.weight"], f["moves_left.weight"]])
+    logits = n @ q(heads).T
+    ps = f["policy.weight"].shape[0]
+    policy = rnd(logits[:, :POLICY_SIZE] + f["policy.bias"][:POLICY_SIZE])
+    wdl = rnd(logits[:, ps : ps + 3] + f["wdl.bias"][:3])
+    moves_left = rnd(logits[:, ps + 32 : ps + 33] + f["moves_left.bias"][:1])[:, 0]
     return policy, wdl, moves_left
 
 

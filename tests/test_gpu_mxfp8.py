@@ -50,3 +50,34 @@ def test_mxfp8_gemm_matches_dequantised_product(m: int, n: int, k: int) -> None:
     ref = (da @ db.T).float()
     # Exact operands; only the FP32 accumulation order and the final BF16 rounding differ.
     torch.testing.assert_close(c.float().cpu(), ref, atol=1e-3 * float(ref.abs().max()), rtol=8e-3)
+
+
+@pytest.mark.parametrize("d,depth,ratio,batch", [(256, 2, 3.0, 256), (512, 12, 3.0, 1024)])
+def test_mxfp8_model_matches_oracle(d: int, depth: int, ratio: float, batch: int) -> None:
+    from ce4b200 import DenseChessNet, DenseChessNetConfig, synthetic
+    from helpers import POLICY_ATOL, WDL_PROB_ATOL, argmax_agreement
+    from oracle import dense as oracle
+
+    weights = synthetic.make_dense_weights(d_model=d, depth=depth, hidden_dim=int(d * ratio), seed=3)
+    planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(batch, 4))
+    model = DenseChessNet(
+        DenseChessNetConfig(d_model=d, depth=depth, expansion_ratio=ratio, precision="mxfp8")
+    )
+    synthetic.load_into(model, weights)
+    model = model.cuda()
+    out = model(planes.clone().cuda())
+    torch.cuda.synchronize()
+    policy, wdl, ml = oracle.forward(weights, planes, depth=depth, mode="mxfp8")
+    policy_bf16 = oracle.forward(weights, planes, depth=depth, mode="bf16")[0]
+    # E4M3 keeps 3 mantissa bits: a one-ulp BF16 difference upstream (FP32 accumulation
+    # order) can flip a code or move a block's E8M0 scale, so a few positions differ by
+    # more than the BF16 bounds while most are bit-identical (d512 x 12: > 90 % identical,
+    # 98 % within 2e-2, max 0.08). The bound that matters: no position strays further
+    # from the reference MXFP8 path than MXFP8 itself sits from BF16 (p99 0.13 there).
+    err = (out.policy_logits.cpu() - policy).abs().max(dim=1).values
+    fmt = (policy - policy_bf16).abs().max(dim=1).values
+    assert float((err <= POLICY_ATOL).float().mean()) >= 0.97, float(err.max())
+    assert float(err.max()) <= float(fmt.quantile(0.99)) + POLICY_ATOL
+    assert argmax_agreement(out.policy_logits, policy) >= 0.995
+    wdl_err = (torch.softmax(out.wdl_logits.cpu(), -1) - torch.softmax(wdl, -1)).abs().max(dim=1).values
+    assert float((wdl_err <= WDL_PROB_ATOL).float().mean()) >= 0.97
