@@ -1,22 +1,24 @@
-"""Benchmark of the chess-engine-4 forward on B200: positions/s at d512 x 12, batch 4096.
+"""Benchmark of the chess-engine-4 forward on B200 (positions/s).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1]
 
-One step = one forward of one batch of synthetic positions (lc0 InputPlane records,
-seeded Bernoulli(0.08) planes) through the dense d512 x 12 SwiGLU tower (hidden 1536,
-BF16, weights N(0, 0.02)). Each rank of a multi-GPU run is an independent replica
-processing its own batch (weak scaling, no collective on the data path). Rank 0 prints
-one JSON line.
+Default workload: the dense d512 x 12 SwiGLU tower (hidden 1536,
+BF16, weights N(0, 0.02)) on a batch of 4096 synthetic positions per GPU (lc0
+InputPlane records, seeded Bernoulli(0.08) planes). Other configurations of BASELINE.json
+are selectable with --config (c0 d128x6, c2 MXFP8 d512 batch 16384, c3 moe64a2 d768 batch
+8192 per GPU, c4 / c4-mxfp8 d1024x16 batch 65536 split over the GPUs). One step = one forward of one batch. Each rank of a
+multi-GPU run is an independent replica on its own batch (weak scaling, no collective on
+the data path). Rank 0 prints one JSON line.
 
 * ``value``: device-timed throughput (CUDA events per step, L2 flushed between steps,
   inputs resident in HBM), all ranks' positions / the slowest rank's time.
 * ``e2e``: the same metric through the engine-facing C ABI call
   (``ce4b_model_evaluate_async``) with pinned host buffers: H2D of the planes, the
   forward (CUDA graph) and D2H of policy / WDL / moves-left inside every timed step.
-* ``roofline``: the dominant kernel (gate_up GEMM with the fused SwiGLU epilogue), timed
-  live with CUDA events recorded by the library around it during the timed steps.
+* ``roofline``: the dominant kernel (the gate_up GEMM with the fused SwiGLU epilogue),
+  timed live with CUDA events the library records around each kernel of the timed steps.
 * ``cpu_baseline``: the CPU restatement of the reference's portable PyTorch forward
-  (oracle/dense.py, mode fp32 = PortableChessNet) on the host cores, bounded sample.
+  (oracle/, FP32) on the host cores, on a bounded sample of the same workload.
 * ``--impl reference``: rank 0 times that CPU implementation as the reference arm.
 """
 
@@ -31,34 +33,91 @@ import subprocess
 import sys
 import tempfile
 import time
+from dataclasses import dataclass
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "chess-engine-4_b200"))
 sys.path.insert(0, str(REPO))
 
-import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-D_MODEL, DEPTH, RATIO, BATCH = 512, 12, 3.0, 4096
-HIDDEN = int(D_MODEL * RATIO)
 IN_DIM = 112 * 64
 POLICY = 1858
-# Algorithmic GEMM FLOPs per position: input projection, 3 projections per layer, heads
-# (policy 1858 + wdl 3 + moves-left 1).
-FLOP_PER_POS = 2 * (IN_DIM * D_MODEL + DEPTH * 3 * D_MODEL * HIDDEN + 1862 * D_MODEL)
-GATE_UP_FLOP_PER_POS = 2 * 2 * HIDDEN * D_MODEL
-METRIC = "positions/sec (dense d512x12 forward, batch 4096 per GPU)"
-WORKLOAD = "dense-d512-L12-h1536-bf16-b4096"
+
+
+@dataclass(frozen=True)
+class Config:
+    name: str
+    arch: str  # "dense" | "moe64a2"
+    d: int
+    depth: int
+    ratio: float  # dense hidden / d, or expert hidden / d for moe64a2
+    batch: int  # positions per step: per GPU (weak) or split over the GPUs (strong)
+    precision: str  # "bf16" | "mxfp8"
+    cpu_sample: int  # positions per CPU-baseline sample
+    strong: bool = False  # BASELINE.json splits this config's batch data-parallel
+
+    def per_gpu(self, world: int) -> int:
+        if not self.strong:
+            return self.batch
+        if self.batch % world:
+            raise ValueError(f"batch {self.batch} does not split over {world} GPUs")
+        return self.batch // world
+
+    @property
+    def hidden(self) -> int:
+        return int(self.d * self.ratio)
+
+    @property
+    def dense_hidden(self) -> int:
+        return self.hidden if self.arch == "dense" else 4 * self.d
+
+    def flop_per_pos(self) -> float:
+        """Algorithmic GEMM FLOPs per position."""
+
+        d = self.d
+        f = 2 * (IN_DIM * d + 1862 * d)
+        if self.arch == "dense":
+            return f + self.depth * 2 * 3 * d * self.hidden
+        half = self.depth // 2
+        return f + half * 2 * 3 * d * self.dense_hidden + half * (2 * 64 * d + 2 * (3 * d * self.hidden * 2))
+
+    def gate_up_flop(self, batch: int) -> float:
+        """FLOPs of one launch of the dominant kernel (gate_up + SwiGLU)."""
+
+        if self.arch == "dense":
+            return 2.0 * batch * 2 * self.hidden * self.d
+        return 2.0 * (2 * batch) * 2 * self.hidden * self.d  # two routes per token
+
+    @property
+    def workload(self) -> str:
+        return f"{self.arch}-d{self.d}-L{self.depth}-h{self.hidden}-{self.precision}-b{self.batch}"
+
+    @property
+    def metric(self) -> str:
+        per = "split over the GPUs" if self.strong else "per GPU"
+        return f"positions/sec ({self.arch} d{self.d}x{self.depth} {self.precision} forward, batch {self.batch} {per})"
+
+
+CONFIGS = {
+    "c0": Config("c0", "dense", 128, 6, 3.0, 256, "bf16", 256),
+    "c1": Config("c1", "dense", 512, 12, 3.0, 4096, "bf16", 512),
+    "c2": Config("c2", "dense", 512, 12, 3.0, 16384, "mxfp8", 512, strong=True),
+    "c3": Config("c3", "moe64a2", 768, 12, 1.0, 8192, "bf16", 128),
+    "c4": Config("c4", "dense", 1024, 16, 3.0, 65536, "bf16", 256, strong=True),
+    "c4-mxfp8": Config("c4-mxfp8", "dense", 1024, 16, 3.0, 65536, "mxfp8", 256, strong=True),
+}
 
 
 def parse_args() -> argparse.Namespace:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=1000)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=300)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--batch", type=int, default=BATCH)
+    p.add_argument("--config", choices=sorted(CONFIGS), default="c1")
+    p.add_argument("--batch", type=int, default=0, help="override the per-GPU batch")
     p.add_argument("--quick", action="store_true", help="skip e2e, latency, clocks and CPU baseline (profiling)")
     return p.parse_args()
 
@@ -77,7 +136,7 @@ def peaks() -> dict:
 
 
 # ---------------------------------------------------------------- distributed plumbing
-def dist_setup(n_gpus: int):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -173,67 +232,79 @@ class ClockSampler:
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {
-            "sm_mhz": statistics.median(sm),
-            "sm_max_mhz": max(mx),
-            "reasons": sorted(reasons),
-            "samples": len(sm),
-        }
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
 
 
-# ---------------------------------------------------------------- CPU implementation
-def cpu_forward_rate(batch: int, sample: int, repeats: int, seed: int = 0) -> dict:
-    """Times the FP32 CPU restatement of PortableChessNet on a bounded sample."""
+# ---------------------------------------------------------------- weights and CPU implementation
+def make_weights(cfg: Config, device: str) -> dict[str, torch.Tensor]:
+    from ce4b200 import synthetic
+
+    if cfg.arch == "dense":
+        return synthetic.make_dense_weights(d_model=cfg.d, depth=cfg.depth, hidden_dim=cfg.hidden, seed=0,
+                                            norm_std=0.0, device=device)
+    return synthetic.make_moe_weights(d_model=cfg.d, depth=cfg.depth, expert_hidden=cfg.hidden, seed=0,
+                                      norm_std=0.0, device=device)
+
+
+def cpu_forward(cfg: Config, weights: dict[str, torch.Tensor], planes: torch.Tensor) -> None:
+    from oracle import dense as oracle_dense
+    from oracle import moe as oracle_moe
+
+    if cfg.arch == "dense":
+        oracle_dense.forward(weights, planes, depth=cfg.depth, mode="fp32")
+    else:
+        oracle_moe.forward(weights, planes, depth=cfg.depth, mode="fp32")
+
+
+def cpu_rate(cfg: Config, sample: int, repeats: int) -> tuple[float, int]:
+    """Positions/s of the FP32 CPU restatement on a bounded sample (median of repeats)."""
 
     from ce4b200 import synthetic
-    from oracle import dense as oracle
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    weights = synthetic.make_dense_weights(d_model=D_MODEL, depth=DEPTH, hidden_dim=HIDDEN, seed=seed)
+    weights = make_weights(cfg, "cpu")
     planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(sample, 1))
+    times = []
     with torch.no_grad():
-        oracle.forward(weights, planes[: min(64, sample)], depth=DEPTH, mode="fp32")
-        times = []
+        cpu_forward(cfg, weights, planes[: min(16, sample)])
         for _ in range(repeats):
             t0 = time.perf_counter()
-            oracle.forward(weights, planes, depth=DEPTH, mode="fp32")
+            cpu_forward(cfg, weights, planes)
             times.append(time.perf_counter() - t0)
-    med = statistics.median(times)
-    return {
-        "value": sample / med,
-        "unit": "positions/s",
-        "cores": threads,
-        "kind": "port",
-        "sample": f"{sample} of the {batch} positions of one step, fp32 PortableChessNet restatement "
-        f"(oracle/dense.py), median of {repeats} runs",
-    }
+    return sample / statistics.median(times), threads
 
 
-def run_reference(args: argparse.Namespace) -> None:
-    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+def cpu_description(cfg: Config, sample: int) -> str:
+    kind = "PortableChessNet" if cfg.arch == "dense" else "MoeBlock eval path"
+    return (f"{sample} of the {cfg.batch} positions of one step; FP32 restatement of the reference's "
+            f"{kind} (oracle/); the reference source does not travel to the GPU box")
+
+
+def run_reference(args: argparse.Namespace, cfg: Config) -> None:
+    rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from ce4b200 import synthetic
-    from oracle import dense as oracle
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    sample = min(args.batch, 512)
-    weights = synthetic.make_dense_weights(d_model=D_MODEL, depth=DEPTH, hidden_dim=HIDDEN, seed=0)
+    sample = cfg.cpu_sample
+    weights = make_weights(cfg, "cpu")
     planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(sample, 1))
     steps, warmup = max(1, min(args.steps, 20)), max(1, min(args.warmup, 3))
     with torch.no_grad():
         for _ in range(warmup):
-            oracle.forward(weights, planes, depth=DEPTH, mode="fp32")
+            cpu_forward(cfg, weights, planes)
         t0 = time.perf_counter()
         for _ in range(steps):
-            oracle.forward(weights, planes, depth=DEPTH, mode="fp32")
+            cpu_forward(cfg, weights, planes)
         elapsed = time.perf_counter() - t0
     value = sample * steps / elapsed
     line = {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": cfg.metric,
         "value": value,
         "unit": "positions/s",
         "n_gpus": args.gpus,
@@ -245,36 +316,28 @@ def run_reference(args: argparse.Namespace) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample_positions_per_step": sample, "l2": "n/a (CPU)"},
-        "cpu_baseline": {
-            "value": value,
-            "unit": "positions/s",
-            "cores": threads,
-            "kind": "port",
-            "sample": f"{sample} positions per step (of {args.batch}); fp32 restatement of "
-            "PortableChessNet (oracle/dense.py); the reference itself does not travel to the box",
-        },
+        "config": {"workload": cfg.workload, "sample_positions_per_step": sample, "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": value, "unit": "positions/s", "cores": threads, "kind": "port",
+                         "sample": cpu_description(cfg, sample)},
         "e2e": {"value": value, "unit": "positions/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------- GPU implementation
-def make_model(device: int, batch: int):
-    from ce4b200 import _lib, synthetic
+def make_model(cfg: Config, device: int, batch: int):
+    from ce4b200 import _lib
 
     lib = _lib.library()
-    cfg = _lib.ModelConfigStruct(
-        arch=_lib.ARCH_DENSE, d_model=D_MODEL, depth=DEPTH, history_length=8,
-        expansion_ratio=RATIO, rms_norm_eps=1e-6, policy_size=POLICY, policy_storage_size=1888,
-        precision=_lib.PRECISION_BF16,
+    c = _lib.ModelConfigStruct(
+        arch=_lib.ARCH_DENSE if cfg.arch == "dense" else _lib.ARCH_MOE64A2, d_model=cfg.d,
+        depth=cfg.depth, history_length=8, expansion_ratio=cfg.ratio, rms_norm_eps=1e-6,
+        policy_size=POLICY, policy_storage_size=1888,
+        precision=_lib.PRECISION_BF16 if cfg.precision == "bf16" else _lib.PRECISION_MXFP8,
     )
     handle = ctypes.c_void_p()
-    _lib.check(lib.ce4b_model_create(ctypes.byref(cfg), device, batch, ctypes.byref(handle)))
-    weights = synthetic.make_dense_weights(
-        d_model=D_MODEL, depth=DEPTH, hidden_dim=HIDDEN, seed=0, norm_std=0.0,
-        device=f"cuda:{device}",
-    )
+    _lib.check(lib.ce4b_model_create(ctypes.byref(c), device, batch, ctypes.byref(handle)))
+    weights = make_weights(cfg, f"cuda:{device}")
     torch.cuda.synchronize()
     for name, t in weights.items():
         t = t.contiguous()
@@ -286,14 +349,14 @@ def make_model(device: int, batch: int):
     return lib, handle
 
 
-def run_ours(args: argparse.Namespace) -> None:
+def run_ours(args: argparse.Namespace, cfg: Config) -> None:
     from ce4b200 import _lib, synthetic
 
-    world, rank, local = dist_setup(args.gpus)
+    world, rank, local = dist_setup()
     device = local
     torch.cuda.set_device(device)
-    batch = args.batch
-    lib, handle = make_model(device, batch)
+    batch = cfg.per_gpu(world)
+    lib, handle = make_model(cfg, device, batch)
     stream = torch.cuda.Stream(device)
     sptr = stream.cuda_stream
 
@@ -303,16 +366,34 @@ def run_ours(args: argparse.Namespace) -> None:
     policy = torch.empty(batch, POLICY, dtype=torch.float32, device=device)
     wdl = torch.empty(batch, 3, dtype=torch.float32, device=device)
     ml = torch.empty(batch, dtype=torch.float32, device=device)
+    tokens = torch.empty(max(1, cfg.depth // 2), 64, dtype=torch.int32, device=device)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)  # > 126 MB L2
 
     def forward() -> None:
         _lib.check(lib.ce4b_model_forward(
             handle, _lib.INPUT_LC0, planes_dev.data_ptr(), None, batch, policy.data_ptr(),
-            wdl.data_ptr(), ml.data_ptr(), 0, 0, None, sptr))
+            wdl.data_ptr(), ml.data_ptr(), 0, 0,
+            tokens.data_ptr() if cfg.arch == "moe64a2" else None, sptr))
 
-    # Trace events: one per kernel of the forward, per timed step (steps are enqueued
-    # back to back; the host never waits inside the timed loop).
-    n_kernels = 2 * DEPTH + 3
+    # One traced forward names the kernels of a step (the library records an event after
+    # each kernel; the label list tells which is which).
+    probe = [torch.cuda.Event(enable_timing=True) for _ in range(512)]
+    with torch.cuda.stream(stream):
+        for e in probe:
+            e.record(stream)
+        arr = (ctypes.c_void_p * len(probe))(*[e.cuda_event for e in probe])
+        _lib.check(lib.ce4b_model_set_trace(handle, arr, len(probe)))
+        forward()
+        _lib.check(lib.ce4b_model_set_trace(handle, None, 0))
+        stream.synchronize()
+    labels = []
+    buf = ctypes.create_string_buffer(64)
+    while lib.ce4b_model_trace_label(handle, len(labels), buf, 64) == 0:
+        labels.append(buf.value.decode())
+    n_kernels = len(labels)
+    dominant = "gate_up_swiglu" if cfg.arch == "dense" else "moe_experts_gate_up_swiglu"
+    dom_idx = [i for i, name in enumerate(labels) if name == dominant]
+
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             forward()
@@ -332,6 +413,7 @@ def run_ours(args: argparse.Namespace) -> None:
         if sampler:
             sampler.__enter__()
         try:
+            # Steps are enqueued back to back; the host never waits inside the timed loop.
             for step in range(args.steps):
                 starts[step].record(stream)
                 _lib.check(lib.ce4b_model_set_trace(handle, arrays[step], n_kernels))
@@ -342,18 +424,12 @@ def run_ours(args: argparse.Namespace) -> None:
         finally:
             if sampler:
                 sampler.__exit__(None, None, None)
-    step_ms, gate_ms = [], []
+    step_ms, dom_ms = [], []
     for step in range(args.steps):
         tr = traces[step]
         step_ms.append(starts[step].elapsed_time(tr[-1]))
-        for i in range(2, n_kernels - 1, 2):  # gate_up kernel of layer l sits at 2 + 2l
-            gate_ms.append(tr[i - 1].elapsed_time(tr[i]))
-    labels = []
-    buf = ctypes.create_string_buffer(64)
-    for i in range(n_kernels):
-        _lib.check(lib.ce4b_model_trace_label(handle, i, buf, 64))
-        labels.append(buf.value.decode())
-    assert all(labels[i] == "gate_up_swiglu" for i in range(2, n_kernels - 1, 2)), labels
+        for i in dom_idx:
+            dom_ms.append((tr[i - 1] if i > 0 else starts[step]).elapsed_time(tr[i]))
     barrier(world)
     total_ms = sum(step_ms)
     slowest_ms = max_over_ranks(total_ms, world)
@@ -372,7 +448,7 @@ def run_ours(args: argparse.Namespace) -> None:
             _lib.check(lib.ce4b_model_evaluate_async(
                 handle, planes_host.data_ptr(), b, pol_h.data_ptr(), wdl_h.data_ptr(), ml_h.data_ptr(), sptr))
 
-        e2e_steps = max(1, min(args.steps, 300))
+        e2e_steps = max(1, min(args.steps, 200))
         with torch.cuda.stream(stream):
             for _ in range(max(3, args.warmup)):
                 evaluate(batch)
@@ -417,16 +493,26 @@ def run_ours(args: argparse.Namespace) -> None:
 
     if rank == 0:
         pk = peaks()
-        gate_avg_ms = statistics.mean(gate_ms)
-        achieved = GATE_UP_FLOP_PER_POS * batch / (gate_avg_ms / 1000.0) / 1e12
-        peak = pk["bf16_tflops_sustained"]
+        dom_avg_ms = statistics.mean(dom_ms)
+        dom_flop = cfg.gate_up_flop(batch)
+        achieved = dom_flop / (dom_avg_ms / 1000.0) / 1e12
+        if cfg.precision == "mxfp8":
+            peak = 2.0 * pk["bf16_tflops_sustained"]
+            peak_source = f"{pk['source']} bf16 sustained x2 (MXFP8 peak not measured)"
+        else:
+            peak = pk["bf16_tflops_sustained"]
+            peak_source = f"{pk['source']} bf16 sustained"
         traffic = None
         traffic_file = REPO / "profiles" / "gate_up_swiglu_traffic.json"
-        if traffic_file.is_file():
+        if cfg.name == "c1" and traffic_file.is_file():
             traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch")
-        cpu = None if args.quick else cpu_forward_rate(batch, 512, 3)
+        cpu = None
+        if not args.quick:
+            rate, threads = cpu_rate(cfg, cfg.cpu_sample, 3)
+            cpu = {"value": rate, "unit": "positions/s", "cores": threads, "kind": "port",
+                   "sample": cpu_description(cfg, cfg.cpu_sample)}
         line = {
-            "metric": METRIC,
+            "metric": cfg.metric,
             "value": value,
             "unit": "positions/s",
             "n_gpus": world,
@@ -434,12 +520,12 @@ def run_ours(args: argparse.Namespace) -> None:
             "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if cfg.strong else "weak",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "e4m3/e8m0 (mxfp8), bf16 residual" if cfg.precision == "mxfp8" else "bf16",
             "data": "synthetic",
             "config": {
-                "workload": WORKLOAD,
+                "workload": cfg.workload,
                 "global_batch": batch * world,
                 "per_gpu_batch": batch,
                 "parallelism": f"replicas x{world} (no collective)",
@@ -447,20 +533,21 @@ def run_ours(args: argparse.Namespace) -> None:
                 "input_layout": "lc0 InputPlane records resident in HBM",
             },
             "roofline": {
-                "kernel": "gate_up GEMM + fused SwiGLU (gemm_tc_kernel<256,4,2,2,...,EpiSwiGLU<128>>)",
+                "kernel": f"{dominant} (tcgen05 GEMM + fused SwiGLU epilogue)",
                 "bound": "tensor",
                 "achieved": achieved,
                 "peak": peak,
                 "unit": "TFLOP/s",
                 "frac": achieved / peak,
-                "frac_of_burst": achieved / pk["bf16_tflops"],
-                "peak_source": f"{pk['source']} bf16 sustained",
+                "frac_of_burst": achieved / (pk["bf16_tflops"] * (2.0 if cfg.precision == "mxfp8" else 1.0)),
+                "peak_source": peak_source,
                 "traffic": traffic,
-                "avg_launch_ms": gate_avg_ms,
-                "flop_per_launch": GATE_UP_FLOP_PER_POS * batch,
+                "avg_launch_ms": dom_avg_ms,
+                "flop_per_launch": dom_flop,
             },
-            "forward_tflops": FLOP_PER_POS * batch / (total_ms / args.steps / 1000.0) / 1e12,
+            "forward_tflops": cfg.flop_per_pos() * batch / (total_ms / args.steps / 1000.0) / 1e12,
             "gpu_launches": n_kernels * args.steps,
+            "kernels_per_step": n_kernels,
             "clocks": clocks,
             "e2e": e2e,
             "latency_b64": latency,
@@ -472,10 +559,14 @@ def run_ours(args: argparse.Namespace) -> None:
 
 def main() -> None:
     args = parse_args()
+    cfg = CONFIGS[args.config]
+    if args.batch:
+        cfg = Config(cfg.name, cfg.arch, cfg.d, cfg.depth, cfg.ratio, args.batch, cfg.precision, cfg.cpu_sample,
+                     cfg.strong)
     if args.impl == "reference":
-        run_reference(args)
+        run_reference(args, cfg)
     else:
-        run_ours(args)
+        run_ours(args, cfg)
 
 
 if __name__ == "__main__":
