@@ -44,6 +44,7 @@ import torch  # noqa: E402
 
 IN_DIM = 112 * 64
 POLICY = 1858
+L2_BYTES = 126 * 1024 * 1024
 
 
 @dataclass(frozen=True)
@@ -113,8 +114,8 @@ CONFIGS = {
 def parse_args() -> argparse.Namespace:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=300)
-    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", choices=sorted(CONFIGS), default="c1")
     p.add_argument("--batch", type=int, default=0, help="override the per-GPU batch")
@@ -178,8 +179,11 @@ def dist_teardown(world: int) -> None:
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons every 200 ms while running."""
+    """Samples SM clocks and clock-event (throttle) reasons while the timed region runs:
+    an NVML polling thread every 20 ms (read-only queries), or nvidia-smi every 200 ms
+    when NVML is unavailable."""
 
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     QUERY = (
         "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -187,53 +191,88 @@ class ClockSampler:
     )
 
     def __init__(self, device: int) -> None:
-        # nvidia-smi numbering can differ from CUDA's under CUDA_VISIBLE_DEVICES: use the UUID.
+        # NVML / nvidia-smi numbering can differ from CUDA's: address the GPU by UUID.
         uuid = str(torch.cuda.get_device_properties(device).uuid)
-        self.device = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.proc: subprocess.Popen | None = None
+        self.uuid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        self.samples: list[tuple[float, float, set[str]]] = []
+        self.source = "none"
+        self._stop = None
+        self._thread = None
+        self._proc: subprocess.Popen | None = None
+        self._file = None
+
+    def _nvml_loop(self, nvml, h) -> None:
+        bits = {
+            "hw_slowdown": nvml.nvmlClocksEventReasonHwSlowdown,
+            "hw_thermal_slowdown": nvml.nvmlClocksEventReasonHwThermalSlowdown,
+            "sw_thermal_slowdown": nvml.nvmlClocksEventReasonSwThermalSlowdown,
+            "sw_power_cap": nvml.nvmlClocksEventReasonSwPowerCap,
+        }
+        mx = float(nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                sm = float(nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM))
+                mask = nvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((sm, mx, {k for k, b in bits.items() if mask & b}))
+            except Exception:
+                pass
+            self._stop.wait(0.02)
 
     def __enter__(self) -> "ClockSampler":
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}",
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            h = nvml.nvmlDeviceGetHandleByUUID(self.uuid.encode())
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._nvml_loop, args=(nvml, h), daemon=True)
+            self._thread.start()
+            self.source = "nvml 20 ms"
+            return self
+        except Exception:
+            self._thread = None
+        try:
+            self._file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.uuid}", f"--query-gpu={self.QUERY}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.file, stderr=subprocess.DEVNULL,
+                stdout=self._file, stderr=subprocess.DEVNULL,
             )
+            self.source = "nvidia-smi 200 ms"
         except OSError:
-            self.proc = None
+            self._proc = None
         return self
 
     def __exit__(self, *exc) -> None:
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self._proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
+                self._proc.kill()
+            self._file.flush()
+            self._file.seek(0)
+            for r in self._file.read().strip().splitlines():
+                r = r.split(",")
+                try:
+                    flags = {n for n, f in zip(self.REASONS, r[5:9]) if f.strip().lower() == "active"}
+                    self.samples.append((float(r[1]), float(r[2]), flags))
+                except (ValueError, IndexError):
+                    continue
+            os.unlink(self._file.name)
 
     def summary(self) -> dict:
-        self.file.flush()
-        self.file.seek(0)
-        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
-        os.unlink(self.file.name)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            if len(r) < 9:
-                continue
-            try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, r[5:9]):
-                if flag.strip().lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": self.source}
+        reasons = set().union(*(r for _, _, r in self.samples))
+        return {"sm_mhz": statistics.median(sm for sm, _, _ in self.samples),
+                "sm_max_mhz": max(mx for _, mx, _ in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": self.source}
 
 
 # ---------------------------------------------------------------- weights and CPU implementation
@@ -402,13 +441,11 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
         barrier(world)
         torch.cuda.synchronize()
 
+        # Timed pass: events only at step boundaries. (An event recorded between two kernels
+        # serialises them and defeats programmatic dependent launch, so the per-kernel
+        # events live in the second pass below.)
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        traces = [[torch.cuda.Event(enable_timing=True) for _ in range(n_kernels)] for _ in range(args.steps)]
-        for tr in traces:  # torch creates the CUDA event on first record
-            for e in tr:
-                e.record(stream)
-        stream.synchronize()
-        arrays = [(ctypes.c_void_p * n_kernels)(*[e.cuda_event for e in tr]) for tr in traces]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         sampler = ClockSampler(device) if not args.quick else None
         if sampler:
             sampler.__enter__()
@@ -416,20 +453,43 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
             # Steps are enqueued back to back; the host never waits inside the timed loop.
             for step in range(args.steps):
                 starts[step].record(stream)
-                _lib.check(lib.ce4b_model_set_trace(handle, arrays[step], n_kernels))
                 forward()
+                ends[step].record(stream)
                 flush.zero_()
-            _lib.check(lib.ce4b_model_set_trace(handle, None, 0))
             stream.synchronize()
         finally:
             if sampler:
                 sampler.__exit__(None, None, None)
-    step_ms, dom_ms = [], []
-    for step in range(args.steps):
+        step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+        # Kernel pass: the same steps with an event after every kernel; gives each kernel's
+        # duration (launch included, since the events serialise the launches).
+        trace_steps = max(1, min(args.steps, 200))
+        traces = [[torch.cuda.Event(enable_timing=True) for _ in range(n_kernels)] for _ in range(trace_steps)]
+        tstarts = [torch.cuda.Event(enable_timing=True) for _ in range(trace_steps)]
+        for tr in traces:  # torch creates the CUDA event on first record
+            for e in tr:
+                e.record(stream)
+        stream.synchronize()
+        arrays = [(ctypes.c_void_p * n_kernels)(*[e.cuda_event for e in tr]) for tr in traces]
+        for step in range(trace_steps):
+            tstarts[step].record(stream)
+            _lib.check(lib.ce4b_model_set_trace(handle, arrays[step], n_kernels))
+            forward()
+            flush.zero_()
+        _lib.check(lib.ce4b_model_set_trace(handle, None, 0))
+        stream.synchronize()
+    dom_ms = []
+    kernel_ms: dict[str, float] = {}
+    traced_step_ms = []
+    for step in range(trace_steps):
         tr = traces[step]
-        step_ms.append(starts[step].elapsed_time(tr[-1]))
-        for i in dom_idx:
-            dom_ms.append((tr[i - 1] if i > 0 else starts[step]).elapsed_time(tr[i]))
+        traced_step_ms.append(tstarts[step].elapsed_time(tr[-1]))
+        for i, name in enumerate(labels):
+            dt = (tr[i - 1] if i > 0 else tstarts[step]).elapsed_time(tr[i])
+            kernel_ms[name] = kernel_ms.get(name, 0.0) + dt / trace_steps
+            if i in dom_idx:
+                dom_ms.append(dt)
     barrier(world)
     total_ms = sum(step_ms)
     slowest_ms = max_over_ranks(total_ms, world)
@@ -440,39 +500,77 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
     e2e = None
     latency = None
     if not args.quick:
-        pol_h = torch.empty(batch, POLICY, dtype=torch.float32).pin_memory()
-        wdl_h = torch.empty(batch, 3, dtype=torch.float32).pin_memory()
-        ml_h = torch.empty(batch, dtype=torch.float32).pin_memory()
+        # Two sets of pinned host outputs, one per stream; the planes are re-sent every call.
+        outs = [tuple(t.pin_memory() for t in (torch.empty(batch, POLICY), torch.empty(batch, 3), torch.empty(batch)))
+                for _ in range(2)]
+        pol_h, wdl_h, ml_h = outs[0]
+        e2e_streams = [stream, torch.cuda.Stream(device)]
 
-        def evaluate(b: int) -> None:
+        def evaluate(b: int, i: int) -> None:
+            pol, wdl_o, ml_o = outs[i % 2]
             _lib.check(lib.ce4b_model_evaluate_async(
-                handle, planes_host.data_ptr(), b, pol_h.data_ptr(), wdl_h.data_ptr(), ml_h.data_ptr(), sptr))
+                handle, planes_host.data_ptr(), b, pol.data_ptr(), wdl_o.data_ptr(), ml_o.data_ptr(),
+                e2e_streams[i % 2].cuda_stream))
 
-        e2e_steps = max(1, min(args.steps, 200))
+        e2e_steps = max(2, min(args.steps, 400))
+        for i in range(max(4, args.warmup)):  # builds the graph of both I/O slots
+            evaluate(batch, i)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        torch.cuda.synchronize(device)
+        # Pipelined: calls alternate over two streams, back to back, as a serving loop
+        # issues them; the H2D of each call and the D2H of the one before it overlap a
+        # forward. Timed from the first H2D to the last D2H.
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(e2e_streams[0])
+        e2e_streams[1].wait_event(ev0)
+        for i in range(e2e_steps):
+            evaluate(batch, i)
+        e2e_streams[0].wait_stream(e2e_streams[1])
+        ev1.record(e2e_streams[0])
+        ev1.synchronize()
+        e2e_ms = ev0.elapsed_time(ev1)
+        # Serial: one call at a time on one stream (H2D, forward, D2H, then the next).
+        serial_steps = max(1, min(args.steps, 100))
+        serial_ms = 0.0
         with torch.cuda.stream(stream):
-            for _ in range(max(3, args.warmup)):
-                evaluate(batch)
-            stream.synchronize()
-            barrier(world)
-            ev0 = torch.cuda.Event(enable_timing=True)
-            ev1 = torch.cuda.Event(enable_timing=True)
-            e2e_ms = 0.0
-            for _ in range(e2e_steps):
-                ev0.record(stream)
-                evaluate(batch)
-                ev1.record(stream)
-                stream.synchronize()
-                e2e_ms += ev0.elapsed_time(ev1)
+            for _ in range(serial_steps):
+                s0 = torch.cuda.Event(enable_timing=True)
+                s1 = torch.cuda.Event(enable_timing=True)
                 flush.zero_()
-            stream.synchronize()
+                s0.record(stream)
+                evaluate(batch, 0)
+                s1.record(stream)
+                s1.synchronize()
+                serial_ms += s0.elapsed_time(s1)
         e2e_slowest = max_over_ranks(e2e_ms, world)
+        serial_slowest = max_over_ranks(serial_ms, world)
+        # Bytes one step touches: weights, planes in, expanded input operand, activations,
+        # FP32 outputs. Back-to-back steps are only reported when that exceeds L2.
+        info = _lib.ModelInfoStruct()
+        _lib.check(lib.ce4b_model_info_get(handle, ctypes.byref(info)))
+        act = cfg.d * 2 * 3 + cfg.dense_hidden * 2 + (2 * cfg.hidden * 2 * 2 if cfg.arch == "moe64a2" else 0)
+        per_pos = 1792 + IN_DIM * (1 if cfg.precision == "mxfp8" else 2) + act + (POLICY + 4) * 4
+        working_set = info.weight_bytes + batch * per_pos
+        pipelined = working_set > L2_BYTES
+        e2e_value = world * batch * e2e_steps / (e2e_slowest / 1000.0)
+        serial_value = world * batch * serial_steps / (serial_slowest / 1000.0)
         e2e = {
-            "value": world * batch * e2e_steps / (e2e_slowest / 1000.0),
+            "value": e2e_value if pipelined else serial_value,
             "unit": "positions/s",
             "h2d_bytes_per_step": batch * 112 * 16,
             "d2h_bytes_per_step": batch * (POLICY + 3 + 1) * 4,
             "steps": e2e_steps,
-            "api": "ce4b_model_evaluate_async (pinned host buffers, CUDA graph per batch size)",
+            "api": ("ce4b_model_evaluate_async, calls alternating over two streams (pinned host buffers, "
+                    "CUDA graph per batch size and I/O slot)") if pipelined else
+                   "ce4b_model_evaluate_async, one call per step on one stream (pinned host buffers)",
+            "l2": (f"not flushed between pipelined steps: a step touches {working_set / 1e6:.0f} MB "
+                   f"(weights, planes, expanded operand, activations, FP32 outputs) > 126 MB L2") if pipelined else
+                  f"flushed before each step (untimed); a step touches only {working_set / 1e6:.0f} MB",
+            "pipelined_value": e2e_value,
+            "serial_value": serial_value,
+            "serial": "one call per step on one stream, L2 flushed before each (untimed)",
         }
         # ---- p50 latency at batch 64 (blocking engine call, host buffers)
         lat = []
@@ -544,7 +642,12 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
                 "traffic": traffic,
                 "avg_launch_ms": dom_avg_ms,
                 "flop_per_launch": dom_flop,
+                "timing": f"CUDA events around each of its {len(dom_ms)} launches in a second pass of "
+                          f"{trace_steps} steps (per-kernel events serialise launches; the timed pass has "
+                          "events at step boundaries only)",
             },
+            "kernel_ms_per_step": {k: round(v, 5) for k, v in kernel_ms.items()},
+            "traced_ms_per_step": statistics.mean(traced_step_ms),
             "forward_tflops": cfg.flop_per_pos() * batch / (total_ms / args.steps / 1000.0) / 1e12,
             "gpu_launches": n_kernels * args.steps,
             "kernels_per_step": n_kernels,

@@ -4,6 +4,7 @@ Public API mirrors ``chess_engine_4.model`` (model classes, configs, output type
 ``chess_engine_4.kernels`` (kernel operators); computation runs in libce4b200.so.
 """
 
+from .engine import Engine, export_model, exported_model, safetensors_metadata
 from .model import (
     ChessNetOutput,
     DenseChessNet,
@@ -21,6 +22,10 @@ from .model import (
 
 __all__ = [
     "ChessNetOutput",
+    "Engine",
+    "export_model",
+    "exported_model",
+    "safetensors_metadata",
     "DenseChessNet",
     "DenseChessNetConfig",
     "Moe64A2ChessNet",

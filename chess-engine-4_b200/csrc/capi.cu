@@ -172,9 +172,9 @@ int ce4b_model_forward(ce4b_model* model, int input_layout, void* input_dev,
   return guarded([&] {
     require(model != nullptr && model->impl, "null model");
     check_cuda(cudaSetDevice(model->impl->device), "cudaSetDevice");
-    model->impl->forward(input_layout, input_dev, scalars_dev, batch, policy_dev, wdl_dev,
-                         moves_left_dev, wdl_probs, normalize_in_place, tokens_per_expert_dev,
-                         as_stream(stream));
+    model->impl->forward_ordered(input_layout, input_dev, scalars_dev, batch, policy_dev,
+                                 wdl_dev, moves_left_dev, wdl_probs, normalize_in_place,
+                                 tokens_per_expert_dev, as_stream(stream));
   });
 }
 

@@ -197,6 +197,10 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
   }
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // The prologue above (barriers, TMEM) may overlap the previous kernel of the stream; no
+  // global memory is read or written before that kernel has completed.
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -433,6 +437,10 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
   }
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // The prologue above (barriers, TMEM) may overlap the previous kernel of the stream; no
+  // global memory is read or written before that kernel has completed.
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {

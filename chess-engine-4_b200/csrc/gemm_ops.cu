@@ -56,15 +56,22 @@ void launch(K kernel, dim3 grid, int threads, int smem, int cluster_x, cudaStrea
   cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  // Every GEMM kernel waits for its predecessor (grid_dependency_wait) before touching
+  // global memory, so it may be launched programmatically: its CTAs take SMs as the
+  // previous kernel's CTAs leave and run their prologue under that kernel's tail.
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  unsigned n_attr = 1;
   if (cluster_x > 0) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(cluster_x);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n_attr = 2;
   }
+  cfg.attrs = attr;
+  cfg.numAttrs = n_attr;
   check_cuda(cudaLaunchKernelEx(&cfg, kernel, args...), "gemm launch");
 }
 

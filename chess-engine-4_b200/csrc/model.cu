@@ -42,6 +42,9 @@ std::string shape_str(const std::vector<int64_t>& s) {
 Model::~Model() {
   if (device >= 0) cudaSetDevice(device);
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& slot : io)
+    if (slot.free) cudaEventDestroy(slot.free);
+  if (forward_done) cudaEventDestroy(forward_done);
   if (stream) cudaStreamDestroy(stream);
   if (arena) cudaFree(arena);
   if (mx_arena) cudaFree(mx_arena);
@@ -99,14 +102,16 @@ void Model::plan_workspace() {
     return off;
   };
   const size_t r = static_cast<size_t>(rows_cap);
-  ws_off.planes = take(r * kInputPlanes * sizeof(ce4b_input_plane));
+  for (auto& slot : io) {
+    slot.planes = take(r * kInputPlanes * sizeof(ce4b_input_plane));
+    slot.policy = take(r * policy_size * 4);
+    slot.wdl = take(r * 3 * 4);
+    slot.moves_left = take(r * 4);
+  }
   ws_off.a_in = take(r * in_dim * 2);
   ws_off.x = take(r * d * 2);
   ws_off.n = take(r * d * 2);
   ws_off.hidden = take(r * std::max(dense_hidden, expert_hidden) * 2);
-  ws_off.policy = take(r * policy_size * 4);
-  ws_off.wdl = take(r * 3 * 4);
-  ws_off.moves_left = take(r * 4);
   if (mx) {
     const size_t t = r / 128;
     ws_off.a_codes = take(r * in_dim);
@@ -190,6 +195,9 @@ void Model::create(const ce4b_model_config& c, int dev, int maxb) {
   check_cuda(cudaMalloc(&workspace, workspace_bytes), "cudaMalloc workspace");
   check_cuda(cudaMemset(workspace, 0, workspace_bytes), "cudaMemset workspace");
   check_cuda(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "create stream");
+  check_cuda(cudaEventCreateWithFlags(&forward_done, cudaEventDisableTiming), "create event");
+  for (auto& slot : io)
+    check_cuda(cudaEventCreateWithFlags(&slot.free, cudaEventDisableTiming), "create event");
 }
 
 void Model::set_tensor(const std::string& name, const void* data, int dtype,
@@ -424,6 +432,19 @@ void Model::moe_layer(const Layer& L, int moe_index, const bf16* next_norm, int 
   trace("moe_combine_rmsnorm", s);
 }
 
+void Model::forward_ordered(int layout, void* input, const void* scalars, int batch,
+                            float* policy, float* wdl, float* moves_left, int wdl_probs,
+                            int normalize_in_place, int32_t* tokens_per_expert, cudaStream_t s) {
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  check_cuda(cudaStreamIsCapturing(s, &capture), "query stream capture");
+  // Under the caller's stream capture the graph's own edges order the launches.
+  const bool order = capture == cudaStreamCaptureStatusNone;
+  if (order) check_cuda(cudaStreamWaitEvent(s, forward_done, 0), "wait previous forward");
+  forward(layout, input, scalars, batch, policy, wdl, moves_left, wdl_probs, normalize_in_place,
+          tokens_per_expert, s);
+  if (order) check_cuda(cudaEventRecord(forward_done, s), "record forward");
+}
+
 void Model::trace(const char* label, cudaStream_t s) {
   if (trace_next >= trace_events.size()) return;
   check_cuda(cudaEventRecord(trace_events[trace_next++], s), "record trace event");
@@ -436,18 +457,22 @@ void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, flo
   require(batch >= 1 && batch <= max_batch, "batch size exceeds model capacity");
   require(host_planes && host_policy && host_wdl && host_moves_left, "null host buffer");
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
-  auto* planes = reinterpret_cast<ce4b_input_plane*>(workspace + ws_off.planes);
-  float* pol = reinterpret_cast<float*>(workspace + ws_off.policy);
-  float* wdl = reinterpret_cast<float*>(workspace + ws_off.wdl);
-  float* ml = reinterpret_cast<float*>(workspace + ws_off.moves_left);
-  const int key = batch * 2 + 1;
+  const int slot = static_cast<int>(io_next % kIoSlots);
+  IoSlot& io_slot = io[slot];
+  auto* planes = reinterpret_cast<ce4b_input_plane*>(workspace + io_slot.planes);
+  float* pol = reinterpret_cast<float*>(workspace + io_slot.policy);
+  float* wdl = reinterpret_cast<float*>(workspace + io_slot.wdl);
+  float* ml = reinterpret_cast<float*>(workspace + io_slot.moves_left);
+  const int key = batch * kIoSlots + slot;
   auto it = graphs.find(key);
   if (it == graphs.end()) {
-    // First use of this batch size: run once outside a capture (kernel attributes), then
-    // capture the forward into a graph on the internal stream. Blocks.
+    // First use of this batch size and slot: run once outside a capture (kernel
+    // attributes), then capture the forward into a graph on the internal stream. Blocks.
     const std::vector<cudaEvent_t> saved = std::move(trace_events);
     trace_events.clear();
     try {
+      check_cuda(cudaStreamWaitEvent(stream, forward_done, 0), "wait previous forward");
+      check_cuda(cudaStreamWaitEvent(stream, io_slot.free, 0), "wait I/O slot");
       forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
       check_cuda(cudaStreamSynchronize(stream), "warm-up forward");
       check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
@@ -472,11 +497,17 @@ void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, flo
     }
     trace_events = saved;
   }
+  ++io_next;
+  // This slot's previous D2H copies are done before its planes are overwritten; the H2D
+  // copy may overlap the previous call's forward, which the graph then waits for.
+  check_cuda(cudaStreamWaitEvent(s, io_slot.free, 0), "wait I/O slot");
   check_cuda(cudaMemcpyAsync(planes, host_planes,
                              static_cast<size_t>(batch) * kInputPlanes * sizeof(ce4b_input_plane),
                              cudaMemcpyHostToDevice, s),
              "copy input planes");
+  check_cuda(cudaStreamWaitEvent(s, forward_done, 0), "wait previous forward");
   check_cuda(cudaGraphLaunch(it->second, s), "launch graph");
+  check_cuda(cudaEventRecord(forward_done, s), "record forward");
   check_cuda(cudaMemcpyAsync(host_policy, pol, static_cast<size_t>(batch) * policy_size * 4,
                              cudaMemcpyDeviceToHost, s),
              "copy policy");
@@ -486,6 +517,7 @@ void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, flo
   check_cuda(cudaMemcpyAsync(host_moves_left, ml, static_cast<size_t>(batch) * 4,
                              cudaMemcpyDeviceToHost, s),
              "copy moves left");
+  check_cuda(cudaEventRecord(io_slot.free, s), "record I/O slot");
 }
 
 void Model::evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,

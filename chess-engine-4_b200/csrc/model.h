@@ -29,7 +29,7 @@ struct Model {
     const uint8_t* down_scales = nullptr;
   };
   struct WorkspaceOffsets {
-    size_t planes = 0, a_in = 0, x = 0, n = 0, hidden = 0, policy = 0, wdl = 0, moves_left = 0;
+    size_t a_in = 0, x = 0, n = 0, hidden = 0;
     size_t route_expert = 0, route_prob = 0, route_pos = 0, block_hist = 0, block_off = 0;
     size_t expert_start = 0, m_tiles = 0, num_m_tiles = 0, xperm = 0, pprob = 0, hperm = 0;
     size_t yperm = 0;
@@ -67,7 +67,19 @@ struct Model {
   std::vector<Layer> layers;
   bool finalized = false;
   cudaStream_t stream = nullptr;
-  std::map<int, cudaGraphExec_t> graphs;  // key: batch * 2 + wdl_probs
+  // Host-buffer evaluation keeps kIoSlots sets of device planes / outputs so that the
+  // copies of one call overlap the forward of the next when calls come on different
+  // streams. A slot is reused only after its last D2H copy (io[slot].free); forwards share
+  // the workspace and are ordered by forward_done.
+  static constexpr int kIoSlots = 2;
+  struct IoSlot {
+    size_t planes = 0, policy = 0, wdl = 0, moves_left = 0;  // workspace offsets
+    cudaEvent_t free = nullptr;
+  };
+  IoSlot io[kIoSlots];
+  unsigned io_next = 0;
+  cudaEvent_t forward_done = nullptr;
+  std::map<int, cudaGraphExec_t> graphs;  // key: batch * kIoSlots + slot
   // Optional per-kernel trace: an event is recorded after each kernel of forward().
   std::vector<cudaEvent_t> trace_events;
   std::vector<std::string> trace_labels;
@@ -86,6 +98,11 @@ struct Model {
   void forward(int layout, void* input, const void* scalars, int batch, float* policy, float* wdl,
                float* moves_left, int wdl_probs, int normalize_in_place,
                int32_t* tokens_per_expert, cudaStream_t s);
+  // forward() ordered after every earlier forward of this model on any stream (outside
+  // stream capture), so calls on different streams never share the workspace in flight.
+  void forward_ordered(int layout, void* input, const void* scalars, int batch, float* policy,
+                       float* wdl, float* moves_left, int wdl_probs, int normalize_in_place,
+                       int32_t* tokens_per_expert, cudaStream_t s);
   void evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
                 float* host_wdl, float* host_moves_left);
   void enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,

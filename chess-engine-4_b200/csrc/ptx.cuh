@@ -360,6 +360,19 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialisation may start while the previous
+// kernel of its stream is still running. grid_dependency_wait() returns once that kernel
+// has completed and its memory operations are visible; grid_launch_dependents() lets the
+// next such kernel start its own prologue early. Both are no-ops for ordinary launches.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- numerics helpers
 __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16(v));

@@ -131,7 +131,9 @@ int ce4b_model_info_get(const ce4b_model* model, ce4b_model_info* info);
  * wdl_probs != 0), moves_left [B] f32. For moe64a2, tokens_per_expert_dev receives
  * [depth/2, 64] int32 counts (may be NULL). For CE4B_INPUT_F32_PLANES with
  * `normalize_in_place` != 0 the rule-50 plane of the input is divided by 99 in place,
- * as normalize_lc0_planes does (src/chess_engine_4/model/dense.py:34-42). */
+ * as normalize_lc0_planes does (src/chess_engine_4/model/dense.py:34-42).
+ * Outside stream capture the forward is ordered after the model's previous forward on
+ * any stream (it shares the model's workspace); under capture the caller's graph orders it. */
 int ce4b_model_forward(ce4b_model* model, int input_layout, void* input_dev,
                        const void* scalars_dev, int batch, float* policy_dev, float* wdl_dev,
                        float* moves_left_dev, int wdl_probs, int normalize_in_place,
@@ -146,7 +148,12 @@ int ce4b_model_evaluate(ce4b_model* model, const ce4b_input_plane* host_planes, 
 /* Asynchronous form of ce4b_model_evaluate on `stream`: enqueues the H2D copy, the
  * graph and the D2H copies and returns. Host buffers must stay valid (and should be
  * pinned) until the stream reaches that point. The first call for a batch size builds
- * its graph and blocks. */
+ * its graphs and blocks.
+ * The model owns two device I/O slots used in turn. Consecutive calls on different
+ * streams overlap: a call's H2D copy and the previous call's D2H copies run while a
+ * forward computes. Forwards of one model never overlap one another (each waits for the
+ * previous one on any stream), and a slot's planes are overwritten only after its last
+ * D2H copies have finished. Calls on one handle must still be serialised on the host. */
 int ce4b_model_evaluate_async(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
                               float* host_policy, float* host_wdl, float* host_moves_left,
                               void* stream);

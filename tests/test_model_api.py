@@ -85,6 +85,41 @@ def test_safetensors_names_follow_export_contract() -> None:
     }
 
 
+def test_exported_file_carries_loader_metadata(tmp_path) -> None:
+    """The exported file has the metadata the C++ loader validates (keys and values of
+    src/chess_engine_4/release/export.py:191-219, MoE keys :153-160)."""
+
+    from safetensors import safe_open
+
+    from ce4b200 import DenseChessNet, DenseChessNetConfig, Moe64A2ChessNet, Moe64A2ChessNetConfig, export_model
+
+    dense = DenseChessNet(DenseChessNetConfig(d_model=64, depth=2, expansion_ratio=3.0))
+    export_model(dense, tmp_path / "d.safetensors")
+    with safe_open(str(tmp_path / "d.safetensors"), "pt") as f:
+        meta = f.metadata()
+        assert set(f.keys()) == set(dense.safetensors_tensors())
+        assert f.get_tensor("policy.weight").dtype == torch.bfloat16
+    assert meta["format"] == "chess-engine-4" and meta["format_version"] == "1"
+    assert meta["architecture"] == "dense" and meta["activation"] == "swiglu"
+    assert (meta["d_model"], meta["depth"], meta["expansion_ratio"]) == ("64", "2", "3.0")
+    assert meta["input_format"] == "lc0-classical-112"
+    assert meta["input_normalization"] == "history-select-rule50-div99-v1"
+    assert (meta["input_planes"], meta["board_size"], meta["policy_size"]) == ("112", "8", "1858")
+    assert meta["policy_storage_size"] == "1888" and meta["rms_norm_eps"] == "1e-06"
+    assert "num_experts" not in meta
+
+    moe = Moe64A2ChessNet(Moe64A2ChessNetConfig(d_model=64, depth=2, expansion_ratio=1.0))
+    export_model(moe, tmp_path / "m.safetensors")
+    with safe_open(str(tmp_path / "m.safetensors"), "pt") as f:
+        meta = f.metadata()
+        assert f.get_tensor("blocks.0.router_qb_beta").dtype == torch.float32
+        assert tuple(f.get_tensor("blocks.0.experts.gate_up.weight").shape) == (64, 128, 64)
+    assert meta["architecture"] == "moe64a2"
+    assert (meta["num_experts"], meta["num_active_experts"], meta["layer_pattern"]) == (
+        "64", "2", "alternating-moe-dense"
+    )
+
+
 def test_forward_rejects_cpu_planes_without_fallback() -> None:
     from ce4b200 import DenseChessNet, DenseChessNetConfig
 
