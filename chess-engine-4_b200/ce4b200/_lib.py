@@ -105,6 +105,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ce4b_model_evaluate": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "ce4b_model_evaluate_async": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "ce4b_model_set_trace": (_i32, [_vp, _vp, _i32]),
+    "ce4b_model_set_task_trace": (_i32, [_vp, _vp, _i32]),
+    "ce4b_model_task_count": (_i32, [_vp, _i32, ctypes.POINTER(_i32)]),
     "ce4b_model_trace_label": (_i32, [_vp, _i32, ctypes.c_char_p, _i32]),
     "ce4b_model_destroy": (None, [_vp]),
     "ce4b_bf16_gemm": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),

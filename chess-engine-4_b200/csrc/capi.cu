@@ -205,6 +205,26 @@ int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count) {
   });
 }
 
+int ce4b_model_set_task_trace(ce4b_model* model, void* device_buffer, int capacity_tasks) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    require(capacity_tasks >= 0 && (capacity_tasks == 0 || device_buffer != nullptr),
+            "bad task trace buffer");
+    require((reinterpret_cast<uintptr_t>(device_buffer) & 7u) == 0, "task trace buffer not 8-byte aligned");
+    model->impl->fwd_trace = capacity_tasks > 0 ? static_cast<unsigned long long*>(device_buffer) : nullptr;
+    model->impl->fwd_trace_cap = capacity_tasks;
+  });
+}
+
+int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks) {
+  return guarded([&] {
+    require(model != nullptr && model->impl && tasks != nullptr, "null argument");
+    const ce4b::Model& m = *model->impl;
+    require(batch >= 1 && batch <= m.max_batch, "batch size exceeds model capacity");
+    *tasks = m.fused ? m.fused_task_count(batch) : 0;
+  });
+}
+
 int ce4b_model_trace_label(const ce4b_model* model, int index, char* buffer, int buffer_len) {
   return guarded([&] {
     require(model != nullptr && model->impl && buffer != nullptr && buffer_len > 0,
@@ -305,7 +325,7 @@ int ce4b_dense_block_forward(const void* x_dev, const void* norm_weight_dev,
                                cudaMemcpyDeviceToDevice, s),
                "copy residual");
     const CUtensorMap t_down = make_tmap_bf16(down_weight_dev, d_model, hidden_dim, hidden_dim,
-                                              static_cast<uint32_t>(resnorm_bn(d_model)));
+                                              static_cast<uint32_t>(resnorm_b_box(d_model)));
     const CUtensorMap t_out = make_tmap_bf16(out_dev, rows, d_model, d_model, 128);
     gemm_resnorm(t_hidden, t_down, t_out, t_out, nullptr, nullptr, rows, d_model, hidden_dim, eps, s);
   });

@@ -327,4 +327,22 @@ void residual_add(bf16* out, const bf16* residual, int64_t elements, cudaStream_
   check_cuda(cudaGetLastError(), "residual_add launch");
 }
 
+// ------------------------------------------------------------------ weight folding
+// out[r, c] = bf16(W[r, c] * w[c]): an RMSNorm weight folded into the following linear
+// (the product of two BF16 values is exact in FP32, so this rounds once).
+__global__ void fold_columns_kernel(const bf16* __restrict__ W, const bf16* __restrict__ w,
+                                    bf16* __restrict__ out, int64_t n, int cols) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % cols);
+    out[i] = __float2bfloat16_rn(__bfloat162float(W[i]) * __bfloat162float(w[c]));
+  }
+}
+
+void fold_columns(const bf16* W, const bf16* w, bf16* out, int64_t rows, int cols, cudaStream_t s) {
+  const int64_t n = rows * cols;
+  fold_columns_kernel<<<grid_for(n, 256), 256, 0, s>>>(W, w, out, n, cols);
+  check_cuda(cudaGetLastError(), "fold_columns launch");
+}
+
 }  // namespace ce4b

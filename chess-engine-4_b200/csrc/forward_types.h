@@ -1,0 +1,62 @@
+// Types shared by the persistent dense forward kernel (forward.cuh) and its host side.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+namespace ce4b {
+
+constexpr int kFwdKBlock = 64;  // BF16 k-block (one 128-byte swizzle span)
+constexpr int kFwdMaxDepth = 32;
+constexpr int kFwdMaxSlices = 8;  // d / 128 <= 8 (d <= 1024)
+constexpr int kFwdNStage = 4;
+constexpr int kFwdTaskRing = 4;
+constexpr int kFwdG = 4;
+constexpr int kFwdThreads = 64 + 128 * kFwdG;
+constexpr int kFwdEpiThreads = 128 * kFwdG;
+constexpr int kErrTimeoutDependency = 7;
+
+enum FwdTaskType : int { kTaskEnd = -1, kTaskInput = 0, kTaskGateUp = 1, kTaskDown = 2 };
+
+// Tensor maps in global memory (64-byte aligned), written once by the host.
+struct FwdMaps {
+  CUtensorMap a_in;    // expanded planes [rows, in_dim], box 64 x 128
+  CUtensorMap x;       // residual stream [rows, d], box 64 x 128 (A of the gate_up tiles)
+  CUtensorMap hidden;  // [rows, h], box 64 x 128
+  CUtensorMap w_in;    // input.weight [d, in_dim], box 64 x 128
+  CUtensorMap gate_up[kFwdMaxDepth];  // bf16(gate_up.weight * norm.weight) [2h, d], box 64 x 128
+  CUtensorMap down[kFwdMaxDepth];     // [d, h], box 64 x 128
+};
+
+struct FwdParams {
+  const FwdMaps* maps;
+  const __nv_bfloat16* bias;  // input.bias [d]
+  __nv_bfloat16* x;           // [rows_cap, d]
+  __nv_bfloat16* hidden;      // [rows_cap, h]
+  float* ss;                  // [rows_cap, sj * kFwdG] partial sums of squares of x
+  float* part;                // [ks, rows_cap, d] input split partials (ks > 1)
+  int* hid_cnt;               // [nb] finished gate_up tiles
+  int* slice_cnt;             // [nb] finished x slices
+  int* part_cnt;              // [nb * sj] finished input splits per slice
+  int* task_counter;          // [1]
+  int* err;
+  int rows_cap;
+  int nb;      // row blocks of 128
+  int d, h, depth;
+  int sj;      // d / 128 column slices
+  int nc;      // h / 128 hidden chunks
+  int ks;      // k splits of the input GEMM
+  int kb_in;   // k-blocks of the input GEMM (in_dim / 64)
+  int total_tasks;
+  float eps;
+  // Optional per-task timeline (nullptr: off): kFwdTraceWords u64 per task id < trace_cap,
+  // %globaltimer ns of {0 fetched, 1 dependencies met, 2 last load issued, 3 first MMA
+  // issued, 4 accumulator committed, 5 epilogue started, 6 epilogue done, 7 epilogue
+  // results stored, 8 epilogue published}, then the CTA index in word 10 (9, 11 unused).
+  unsigned long long* trace;
+  int trace_cap;
+};
+
+constexpr int kFwdTraceWords = 12;
+
+}  // namespace ce4b

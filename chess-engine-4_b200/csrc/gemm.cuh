@@ -102,6 +102,9 @@ struct EpiCtx {
   uint32_t epi_bar;     // cluster exchange barrier
   uint32_t x_bar;       // producer prefetch barrier
   uint32_t tempty_bar;  // accumulator release barrier of this tile
+  bool tempty_remote = false;  // tempty_bar is a shared::cluster address (CTA pairs)
+  int rank_base = 0;    // cluster rank of this CTA's slice 0 (row-statistics exchange)
+  int rank_stride = 1;  // cluster rank step between slices (2 for CTA pairs)
   int iter;             // tile iteration of this CTA (0, 1, ...)
   const CUtensorMap* tmO1;
   const CUtensorMap* tmO2;
@@ -111,7 +114,11 @@ struct EpiCtx {
 // Every epilogue thread calls this once per tile after its last tcgen05.ld completed.
 __device__ __forceinline__ void release_accumulator(const EpiCtx& ctx) {
   tc_fence_before();
-  mbar_arrive(ctx.tempty_bar);
+  if (ctx.tempty_remote) {
+    mbar_arrive_remote(ctx.tempty_bar);
+  } else {
+    mbar_arrive(ctx.tempty_bar);
+  }
 }
 
 template <int G>
@@ -340,6 +347,283 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ CTA-pair GEMM
+// The same pipeline on tcgen05 CTA pairs (cta_group::2). A pair tile is 256 rows x BN
+// columns: the even CTA of the pair computes rows 0..127 (in its tensor memory), the odd
+// CTA rows 128..255. Each CTA loads its own 128 A rows and half of the B tile (BN/2 rows;
+// for SwiGLU the even CTA loads the gate rows and the odd CTA the up rows) into its own
+// shared memory, so a CTA stages 16 KB + BN*64 B per k-block for a 128 x BN result: half
+// the B traffic of a single-CTA tile, which is what limits the single-CTA main loop (the
+// tensor core's operand reads and TMA's writes share the SM's shared-memory bandwidth).
+// Both CTAs' loads complete on the even CTA's full barrier; its single MMA thread issues
+// M=256 MMAs and multicasts each commit to the empty / accumulator-full barriers of both
+// CTAs; both CTAs' epilogue threads release the accumulator on the even CTA's barrier.
+// CLUSTER_N > 1 groups CLUSTER_N pairs in one cluster (ranks 2j, 2j+1 = pair j = column
+// slice j of the same 256 rows) for the row-statistics exchange of EpiResNorm.
+struct DensePairSched {
+  int m;            // rows of A / C
+  int n_tiles;      // output column tiles
+  int num_tiles;    // ceil(m / 256) * n_tiles
+  int b_tile_rows;  // B rows advanced per n_tile
+  int b_half_rows;  // B rows held by each CTA (BN / 2)
+  int b_up_offset;  // SwiGLU: the odd CTA's rows start this far past the even CTA's, else 0
+  __device__ __forceinline__ int count() const { return num_tiles; }
+  __device__ __forceinline__ TileCoord coord(int t, int half) const {
+    TileCoord c;
+    const int mt = t / n_tiles;
+    c.n_tile = t - mt * n_tiles;
+    c.a_row = (2 * mt + half) * kBM;
+    c.out_row = c.a_row;
+    c.rows = min(kBM, m - c.a_row);  // <= 0 for the odd CTA of a final half-empty tile
+    c.b_row = c.n_tile * b_tile_rows + half * (b_up_offset != 0 ? b_up_offset : b_half_rows);
+    c.b_row2 = c.b_row;
+    c.group = 0;
+    return c;
+  }
+};
+
+template <int BN, int NSTAGE, int NACC, class Epi>
+struct GemmPairSmem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = (BN / 2) * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kRingBytes = NSTAGE * kStageBytes;
+  static constexpr int kEpiBytes = (Epi::kSmemBytes + 1023) / 1024 * 1024;
+  static constexpr int kBarrierBytes = (2 * NSTAGE + 2 * NACC + 3) * 8 + 8;
+  static constexpr int kBytes = 1024 + kRingBytes + kEpiBytes + kBarrierBytes;
+  static constexpr uint32_t kTmemCols = (NACC * BN <= 32)    ? 32
+                                        : (NACC * BN <= 64)  ? 64
+                                        : (NACC * BN <= 128) ? 128
+                                        : (NACC * BN <= 256) ? 256
+                                                             : 512;
+  static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
+  static_assert(kBytes <= 232448, "shared memory budget exceeded");
+};
+
+// Bounded pause used where a CTA cannot observe its own in-flight loads (the odd CTA's
+// loads complete on the even CTA's barrier): long enough for any issued TMA to land.
+__device__ __forceinline__ void settle_inflight_loads() {
+  const unsigned long long start = global_timer_ns();
+  while (global_timer_ns() - start < 200000ull) {
+  }
+}
+
+template <int BN, int NSTAGE, int NACC, int G, int CLUSTER_N, class Epi>
+__global__ void __launch_bounds__(gemm_threads(G), 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmO1, const __grid_constant__ CUtensorMap tmO2,
+                     const DensePairSched sched, const typename Epi::Params ep, const int kblocks,
+                     int* err) {
+  using L = GemmPairSmem<BN, NSTAGE, NACC, Epi>;
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "invalid pair MMA N");
+  static_assert(NACC * BN <= 512, "TMEM overflow");
+  static_assert(2 * CLUSTER_N <= 16, "cluster too large");
+  constexpr uint32_t kEpiThreads = 128 * G;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint32_t base = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  base += pad;
+
+  const uint32_t epi_base = base + L::kRingBytes;
+  const uint32_t bar_base = epi_base + L::kEpiBytes;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (NSTAGE + s); };
+  auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * NSTAGE + a); };
+  auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * NSTAGE + NACC + a); };
+  const uint32_t drain_bar = bar_base + 8u * (2 * NSTAGE + 2 * NACC);
+  const uint32_t epi_bar = drain_bar + 8u;
+  const uint32_t x_bar = drain_bar + 16u;
+  uint32_t* tmem_slot =
+      reinterpret_cast<uint32_t*>(smem + L::kRingBytes + L::kEpiBytes + L::kBarrierBytes - 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int half = static_cast<int>(rank & 1u);
+  const uint32_t even = rank & ~1u;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << even);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < NACC; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 2 * kEpiThreads);
+    }
+    mbar_init(drain_bar, 1);
+    mbar_init(epi_bar, Epi::bar_count(ep, G));
+    mbar_init(x_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  // The prologue above may overlap the previous kernel of the stream; no global memory is
+  // read or written before that kernel has completed.
+  grid_dependency_wait();
+  grid_launch_dependents();
+
+  const int first = static_cast<int>(blockIdx.x >> 1);
+  const int stride = static_cast<int>(gridDim.x >> 1);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool x_issued = false;
+      const int ntiles = sched.count();
+      for (int t = first; t < ntiles && ok; t += stride) {
+        const TileCoord tc = sched.coord(t, half);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u)) {
+            record_error(err, kErrTimeoutProducer);
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + stage * L::kStageBytes;
+          const uint32_t sb = sa + L::kABytes;
+          const uint32_t full_even = mapa_shared(full_bar(stage), even);
+          if (half == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * L::kStageBytes);
+          tma_load_2d_pair(sa, &tmA, full_even, kb * kBK, tc.a_row);
+          tma_load_2d_pair(sb, &tmB, full_even, kb * kBK, tc.b_row);
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (kb == 0 && !x_issued && Epi::prefetch(ep, tc, &tmO1, epi_base, x_bar)) x_issued = true;
+        }
+      }
+      if (!ok) {
+        // Let every load already issued land before the CTA can retire.
+        if (half == 0) {
+          for (int s = 0; s < NSTAGE; ++s) {
+            if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_phase >> s) & 1u);
+          }
+        } else {
+          settle_inflight_loads();
+        }
+        if (x_issued) mbar_wait(x_bar, 0);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && half == 0) {
+      constexpr uint32_t idesc = idesc_bf16(2 * kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      const int ntiles = sched.count();
+      for (int t = first; t < ntiles && ok; t += stride) {
+        if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1u)) {
+          record_error(err, kErrTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_cluster(full_bar(stage), phase)) {
+            record_error(err, kErrTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * L::kStageBytes;
+          const uint64_t adesc = sdesc_k128(sa);
+          const uint64_t bdesc = sdesc_k128(sa + L::kABytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_bf16_pair(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair_mc(empty_bar(stage), pair_mask);
+          if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(tfull_bar(acc), pair_mask);
+        if (++acc == NACC) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA issued by this thread must finish before either CTA releases TMEM or
+      // shared memory.
+      umma_commit_pair(drain_bar);
+      if (!mbar_wait(drain_bar, 0)) record_error(err, kErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    EpiThread et;
+    et.r = quarter * 32 + lane;
+    et.g = (warp - 2) >> 2;
+    et.tid = threadIdx.x - 64;
+    EpiCtx ctx;
+    ctx.smem = epi_base;
+    ctx.smem_ptr = smem + L::kRingBytes;
+    ctx.ring = base;
+    ctx.epi_bar = epi_bar;
+    ctx.x_bar = x_bar;
+    ctx.tmO1 = &tmO1;
+    ctx.tmO2 = &tmO2;
+    ctx.err = err;
+    ctx.tempty_remote = true;
+    ctx.rank_base = half;
+    ctx.rank_stride = 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int iter = 0;
+    const int ntiles = sched.count();
+    for (int t = first; t < ntiles; t += stride, ++iter) {
+      const TileCoord tc = sched.coord(t, half);
+      if (!mbar_wait_cluster(tfull_bar(acc), acc_phase)) {
+        record_error(err, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      et.taddr =
+          tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      ctx.iter = iter;
+      ctx.tempty_bar = mapa_shared(tempty_bar(acc), even);
+      Epi::template run<G>(ep, tc, et, ctx);
+      if (++acc == NACC) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (et.tid == 0) bulk_wait_all();  // bulk stores read shared memory until complete
+  }
+
+  __syncthreads();
+  // Both CTAs are done with the pair's shared memory and tensor memory (the even CTA's
+  // MMAs drained above) before either releases them.
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, L::kTmemCols);
   }
 }
 
@@ -751,7 +1035,7 @@ struct EpiStoreBF16 {
     release_accumulator(ctx);
     fence_proxy_async_smem();
     epi_bar_sync<G>();
-    if (et.tid == 0) store_staged(ctx.tmO1, ctx.smem, BN, n0, tc.out_row);
+    if (et.tid == 0 && tc.rows > 0) store_staged(ctx.tmO1, ctx.smem, BN, n0, tc.out_row);
     (void)p;
   }
 };
@@ -807,7 +1091,7 @@ struct EpiSwiGLU {
     release_accumulator(ctx);
     fence_proxy_async_smem();
     epi_bar_sync<G>();
-    if (et.tid == 0) {
+    if (et.tid == 0 && tc.rows > 0) {
       if constexpr (MX) {
         store_staged_u8(ctx.tmO1, ctx.smem, HC, tc.n_tile * HC, tc.out_row);
       } else {
@@ -906,15 +1190,19 @@ struct EpiResNorm {
     release_accumulator(ctx);
     fence_proxy_async_smem();
     epi_bar_sync<G>();
-    if (et.tid == 0) store_staged(ctx.tmO1, xs, BN, n0, tc.out_row);
+    if (et.tid == 0 && tc.rows > 0) store_staged(ctx.tmO1, xs, BN, n0, tc.out_row);
     if (p.norm_w == nullptr || !ok) return;
 
     // Push this (slice, group) partial to every CTA of the cluster, then collect.
     if (active) {
       const uint32_t rank = static_cast<uint32_t>(tc.n_tile);
       const uint32_t slot = smem_u32(&recv[(rank * kGroups + et.g) * kBM + et.r]);
-      for (int k = 0; k < p.cluster_n; ++k) st_cluster_f32(mapa_shared(slot, k), ss);
-      for (int k = 0; k < p.cluster_n; ++k) mbar_arrive_remote(mapa_shared(ctx.epi_bar, k));
+      for (int k = 0; k < p.cluster_n; ++k) {
+        st_cluster_f32(mapa_shared(slot, ctx.rank_base + ctx.rank_stride * k), ss);
+      }
+      for (int k = 0; k < p.cluster_n; ++k) {
+        mbar_arrive_remote(mapa_shared(ctx.epi_bar, ctx.rank_base + ctx.rank_stride * k));
+      }
     }
     if (!mbar_wait_cluster(ctx.epi_bar, 0)) {
       record_error(ctx.err, kErrTimeoutCluster);
@@ -949,7 +1237,7 @@ struct EpiResNorm {
     }
     fence_proxy_async_smem();
     epi_bar_sync<G>();
-    if (et.tid == 0) {
+    if (et.tid == 0 && tc.rows > 0) {
       if constexpr (MX) {
         store_staged_u8(ctx.tmO2, ctx.ring, BN, n0, tc.out_row);
       } else {
@@ -978,6 +1266,13 @@ struct EpiHeads {
     int policy_storage;         // 1888 (start of the wdl block)
     int n_total;                // policy_storage + 64
     int wdl_probs;
+    // Optional RMSNorm row scale folded out of the A operand (persistent forward): A is the
+    // residual stream x, the weights carry the final norm weight, and each row's logits
+    // are bf16(acc * rsqrt(sum(ss[row, :ss_parts]) / d + eps) + bias).
+    const float* ss = nullptr;
+    int ss_parts = 0;
+    float d = 0.0f;
+    float eps = 0.0f;
   };
   __device__ static uint32_t bar_count(const Params&, int) { return 1; }
   __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
@@ -992,14 +1287,26 @@ struct EpiHeads {
     const int row0 = tc.out_row + (et.r & ~31);  // first row of this warp's 32 rows
     float* tbuf = reinterpret_cast<float*>(ctx.smem_ptr) + (et.tid >> 5) * 32 * kPitch;
     const int n0 = tc.n_tile * BN;
+    float scale = 1.0f;
+    if (p.ss != nullptr) {
+      const float* ss = p.ss + static_cast<size_t>(tc.out_row + et.r) * p.ss_parts;
+      float total = 0.0f;
+      for (int q = 0; q < p.ss_parts; ++q) total += ss[q];
+      scale = 1.0f / sqrtf(total / p.d + p.eps);
+    }
     for (int c = et.g * 32; c < BN; c += G * 32) {
       const int c0 = n0 + c;
       if (c0 >= p.n_total) break;  // uniform across the warp
       float v[32], b[32];
       load_acc32(et.taddr + c, v);
       load_bf16<32>(p.bias + c0, b);  // bias is padded to a multiple of 32 columns
+      if (p.ss != nullptr) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
+        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(__fmul_rn(v[j], scale), b[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
+      }
       round_bf16_inplace(v);
       const int row = tc.out_row + et.r;
       const bool valid = et.r < tc.rows;

@@ -1,10 +1,13 @@
 // Host launchers for the tcgen05 GEMM instantiations used by the forward path, plus the
 // TMA tensor-map helper.
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <set>
 #include <utility>
 
+#include "forward.cuh"
 #include "gemm.cuh"
 #include "internal.h"
 
@@ -46,6 +49,35 @@ void ensure_smem(K kernel, int bytes) {
   check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
              "cudaFuncSetAttribute(max dynamic smem)");
   done.insert(key);
+}
+
+// Clusters of `cluster` CTAs of `kernel` that fit on the device at once (cached).
+template <class K>
+int max_active_clusters(K kernel, int threads, int smem, int cluster) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int>, int> cache;
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(kernel), cluster);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(cluster), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  check_cuda(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg), "cudaOccupancyMaxActiveClusters");
+  require(n >= 1, "no cluster of " + std::to_string(cluster) + " CTAs fits on this device");
+  cache.emplace(key, n);
+  return n;
 }
 
 template <class K, class... Args>
@@ -226,6 +258,8 @@ void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap
   DenseSched sched{m, hidden_dim / hc, ceil_div(m, kBM) * (hidden_dim / hc), hc, hidden_dim};
   const int grid = std::min(sched.num_tiles, sm_count());
   if (hc == 128) {
+    // Single-CTA tiles: measured as fast as CTA pairs here (the per-tile MMA rate is the
+    // same; the kernel's span is set by its prologue, first loads and last epilogue).
     constexpr int BN = 256, NS = 4, NA = 2;
     using Epi = EpiSwiGLU<128>;
     auto kernel = gemm_tc_kernel<BN, NS, NA, 2, kG, false, DenseSched, Epi>;
@@ -255,6 +289,38 @@ int resnorm_bn(int d) {
                                  " is not supported (multiple of 64, at most 2048)");
 }
 
+// CTA pairs with 256-column slices for the wide models (768, 1024: clusters of 6 and 8).
+// Narrower models keep single-CTA 128-column slices: the MMA rate per SM is set by the
+// slice width N (about 50 % of peak at N = 128, 68-71 % at N = 256, single CTA or pair
+// alike), and at d <= 512 a cluster of 2 * d / 128 CTAs would not all fit at once (15
+// clusters of 8 are resident at this shared-memory size) while 4-CTA clusters do.
+int resnorm_pair_bn(int d) {
+  if (d % 256 == 0 && d >= 768 && d / 256 <= 4) return 256;
+  return 0;
+}
+
+int resnorm_b_box(int d) {
+  const int pair_bn = resnorm_pair_bn(d);
+  return pair_bn != 0 ? pair_bn / 2 : resnorm_bn(d);
+}
+
+// CTA pairs: a cluster of 2 * cn CTAs covers 256 rows across the full width d; pair j
+// (ranks 2j, 2j+1) owns column slice j, each CTA 128 rows of it. One tile per CTA.
+template <int BN, int NS>
+static void gemm_resnorm_pair(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
+                              const CUtensorMap& tN, const bf16* bias, const bf16* norm_w, int m,
+                              int d, int k, float eps, cudaStream_t s) {
+  using Epi = EpiResNorm<BN>;
+  auto kernel = gemm_pair_kernel<BN, NS, 1, kG, 4, Epi>;
+  constexpr int smem = GemmPairSmem<BN, NS, 1, Epi>::kBytes;
+  ensure_smem(kernel, smem);
+  const int cn = d / BN;
+  DensePairSched ps{m, cn, ceil_div(m, 2 * kBM) * cn, BN, BN / 2, 0};
+  typename Epi::Params ep{bias, norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual, cn, eps};
+  launch(kernel, dim3(2 * ps.num_tiles), gemm_threads(kG), smem, 2 * cn, s, tA, tB, tX, tN, ps,
+         ep, ceil_div(k, kBK), device_error_word());
+}
+
 template <int BN, int NS>
 static void gemm_resnorm_bn(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
                             const CUtensorMap& tN, const bf16* bias, const bf16* norm_w, int m,
@@ -274,6 +340,10 @@ static void gemm_resnorm_bn(const CUtensorMap& tA, const CUtensorMap& tB, const 
 void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
                   const CUtensorMap& tN, const bf16* bias, const bf16* norm_w, int m, int d, int k,
                   float eps, cudaStream_t s) {
+  if (resnorm_pair_bn(d) == 256) {
+    gemm_resnorm_pair<256, 4>(tA, tB, tX, tN, bias, norm_w, m, d, k, eps, s);
+    return;
+  }
   switch (resnorm_bn(d)) {
     case 64: gemm_resnorm_bn<64, 7>(tA, tB, tX, tN, bias, norm_w, m, d, k, eps, s); break;
     case 128: gemm_resnorm_bn<128, 5>(tA, tB, tX, tN, bias, norm_w, m, d, k, eps, s); break;
@@ -281,10 +351,29 @@ void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMa
   }
 }
 
+// ------------------------------------------------------------------ persistent dense forward
+void dense_forward(const FwdParams& p, cudaStream_t s) {
+  require(p.total_tasks >= 1 && p.depth >= 1 && p.depth <= kFwdMaxDepth && p.ks >= 1 &&
+              p.ks <= p.kb_in && p.d % 128 == 0 && p.d / 128 <= kFwdMaxSlices && p.h % 128 == 0,
+          "persistent forward: unsupported shape");
+  auto kernel = dense_forward_kernel;
+  ensure_smem(kernel, FwdSmem::kBytes);
+  const int grid = std::min(sm_count(), p.total_tasks);
+  launch(kernel, dim3(grid), kFwdThreads, FwdSmem::kBytes, 0, s, p);
+}
+
 // ------------------------------------------------------------------ heads
 void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, float* policy,
                 float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,
                 int wdl_probs, cudaStream_t s) {
+  gemm_heads_scaled(tA, tB, bias, policy, wdl, moves_left, m, d, policy_size, policy_storage,
+                    wdl_probs, nullptr, 0, 0.0f, s);
+}
+
+void gemm_heads_scaled(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias,
+                       float* policy, float* wdl, float* moves_left, int m, int d,
+                       int policy_size, int policy_storage, int wdl_probs, const float* ss,
+                       int ss_parts, float eps, cudaStream_t s) {
   constexpr int BN = 256, NS = 3, NA = 2;
   using Epi = EpiHeads;
   auto kernel = gemm_tc_kernel<BN, NS, NA, 1, kG, false, DenseSched, Epi>;
@@ -294,6 +383,10 @@ void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, 
   DenseSched sched{m, ceil_div(n_total, BN), ceil_div(m, kBM) * ceil_div(n_total, BN), BN, 0};
   typename Epi::Params ep{bias, policy, wdl, moves_left, policy_size, policy_storage, n_total,
                           wdl_probs};
+  ep.ss = ss;
+  ep.ss_parts = ss_parts;
+  ep.d = static_cast<float>(d);
+  ep.eps = eps;
   const int grid = std::min(sched.num_tiles, sm_count());
   launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, null_map(), null_map(), sched,
          ep, ceil_div(d, kBK), device_error_word());

@@ -60,10 +60,15 @@ void gemm_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUtenso
 int swiglu_chunk(int hidden);  // 128 if hidden % 128 == 0, else 64
 void gemm_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH, int m,
                  int hidden_dim, int k, cudaStream_t s);
-// Residual/bias epilogue with optional fused RMSNorm; tB box rows must equal resnorm_bn(d).
+// Residual/bias epilogue with optional fused RMSNorm; tB box rows must equal resnorm_b_box(d).
 // tX is the residual stream x [M, d] (read for the residual mode, written), tN the
 // normalised output [M, d] (used when norm_w is set).
 int resnorm_bn(int d);
+// Persistent dense forward (input GEMM, all layers, RMSNorm passes) in one launch.
+struct FwdParams;
+void dense_forward(const FwdParams& p, cudaStream_t s);
+// Rows of the tB box that gemm_resnorm expects for width d (BN, or BN/2 on CTA pairs).
+int resnorm_b_box(int d);
 void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
                   const CUtensorMap& tN, const bf16* bias, const bf16* norm_w, int m, int d, int k,
                   float eps, cudaStream_t s);
@@ -71,6 +76,14 @@ void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMa
 void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, float* policy,
                 float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,
                 int wdl_probs, cudaStream_t s);
+// gemm_heads with the final RMSNorm folded out of A: A is x, the head weights carry the norm
+// weight, and each row is scaled by rsqrt(sum(ss[row, :ss_parts]) / d + eps) before the bias.
+void gemm_heads_scaled(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias,
+                       float* policy, float* wdl, float* moves_left, int m, int d,
+                       int policy_size, int policy_storage, int wdl_probs, const float* ss,
+                       int ss_parts, float eps, cudaStream_t s);
+// out[r, c] = bf16(W[r, c] * w[c]) for a row-major [rows, cols] BF16 matrix.
+void fold_columns(const bf16* W, const bf16* w, bf16* out, int64_t rows, int cols, cudaStream_t s);
 
 // ---------------------------------------------------------------- MoE
 // Router GEMM (A = normalised rows [T, d], B = router weight [64, d] with 64-row boxes)

@@ -17,6 +17,9 @@
 
 #include "internal.h"
 #include "model.h"
+
+#include "forward_types.h"
+
 #include "safetensors.h"
 
 namespace ce4b {
@@ -42,6 +45,8 @@ std::string shape_str(const std::vector<int64_t>& s) {
 Model::~Model() {
   if (device >= 0) cudaSetDevice(device);
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  if (fwd_dev) cudaFree(fwd_dev);
+  if (fwd_weights) cudaFree(fwd_weights);
   for (auto& slot : io)
     if (slot.free) cudaEventDestroy(slot.free);
   if (forward_done) cudaEventDestroy(forward_done);
@@ -121,6 +126,14 @@ void Model::plan_workspace() {
     ws_off.h_codes = take(r * dense_hidden);
     ws_off.h_scales = take(t * (dense_hidden / 128) * 512);
   }
+  if (fused) {
+    const size_t sj = static_cast<size_t>(d / 128);
+    const size_t nb = r / 128;
+    ws_off.fwd_ss = take(r * sj * kFwdG * 4);
+    ws_off.fwd_part = fwd_ks > 1 ? take(static_cast<size_t>(fwd_ks) * r * d * 4) : 0;
+    fwd_sync_bytes = (2 * nb + nb * sj + 1) * 4;
+    ws_off.fwd_sync = take(fwd_sync_bytes);
+  }
   if (cfg.arch == CE4B_ARCH_MOE64A2) {
     // Expert rows: 2 routes per token, each expert segment padded to 128 rows.
     perm_rows = static_cast<int>((2 * r + 64 * 127 + 127) / 128 * 128);
@@ -185,6 +198,9 @@ void Model::create(const ce4b_model_config& c, int dev, int maxb) {
   policy_storage = c.policy_storage_size;
   max_batch = maxb;
   rows_cap = (maxb + 127) / 128 * 128;
+  fused = c.arch == CE4B_ARCH_DENSE && !mx && c.d_model % 128 == 0 &&
+          c.d_model / 128 <= kFwdMaxSlices && dense_hidden % 128 == 0 && c.depth <= kFwdMaxDepth;
+  fwd_ks = 1;  // input GEMM tiles over the full 7168 (FP32 split partials cost more than they save)
   (void)resnorm_bn(c.d_model);  // validates width against the cluster limit
 
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
@@ -231,7 +247,7 @@ void Model::finalize() {
   tm_n = make_tmap_bf16(ws_n, rows_cap, d, d, 128);
   tm_x = make_tmap_bf16(workspace + ws_off.x, rows_cap, d, d, 128);
   tm_hidden = make_tmap_bf16(ws_hidden, rows_cap, dense_hidden, dense_hidden, 128);
-  const uint32_t bn = static_cast<uint32_t>(resnorm_bn(d));
+  const uint32_t bn = static_cast<uint32_t>(resnorm_b_box(d));
   tm_w_in = make_tmap_bf16(w("input.weight"), d, in_dim, in_dim, bn);
   tm_heads = make_tmap_bf16(w("policy.weight"), policy_storage + 64, d, d, 256);
   layers.clear();
@@ -259,6 +275,38 @@ void Model::finalize() {
     tm_xperm = make_tmap_bf16(workspace + ws_off.xperm, perm_rows, d, d, 128);
     tm_hperm = make_tmap_bf16(workspace + ws_off.hperm, perm_rows, expert_hidden, expert_hidden, 128);
     tm_yperm = make_tmap_bf16(workspace + ws_off.yperm, perm_rows, d, d, 128);
+  }
+  if (fused) {
+    // Norm-folded weights: gate_up of layer l times blocks.l.norm.weight, heads times
+    // final_norm.weight (column scaling, one BF16 rounding each).
+    const size_t gu_elems = static_cast<size_t>(2) * dense_hidden * d;
+    const size_t heads_rows = static_cast<size_t>(policy_storage) + 64;
+    if (fwd_weights == nullptr) {
+      check_cuda(cudaMalloc(&fwd_weights, (cfg.depth * gu_elems + heads_rows * d) * sizeof(bf16)),
+                 "cudaMalloc folded weights");
+    }
+    FwdMaps maps{};
+    maps.a_in = make_tmap_bf16(ws_a_in, rows_cap, in_dim, in_dim, 128);
+    maps.x = make_tmap_bf16(workspace + ws_off.x, rows_cap, d, d, 128);
+    maps.hidden = make_tmap_bf16(ws_hidden, rows_cap, dense_hidden, dense_hidden, 128);
+    maps.w_in = make_tmap_bf16(w("input.weight"), d, in_dim, in_dim, 128);
+    for (int l = 0; l < cfg.depth; ++l) {
+      const std::string p = "blocks." + std::to_string(l);
+      bf16* gu = fwd_weights + l * gu_elems;
+      fold_columns(w(p + ".gate_up.weight"), w(p + ".norm.weight"), gu, 2 * dense_hidden, d, stream);
+      maps.gate_up[l] = make_tmap_bf16(gu, 2 * dense_hidden, d, d, 128);
+      maps.down[l] = make_tmap_bf16(w(p + ".down.weight"), d, dense_hidden, dense_hidden, 128);
+    }
+    bf16* heads = fwd_weights + cfg.depth * gu_elems;
+    fold_columns(w("policy.weight"), w("final_norm.weight"), heads, static_cast<int64_t>(heads_rows), d,
+                 stream);
+    tm_heads_folded = make_tmap_bf16(heads, heads_rows, d, d, 256);
+    check_cuda(cudaStreamSynchronize(stream), "fold norm weights");
+    if (fwd_dev == nullptr) {
+      check_cuda(cudaMalloc(&fwd_dev, sizeof(FwdMaps)), "cudaMalloc forward tensor maps");
+    }
+    check_cuda(cudaMemcpy(fwd_dev, &maps, sizeof(FwdMaps), cudaMemcpyHostToDevice),
+               "copy forward tensor maps");
   }
   if (mx) quantize_weights();
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
@@ -352,6 +400,51 @@ void Model::forward_mx(int layout, void* input, const void* scalars, int batch, 
   trace("heads", s);
 }
 
+// Dense BF16 tower as one persistent kernel between the plane expansion and the heads.
+void Model::forward_fused(int layout, void* input, const void* scalars, int batch, float* policy,
+                          float* wdl, float* moves_left, int wdl_probs, int write_back,
+                          cudaStream_t s) {
+  const int d = cfg.d_model;
+  auto* sync = reinterpret_cast<int*>(workspace + ws_off.fwd_sync);
+  // Counters restart from zero every forward (before the expansion, so that the
+  // persistent kernel's predecessor in the stream is a kernel).
+  check_cuda(cudaMemsetAsync(sync, 0, fwd_sync_bytes, s), "reset forward counters");
+  expand_input(layout, input, scalars, batch, cfg.history_length,
+               reinterpret_cast<bf16*>(workspace + ws_off.a_in), write_back, s);
+  trace("expand_planes", s);
+  const int nb_cap = rows_cap / 128;
+  FwdParams p{};
+  p.maps = reinterpret_cast<const FwdMaps*>(fwd_dev);
+  p.bias = w("input.bias");
+  p.x = reinterpret_cast<bf16*>(workspace + ws_off.x);
+  p.hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);
+  p.ss = reinterpret_cast<float*>(workspace + ws_off.fwd_ss);
+  p.part = fwd_ks > 1 ? reinterpret_cast<float*>(workspace + ws_off.fwd_part) : nullptr;
+  p.sj = d / 128;
+  p.hid_cnt = sync;
+  p.slice_cnt = sync + nb_cap;
+  p.part_cnt = sync + 2 * nb_cap;
+  p.task_counter = sync + 2 * nb_cap + nb_cap * p.sj;
+  p.err = device_error_word();
+  p.rows_cap = rows_cap;
+  p.nb = (batch + 127) / 128;
+  p.d = d;
+  p.h = dense_hidden;
+  p.depth = cfg.depth;
+  p.nc = dense_hidden / 128;
+  p.ks = fwd_ks;
+  p.kb_in = in_dim / kFwdKBlock;
+  p.total_tasks = fused_task_count(batch);
+  p.eps = cfg.rms_norm_eps;
+  p.trace = fwd_trace;
+  p.trace_cap = fwd_trace_cap;
+  dense_forward(p, s);
+  trace("dense_tower", s);
+  gemm_heads_scaled(tm_x, tm_heads_folded, w("policy.bias"), policy, wdl, moves_left, batch, d,
+                    policy_size, policy_storage, wdl_probs, p.ss, p.sj * kFwdG, cfg.rms_norm_eps, s);
+  trace("heads", s);
+}
+
 void Model::forward(int layout, void* input, const void* scalars, int batch, float* policy,
                     float* wdl, float* moves_left, int wdl_probs, int normalize_in_place,
                     int32_t* tokens_per_expert, cudaStream_t s) {
@@ -368,6 +461,10 @@ void Model::forward(int layout, void* input, const void* scalars, int batch, flo
 
   trace_next = 0;
   trace_labels.clear();
+  if (fused) {
+    forward_fused(layout, input, scalars, batch, policy, wdl, moves_left, wdl_probs, write_back, s);
+    return;
+  }
   if (mx) {
     forward_mx(layout, input, scalars, batch, policy, wdl, moves_left, wdl_probs, write_back, s);
     return;

@@ -34,6 +34,7 @@ struct Model {
     size_t expert_start = 0, m_tiles = 0, num_m_tiles = 0, xperm = 0, pprob = 0, hperm = 0;
     size_t yperm = 0;
     size_t a_codes = 0, a_scales = 0, n_codes = 0, n_scales = 0, h_codes = 0, h_scales = 0;
+    size_t fwd_ss = 0, fwd_part = 0, fwd_sync = 0;  // persistent dense forward
   };
 
   ce4b_model_config cfg{};
@@ -53,6 +54,20 @@ struct Model {
   std::map<std::string, Slot> slots;
   uint8_t* workspace = nullptr;
   bool mx = false;                // precision MXFP8
+  // Dense BF16 towers run as one persistent kernel (forward.cuh): its tensor maps and
+  // norm-weight table live in fwd_dev; fwd_ks = k splits of the input GEMM.
+  bool fused = false;
+  int fwd_ks = 1;
+  uint8_t* fwd_dev = nullptr;      // FwdMaps
+  bf16* fwd_weights = nullptr;     // norm-folded gate_up [depth][2h, d], then heads [Ps + 64, d]
+  CUtensorMap tm_heads_folded{};
+  size_t fwd_sync_bytes = 0;
+  unsigned long long* fwd_trace = nullptr;  // optional per-task timeline (device buffer)
+  int fwd_trace_cap = 0;
+  int fused_task_count(int batch) const {
+    const int nb = (batch + 127) / 128, sj = cfg.d_model / 128, nc = dense_hidden / 128;
+    return nb * sj * fwd_ks + cfg.depth * nb * (nc + sj);
+  }
   uint8_t* mx_arena = nullptr;    // quantised weights (codes + scales)
   size_t mx_arena_bytes = 0;
   const uint8_t* w_in_scales = nullptr;
@@ -111,6 +126,8 @@ struct Model {
   void quantize_weights();
   void forward_mx(int layout, void* input, const void* scalars, int batch, float* policy,
                   float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s);
+  void forward_fused(int layout, void* input, const void* scalars, int batch, float* policy,
+                     float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s);
   void moe_layer(const Layer& L, int moe_index, const bf16* next_norm, int batch,
                  int32_t* tokens_per_expert, cudaStream_t s);
 

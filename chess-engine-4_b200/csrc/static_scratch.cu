@@ -97,7 +97,7 @@ extern "C" int ce4b_dense_block_forward_static(const void* x_dev, const void* no
                                cudaMemcpyDeviceToDevice, s),
                "copy residual");
     const CUtensorMap t_down = make_tmap_bf16(down_weight_dev, d_model, hidden_dim, hidden_dim,
-                                              static_cast<uint32_t>(resnorm_bn(d_model)));
+                                              static_cast<uint32_t>(resnorm_b_box(d_model)));
     const CUtensorMap t_out = make_tmap_bf16(out_dev, rows, d_model, d_model, 128);
     gemm_resnorm(t_hidden, t_down, t_out, t_out, nullptr, nullptr, rows, d_model, hidden_dim, eps, s);
     return CE4B_OK;

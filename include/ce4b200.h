@@ -162,6 +162,20 @@ int ce4b_model_evaluate_async(ce4b_model* model, const ce4b_input_plane* host_pl
  * events[i] (cudaEvent_t) on its stream after its i-th kernel; count 0 disables.
  * ce4b_model_trace_label names kernel i of the last traced forward. */
 int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count);
+/* Per-task timeline of the persistent dense forward (dense BF16 models). With
+ * capacity_tasks > 0, each forward writes 12 uint64 per task id < capacity_tasks into the
+ * device buffer: %globaltimer ns when the task was fetched, its inputs were ready, its
+ * last load was issued, its first MMA was issued, its accumulator was committed, its
+ * epilogue started and finished, its epilogue results were stored and published, and
+ * (last slice of a row block) its RMSNorm pass finished; then the CTA index and one
+ * unused word. 0 disables. Task ids are numbered
+ * input-GEMM tiles first (row block, slice, k split), then per layer the gate_up tiles
+ * (row block, hidden chunk) and the down tiles (row block, slice).
+ * ce4b_model_task_count gives the number of tasks of a forward at `batch` (0 when the
+ * model does not use the persistent forward). */
+int ce4b_model_set_task_trace(ce4b_model* model, void* device_buffer, int capacity_tasks);
+int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks);
+
 int ce4b_model_trace_label(const ce4b_model* model, int index, char* buffer, int buffer_len);
 
 void ce4b_model_destroy(ce4b_model* model);

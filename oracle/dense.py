@@ -73,13 +73,22 @@ def forward(
     mode: str = "fp32",
     moe_layers: frozenset[int] = frozenset(),
     moe_forward=None,
+    fold_norm: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Returns (policy_logits [B,1858], wdl_logits [B,3], moves_left [B]) in float32.
 
-    ``moe_layers`` / ``moe_forward`` let oracle.moe reuse this tower for moe64a2."""
+    ``moe_layers`` / ``moe_forward`` let oracle.moe reuse this tower for moe64a2.
+
+    ``fold_norm`` (bf16 mode, dense only) restates the arithmetic of libce4b200's
+    persistent dense forward instead of the reference's rounding points: each RMSNorm
+    weight is folded into the next linear's weight, W' = bf16(W * diag(w)), and the row
+    scale r = rsqrt(mean(x^2) + eps) multiplies the FP32 product, so the normalised row
+    is never rounded: gate/up = bf16(r * (x W'^T)), heads = bf16(r * (x W'_h^T) + b)."""
 
     if mode not in ("fp32", "bf16", "mxfp8"):
         raise ValueError(mode)
+    if fold_norm and (mode != "bf16" or moe_layers):
+        raise ValueError("fold_norm restates the dense BF16 persistent forward only")
     rnd = _bf16 if mode in ("bf16", "mxfp8") else (lambda t: t)
     # MXFP8 (all linears, recipe of the reference's custom path): both GEMM operands are
     # MXFP8 round trips of their BF16 values; everything else is the BF16 forward.
@@ -93,15 +102,23 @@ def forward(
             assert moe_forward is not None
             x = moe_forward(x, layer, mode)
             continue
-        n = rnd(_rmsnorm(x, f[f"{p}.norm.weight"], eps))
-        gu = q(n) @ q(f[f"{p}.gate_up.weight"]).T
+        if fold_norm:
+            r = torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + eps)
+            gu = (x @ _bf16(f[f"{p}.gate_up.weight"] * f[f"{p}.norm.weight"]).T) * r
+        else:
+            n = rnd(_rmsnorm(x, f[f"{p}.norm.weight"], eps))
+            gu = q(n) @ q(f[f"{p}.gate_up.weight"]).T
         h = gu.shape[1] // 2
         g, u = rnd(gu[:, :h]), rnd(gu[:, h:])
         hidden = rnd(g / (1.0 + torch.exp(-g)) * u)
         x = rnd(x + rnd(q(hidden) @ q(f[f"{p}.down.weight"]).T))
-    n = q(rnd(_rmsnorm(x, f["final_norm.weight"], eps)))
     heads = torch.cat([f["policy.weight"], f["wdl.weight"], f["moves_left.weight"]])
-    logits = n @ q(heads).T
+    if fold_norm:
+        r = torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + eps)
+        logits = (x @ _bf16(heads * f["final_norm.weight"]).T) * r
+    else:
+        n = q(rnd(_rmsnorm(x, f["final_norm.weight"], eps)))
+        logits = n @ q(heads).T
     ps = f["policy.weight"].shape[0]
     policy = rnd(logits[:, :POLICY_SIZE] + f["policy.bias"][:POLICY_SIZE])
     wdl = rnd(logits[:, ps : ps + 3] + f["wdl.bias"][:3])
