@@ -1,5 +1,6 @@
 // Memory-bound kernels around the GEMMs: input-plane expansion (three input layouts),
 // standalone RMSNorm / SwiGLU / residual add for the kernel-op API.
+#include <algorithm>
 #include "internal.h"
 #include "mxfp8.cuh"
 #include "ptx.cuh"
@@ -14,17 +15,17 @@ __device__ __forceinline__ int source_plane(int p, int history_planes) {
   return p < history_planes ? p : kHistoryPlanes + (p - history_planes);
 }
 
-// One thread = 8 squares (one 16-byte BF16 chunk) of one selected plane.
+// Blocks take positions; a thread writes 8 squares (one 16-byte BF16 chunk) of one selected
+// plane (32-bit in-position indexing; consecutive threads write consecutive chunks).
 __global__ void expand_lc0_kernel(const ce4b_input_plane* __restrict__ planes, bf16* __restrict__ out,
                                   int batch, int history) {
   const int sel = selected_planes(history);
   const int hp = history * kPlanesPerHistory;
-  const int64_t chunks = static_cast<int64_t>(batch) * sel * 8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int chunk = static_cast<int>(i % 8);
-    const int p = static_cast<int>((i / 8) % sel);
-    const int64_t b = i / (8 * sel);
+  for (int64_t b = blockIdx.x; b < batch; b += gridDim.x)
+  for (int c = threadIdx.x; c < sel * 8; c += blockDim.x) {
+    const int chunk = c & 7;
+    const int p = c >> 3;
+    const int64_t i = b * sel * 8 + c;
     const ce4b_input_plane pl = planes[b * kInputPlanes + source_plane(p, hp)];
     float v = pl.value;
     if (p == hp + 5) v = v / 99.0f;
@@ -47,12 +48,11 @@ __global__ void expand_dense_kernel(T* __restrict__ planes, bf16* __restrict__ o
                                     int history, int write_back) {
   const int sel = selected_planes(history);
   const int hp = history * kPlanesPerHistory;
-  const int64_t chunks = static_cast<int64_t>(batch) * sel * 8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int chunk = static_cast<int>(i % 8);
-    const int p = static_cast<int>((i / 8) % sel);
-    const int64_t b = i / (8 * sel);
+  for (int64_t b = blockIdx.x; b < batch; b += gridDim.x)
+  for (int c = threadIdx.x; c < sel * 8; c += blockDim.x) {
+    const int chunk = c & 7;
+    const int p = c >> 3;
+    const int64_t i = b * sel * 8 + c;
     const int src = source_plane(p, hp);
     T* in = planes + (b * kInputPlanes + src) * 64 + chunk * 8;
     float f[8];
@@ -94,12 +94,11 @@ __global__ void expand_packed_kernel(const uint8_t* __restrict__ packed, const S
                                      bf16* __restrict__ out, int batch, int history) {
   const int sel = selected_planes(history);
   const int hp = history * kPlanesPerHistory;
-  const int64_t chunks = static_cast<int64_t>(batch) * sel * 8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int chunk = static_cast<int>(i % 8);
-    const int p = static_cast<int>((i / 8) % sel);
-    const int64_t b = i / (8 * sel);
+  for (int64_t b = blockIdx.x; b < batch; b += gridDim.x)
+  for (int c = threadIdx.x; c < sel * 8; c += blockDim.x) {
+    const int chunk = c & 7;
+    const int p = c >> 3;
+    const int64_t i = b * sel * 8 + c;
     const int src = source_plane(p, hp);
     float f[8];
     if (src < kHistoryPlanes) {
@@ -261,9 +260,8 @@ int grid_for(int64_t work, int threads) {
 
 void expand_input(int layout, const void* input, const void* scalars, int batch, int history,
                   bf16* out, int write_back_rule50, cudaStream_t s) {
-  const int64_t chunks = static_cast<int64_t>(batch) * selected_planes(history) * 8;
   const int threads = 256;
-  const int grid = grid_for(chunks, threads);
+  const int grid = std::max(1, std::min(batch, sm_count() * 16));
   switch (layout) {
     case CE4B_INPUT_LC0:
       expand_lc0_kernel<<<grid, threads, 0, s>>>(static_cast<const ce4b_input_plane*>(input), out,
