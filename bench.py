@@ -145,43 +145,10 @@ def peaks() -> dict:
 
 # ---------------------------------------------------------------- distributed plumbing
 def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
+    from ce4b200 import replicas
 
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group(
-            "nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local)
-        )
-    return world, rank, local
-
-
-def barrier(world: int) -> None:
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-
-
-def max_over_ranks(value: float, world: int) -> float:
-    if world == 1:
-        return value
-    import torch.distributed as dist
-
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
-def dist_teardown(world: int) -> None:
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+    group = replicas.init_from_env()
+    return group, group.world, group.rank, group.local_rank
 
 
 # ---------------------------------------------------------------- clocks
@@ -398,7 +365,7 @@ def make_model(cfg: Config, device: int, batch: int):
 def run_ours(args: argparse.Namespace, cfg: Config) -> None:
     from ce4b200 import _lib, synthetic
 
-    world, rank, local = dist_setup()
+    group, world, rank, local = dist_setup()
     device = local
     torch.cuda.set_device(device)
     batch = cfg.per_gpu(world)
@@ -448,7 +415,7 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
             forward()
             flush.zero_()
         stream.synchronize()
-        barrier(world)
+        group.barrier()
         torch.cuda.synchronize()
 
         # Timed pass: events only at step boundaries. (An event recorded between two kernels
@@ -500,9 +467,9 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
             kernel_ms[name] = kernel_ms.get(name, 0.0) + dt / trace_steps
             if i in dom_idx:
                 dom_ms.append(dt)
-    barrier(world)
+    group.barrier()
     total_ms = sum(step_ms)
-    slowest_ms = max_over_ranks(total_ms, world)
+    slowest_ms = group.max(total_ms)
     value = world * batch * args.steps / (slowest_ms / 1000.0)
     clocks = sampler.summary() if sampler else None
 
@@ -526,7 +493,7 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
         for i in range(max(4, args.warmup)):  # builds the graph of both I/O slots
             evaluate(batch, i)
         torch.cuda.synchronize(device)
-        barrier(world)
+        group.barrier()
         torch.cuda.synchronize(device)
         # Pipelined: calls alternate over two streams, back to back, as a serving loop
         # issues them; the H2D of each call and the D2H of the one before it overlap a
@@ -554,8 +521,8 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
                 s1.record(stream)
                 s1.synchronize()
                 serial_ms += s0.elapsed_time(s1)
-        e2e_slowest = max_over_ranks(e2e_ms, world)
-        serial_slowest = max_over_ranks(serial_ms, world)
+        e2e_slowest = group.max(e2e_ms)
+        serial_slowest = group.max(serial_ms)
         # Bytes one step touches: weights, planes in, expanded input operand, activations,
         # FP32 outputs. Back-to-back steps are only reported when that exceeds L2.
         info = _lib.ModelInfoStruct()
@@ -669,7 +636,7 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    dist_teardown(world)
+    group.close()
 
 
 def main() -> None:
