@@ -127,6 +127,9 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--config", choices=sorted(CONFIGS), default="c1")
     p.add_argument("--batch", type=int, default=0, help="override the per-GPU batch")
     p.add_argument("--quick", action="store_true", help="skip e2e, latency, clocks and CPU baseline (profiling)")
+    p.add_argument("--ep", action="store_true",
+                   help="moe64a2 under torchrun: split the 64 experts over the ranks (NCCL all-to-all of routed "
+                        "rows) instead of replicating them")
     return p.parse_args()
 
 
@@ -370,6 +373,14 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
     torch.cuda.set_device(device)
     batch = cfg.per_gpu(world)
     lib, handle = make_model(cfg, device, batch)
+    expert_parallel = args.ep and cfg.arch == "moe64a2" and world > 1
+    if expert_parallel:
+        import torch.distributed as dist
+
+        box = [_lib.nccl_unique_id() if rank == 0 else b""]
+        dist.broadcast_object_list(box, src=0)
+        uid = ctypes.create_string_buffer(box[0], 128)
+        _lib.check(lib.ce4b_model_enable_expert_parallel(handle, rank, world, uid))
     stream = torch.cuda.Stream(device)
     sptr = stream.cuda_stream
 
@@ -603,7 +614,9 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
                 "workload": cfg.workload,
                 "global_batch": batch * world,
                 "per_gpu_batch": batch,
-                "parallelism": f"replicas x{world} (no collective)",
+                "parallelism": (f"expert parallel x{world} ({64 // world} experts per GPU, NCCL send/recv of "
+                                "routed rows; dense layers data-parallel)") if expert_parallel else
+                               f"replicas x{world} (no collective)",
                 "l2": "flushed between timed steps (256 MiB write, untimed)",
                 "input_layout": "lc0 InputPlane records resident in HBM",
             },

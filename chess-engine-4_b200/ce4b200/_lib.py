@@ -106,6 +106,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ce4b_model_evaluate_async": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "ce4b_model_set_trace": (_i32, [_vp, _vp, _i32]),
     "ce4b_model_set_task_trace": (_i32, [_vp, _vp, _i32]),
+    "ce4b_nccl_unique_id": (_i32, [_vp, _i32]),
+    "ce4b_model_enable_expert_parallel": (_i32, [_vp, _i32, _i32, _vp]),
+    "ce4b_expert_parallel_plan": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32, ctypes.POINTER(_i32)]),
     "ce4b_model_task_count": (_i32, [_vp, _i32, ctypes.POINTER(_i32)]),
     "ce4b_model_trace_label": (_i32, [_vp, _i32, ctypes.c_char_p, _i32]),
     "ce4b_model_destroy": (None, [_vp]),
@@ -170,6 +173,14 @@ def check(status: int) -> None:
     if status == CE4B_ERR_IO:
         raise OSError(message)
     raise Ce4bError(status, message)
+
+
+def nccl_unique_id() -> bytes:
+    """128-byte NCCL unique id for ce4b_model_enable_expert_parallel (made by rank 0)."""
+
+    buf = ctypes.create_string_buffer(128)
+    check(library().ce4b_nccl_unique_id(buf, 128))
+    return buf.raw
 
 
 def check_device_error(device: int) -> int:

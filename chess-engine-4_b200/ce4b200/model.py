@@ -430,6 +430,12 @@ class _NativeModel:
         )
         return policy, wdl, moves_left
 
+    def enable_expert_parallel(self, rank: int, world: int, unique_id: bytes) -> None:
+        if len(unique_id) != 128:
+            raise ValueError("the NCCL unique id has 128 bytes")
+        buf = ctypes.create_string_buffer(unique_id, 128)
+        _lib.check(self.lib.ce4b_model_enable_expert_parallel(self.handle, rank, world, buf))
+
     def __del__(self) -> None:
         handle = getattr(self, "handle", None)
         if handle is not None and handle.value:
@@ -469,6 +475,11 @@ class _NativeForwardMixin(nn.Module):
         engine: _NativeModel | None = self.__dict__.get("_native")
         index = device.index if device.index is not None else torch.cuda.current_device()
         if engine is None or engine.device != index or engine.max_batch < batch:
+            if self.__dict__.get("_ep") is not None:
+                raise ValueError(
+                    f"expert-parallel model: batch {batch} on cuda:{index} exceeds the engine "
+                    "given to enable_expert_parallel"
+                )
             capacity = max(batch, engine.max_batch if engine is not None else 0)
             capacity = (capacity + 255) // 256 * 256
             self.__dict__["_native"] = None
@@ -654,6 +665,38 @@ class Moe64A2ChessNet(_NativeForwardMixin):
         self.policy_head = Linear(config.d_model, mxfp8_aligned_size(POLICY_SIZE))
         self.wdl_head = Linear(config.d_model, 32)
         self.moves_left_head = Linear(config.d_model, 32)
+
+    def enable_expert_parallel(
+        self,
+        *,
+        max_batch: int,
+        device: int | None = None,
+        rank: int | None = None,
+        world: int | None = None,
+        unique_id: bytes | None = None,
+    ) -> None:
+        """Splits the 64 experts over the ranks (64 / world consecutive experts each): every
+        MoE layer sends each routed row to its expert's rank and back with NCCL. Collective:
+        every rank calls it, each with its own GPU. rank / world default to the
+        torch.distributed default group, which also carries rank 0's NCCL unique id to the
+        others. Later forwards take this rank's positions (at most ``max_batch``) and return
+        their outputs, equal to the single-GPU forward's."""
+
+        if rank is None or world is None:
+            import torch.distributed as dist
+
+            rank, world = dist.get_rank(), dist.get_world_size()
+        if unique_id is None:
+            import torch.distributed as dist
+
+            box = [_lib.nccl_unique_id() if rank == 0 else b""]
+            dist.broadcast_object_list(box, src=0)
+            unique_id = box[0]
+        index = device if device is not None else torch.cuda.current_device()
+        self.__dict__["_ep"] = None
+        engine = self._engine(max_batch, torch.device("cuda", index))
+        engine.enable_expert_parallel(rank, world, unique_id)
+        self.__dict__["_ep"] = (rank, world)
 
     def safetensors_tensors(self) -> dict[str, torch.Tensor]:
         """Weights under the Safetensors v1 names (src/chess_engine_4/release/export.py:96-188)."""

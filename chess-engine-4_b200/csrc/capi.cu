@@ -6,8 +6,11 @@
 #include <string>
 #include <vector>
 
+#include <cstring>
+
 #include "internal.h"
 #include "model.h"
+#include "nccl_dl.h"
 
 namespace ce4b {
 
@@ -202,6 +205,40 @@ int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count) {
     require(count >= 0 && (count == 0 || events != nullptr), "bad trace event array");
     model->impl->trace_events.assign(reinterpret_cast<const cudaEvent_t*>(events),
                                      reinterpret_cast<const cudaEvent_t*>(events) + count);
+  });
+}
+
+int ce4b_nccl_unique_id(void* out, int out_len) {
+  return guarded([&] {
+    require(out != nullptr && out_len >= static_cast<int>(sizeof(ncclUniqueId)),
+            "unique id buffer must hold 128 bytes");
+    ncclUniqueId id;
+    ce4b::check_nccl(ce4b::nccl().GetUniqueId(&id), "ncclGetUniqueId");
+    std::memcpy(out, &id, sizeof(id));
+  });
+}
+
+int ce4b_model_enable_expert_parallel(ce4b_model* model, int rank, int world, const void* unique_id) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    model->impl->enable_expert_parallel(rank, world, unique_id);
+  });
+}
+
+int ce4b_expert_parallel_plan(int world, int rank, const int32_t* meta_send, const int32_t* meta_recv,
+                              int32_t* send_rows, int32_t* recv_rows, int32_t* tiles, int tiles_cap,
+                              int* num_tiles) {
+  return guarded([&] {
+    require(meta_send && meta_recv && send_rows && recv_rows && num_tiles, "null argument");
+    const ce4b::EpPlan p = ce4b::ep_plan(world, rank, reinterpret_cast<const int2*>(meta_send),
+                                         reinterpret_cast<const int2*>(meta_recv));
+    for (int r = 0; r < world; ++r) {
+      send_rows[r] = p.send_rows[r];
+      recv_rows[r] = p.recv_rows[r];
+    }
+    *num_tiles = static_cast<int>(p.tiles.size());
+    require(tiles == nullptr || tiles_cap >= *num_tiles, "tile buffer too small");
+    if (tiles != nullptr) std::memcpy(tiles, p.tiles.data(), p.tiles.size() * sizeof(int4));
   });
 }
 

@@ -44,6 +44,7 @@ std::string shape_str(const std::vector<int64_t>& s) {
 
 Model::~Model() {
   if (device >= 0) cudaSetDevice(device);
+  disable_expert_parallel();
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   if (fwd_dev) cudaFree(fwd_dev);
   if (fwd_weights) cudaFree(fwd_weights);
@@ -478,7 +479,11 @@ void Model::forward(int layout, void* input, const void* scalars, int batch, flo
     const Layer& L = layers[l];
     const bf16* next_norm = l + 1 < cfg.depth ? layers[l + 1].norm : w("final_norm.weight");
     if (L.moe) {
-      moe_layer(L, l / 2, next_norm, batch, tokens_per_expert, s);
+      if (ep_world > 1) {
+        moe_layer_ep(L, l / 2, next_norm, batch, tokens_per_expert, s);
+      } else {
+        moe_layer(L, l / 2, next_norm, batch, tokens_per_expert, s);
+      }
       continue;
     }
     gemm_swiglu(tm_n, L.tm_gate_up, tm_hidden, batch, dense_hidden, d, s);
@@ -560,9 +565,12 @@ void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, flo
   float* pol = reinterpret_cast<float*>(workspace + io_slot.policy);
   float* wdl = reinterpret_cast<float*>(workspace + io_slot.wdl);
   float* ml = reinterpret_cast<float*>(workspace + io_slot.moves_left);
+  // Expert-parallel models synchronise with the host inside the forward (NCCL segment
+  // sizes), so they run without a graph.
+  const bool use_graph = ep_world == 1;
   const int key = batch * kIoSlots + slot;
   auto it = graphs.find(key);
-  if (it == graphs.end()) {
+  if (use_graph && it == graphs.end()) {
     // First use of this batch size and slot: run once outside a capture (kernel
     // attributes), then capture the forward into a graph on the internal stream. Blocks.
     const std::vector<cudaEvent_t> saved = std::move(trace_events);
@@ -603,7 +611,11 @@ void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, flo
                              cudaMemcpyHostToDevice, s),
              "copy input planes");
   check_cuda(cudaStreamWaitEvent(s, forward_done, 0), "wait previous forward");
-  check_cuda(cudaGraphLaunch(it->second, s), "launch graph");
+  if (use_graph) {
+    check_cuda(cudaGraphLaunch(it->second, s), "launch graph");
+  } else {
+    forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, s);
+  }
   check_cuda(cudaEventRecord(forward_done, s), "record forward");
   check_cuda(cudaMemcpyAsync(host_policy, pol, static_cast<size_t>(batch) * policy_size * 4,
                              cudaMemcpyDeviceToHost, s),

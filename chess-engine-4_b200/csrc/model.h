@@ -10,6 +10,18 @@
 
 namespace ce4b {
 
+// Host plan of one expert-parallel exchange (csrc/expert_parallel.cu): rows of the local
+// permuted buffer sent to each rank, rows received from each rank (in rank order, each
+// source's expert segments in expert order) and the m-tile table over the received rows
+// ({global expert, first row, valid rows, 0}).
+struct EpPlan {
+  std::vector<int> send_off, send_rows, recv_off, recv_rows;
+  std::vector<int4> tiles;
+  int recv_total = 0;
+};
+// meta_send[g] / meta_recv[r * (64 / world) + e] = {segment rows padded to 128, valid rows}.
+EpPlan ep_plan(int world, int rank, const int2* meta_send, const int2* meta_recv);
+
 struct Model {
   struct Slot {
     size_t offset = 0;
@@ -128,6 +140,31 @@ struct Model {
                   float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s);
   void forward_fused(int layout, void* input, const void* scalars, int batch, float* policy,
                      float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s);
+  // Expert parallelism (moe64a2): each of ep_world ranks computes 64 / ep_world experts;
+  // routed rows travel with NCCL (ep_comm is an ncclComm_t).
+  int ep_world = 1;
+  int ep_rank = 0;
+  void* ep_comm = nullptr;
+  size_t ep_cap_rows = 0;
+  uint8_t* ep_buf = nullptr;
+  void* ep_host = nullptr;  // pinned: segment metadata and the m-tile table
+  bf16* ep_x = nullptr;
+  bf16* ep_h = nullptr;
+  bf16* ep_y = nullptr;
+  float* ep_p = nullptr;
+  int* ep_counts = nullptr;
+  int2* ep_meta = nullptr;
+  int4* ep_tiles = nullptr;
+  int* ep_num_tiles = nullptr;
+  CUtensorMap tm_ep_x{}, tm_ep_h{}, tm_ep_y{};
+  void enable_expert_parallel(int rank, int world, const void* unique_id);
+  void disable_expert_parallel();
+  void moe_layer_ep(const Layer& L, int moe_index, const bf16* next_norm, int batch,
+                    int32_t* tokens_per_expert, cudaStream_t s);
+  void graphs_clear() {
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    graphs.clear();
+  }
   void moe_layer(const Layer& L, int moe_index, const bf16* next_norm, int batch,
                  int32_t* tokens_per_expert, cudaStream_t s);
 

@@ -162,6 +162,28 @@ int ce4b_model_evaluate_async(ce4b_model* model, const ce4b_input_plane* host_pl
  * events[i] (cudaEvent_t) on its stream after its i-th kernel; count 0 disables.
  * ce4b_model_trace_label names kernel i of the last traced forward. */
 int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count);
+/* ------------------------------------------------------------------ expert parallelism
+ * moe64a2 across `world` GPUs (one process and one model handle per GPU): each rank
+ * computes 64 / world consecutive experts; every MoE layer sends each routed row to the
+ * rank of its expert and back with NCCL send/recv (the reference's
+ * static dispatch path, src/chess_engine_4/model/moe.py:226-287). Each rank passes its own
+ * batch of positions to ce4b_model_forward / ce4b_model_evaluate; results equal the
+ * single-GPU forward of those positions. The forward synchronises with the host once per
+ * MoE layer (segment sizes), so expert-parallel forwards are not graph-captured.
+ * ce4b_nccl_unique_id fills the 128-byte NCCL unique id (rank 0 makes it, every rank passes
+ * the same bytes); ce4b_model_enable_expert_parallel is collective over the ranks. */
+int ce4b_nccl_unique_id(void* out, int out_len);
+int ce4b_model_enable_expert_parallel(ce4b_model* model, int rank, int world, const void* unique_id);
+
+/* Host planning of one exchange, as the forward does it (no GPU): meta_send[64][2] holds
+ * this rank's {segment rows padded to 128, valid rows} per expert, meta_recv[world][64 /
+ * world][2] the same from every rank for this rank's experts. Outputs rows sent to / received
+ * from each rank and the m-tile table over the received rows (int32 x4 per tile: global
+ * expert, first row, valid rows, 0); tiles may be NULL to only count them. */
+int ce4b_expert_parallel_plan(int world, int rank, const int32_t* meta_send, const int32_t* meta_recv,
+                              int32_t* send_rows, int32_t* recv_rows, int32_t* tiles, int tiles_cap,
+                              int* num_tiles);
+
 /* Per-task timeline of the persistent dense forward (dense BF16 models). With
  * capacity_tasks > 0, each forward writes 12 uint64 per task id < capacity_tasks into the
  * device buffer: %globaltimer ns when the task was fetched, its inputs were ready, its

@@ -43,7 +43,7 @@ def _free_port() -> int:
 
 
 def test_two_rank_replica_group_on_gloo() -> None:
-    from dist_worker import replica_worker
+    from dist_worker import collect, replica_worker
 
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
@@ -51,7 +51,7 @@ def test_two_rank_replica_group_on_gloo() -> None:
     procs = [ctx.Process(target=replica_worker, args=(r, 2, port, 4097, queue)) for r in range(2)]
     for p in procs:
         p.start()
-    results = sorted(queue.get(timeout=120) for _ in procs)
+    results = sorted(collect(procs, queue, 120))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
