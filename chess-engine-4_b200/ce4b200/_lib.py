@@ -107,6 +107,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ce4b_model_set_trace": (_i32, [_vp, _vp, _i32]),
     "ce4b_model_set_task_trace": (_i32, [_vp, _vp, _i32]),
     "ce4b_nccl_unique_id": (_i32, [_vp, _i32]),
+    "ce4b_policy_softmax": (_i32, [_vp, _i32, _i32, _vp, _vp, ctypes.c_float, _vp, _vp]),
+    "ce4b_model_evaluate_legal": (_i32, [_vp, _vp, _i32, _vp, _vp, ctypes.c_float, _vp, _vp, _vp]),
     "ce4b_model_enable_expert_parallel": (_i32, [_vp, _i32, _i32, _vp]),
     "ce4b_expert_parallel_plan": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32, ctypes.POINTER(_i32)]),
     "ce4b_model_task_count": (_i32, [_vp, _i32, ctypes.POINTER(_i32)]),

@@ -176,6 +176,27 @@ class Engine:
         _lib.check(self.lib.ce4b_model_evaluate_async(self.handle, planes.data_ptr(), batch, policy.data_ptr(),
                                                       wdl.data_ptr(), ml.data_ptr(), stream.cuda_stream))
 
+    def evaluate_legal(
+        self, planes: torch.Tensor, move_offsets: torch.Tensor, move_indices: torch.Tensor,
+        temperature: float = 1.0,
+    ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Legal-move probabilities instead of the full policy (the lc0 backend's
+        post-processing on the GPU): returns (probs [nnz], wdl probabilities [B, 3],
+        moves-left [B]); move_offsets int32 [B + 1], move_indices int32 [nnz]."""
+
+        batch = self._check_planes(planes)
+        offsets = move_offsets.to(torch.int32).contiguous()
+        indices = move_indices.to(torch.int32).contiguous()
+        if offsets.shape != (batch + 1,) or int(offsets[-1]) != indices.numel():
+            raise ValueError("move_offsets must be [B + 1] ending at len(move_indices)")
+        probs = torch.empty(indices.numel(), dtype=torch.float32)
+        wdl = torch.empty(batch, 3, dtype=torch.float32)
+        ml = torch.empty(batch, dtype=torch.float32)
+        _lib.check(self.lib.ce4b_model_evaluate_legal(
+            self.handle, planes.data_ptr(), batch, offsets.data_ptr(), indices.data_ptr(),
+            float(temperature), probs.data_ptr(), wdl.data_ptr(), ml.data_ptr()))
+        return probs, wdl, ml
+
     def close(self) -> None:
         if self.handle is not None and self.handle.value:
             self.lib.ce4b_model_destroy(self.handle)

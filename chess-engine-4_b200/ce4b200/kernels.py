@@ -309,3 +309,25 @@ def moe_route(
             )
         )
     return experts, probs, counts
+
+
+def policy_softmax(
+    policy: torch.Tensor, move_offsets: torch.Tensor, move_indices: torch.Tensor, temperature: float = 1.0
+) -> torch.Tensor:
+    """Legal-move probabilities on the device: for position b, softmax((logit - max) *
+    temperature) over policy[b, move_indices[move_offsets[b]:move_offsets[b + 1]]]
+    (third_party/lc0/src/neural/backends/ce4/backend.cc:182-195)."""
+
+    if policy.dim() != 2 or policy.dtype != torch.float32 or not policy.is_cuda:
+        raise ValueError("policy must be a CUDA float32 [B, P] tensor")
+    batch, size = policy.shape
+    offsets = move_offsets.to(device=policy.device, dtype=torch.int32).contiguous()
+    indices = move_indices.to(device=policy.device, dtype=torch.int32).contiguous()
+    if offsets.shape != (batch + 1,):
+        raise ValueError("move_offsets must have B + 1 entries")
+    probs = torch.empty(indices.numel(), dtype=torch.float32, device=policy.device)
+    stream = torch.cuda.current_stream(policy.device).cuda_stream
+    _lib.check(_lib.library().ce4b_policy_softmax(
+        policy.contiguous().data_ptr(), batch, size, offsets.data_ptr(), indices.data_ptr(),
+        float(temperature), probs.data_ptr(), stream))
+    return probs

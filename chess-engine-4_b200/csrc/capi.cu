@@ -208,6 +208,29 @@ int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count) {
   });
 }
 
+int ce4b_policy_softmax(const float* policy_dev, int batch, int policy_size,
+                        const int32_t* move_offsets_dev, const int32_t* move_indices_dev,
+                        float temperature, float* probs_dev, void* stream) {
+  return guarded([&] {
+    require(batch >= 0 && policy_size >= 1, "bad policy shape");
+    ce4b::policy_softmax(policy_dev, batch, policy_size, move_offsets_dev, move_indices_dev,
+                         temperature, probs_dev, as_stream(stream));
+  });
+}
+
+int ce4b_model_evaluate_legal(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
+                              const int32_t* host_move_offsets, const int32_t* host_move_indices,
+                              float temperature, float* host_move_probs, float* host_wdl,
+                              float* host_moves_left) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    ce4b::Model& m = *model->impl;
+    m.enqueue_evaluate_legal(host_planes, batch, host_move_offsets, host_move_indices, temperature,
+                             host_move_probs, host_wdl, host_moves_left, m.stream);
+    ce4b::check_cuda(cudaStreamSynchronize(m.stream), "synchronize evaluation");
+  });
+}
+
 int ce4b_nccl_unique_id(void* out, int out_len) {
   return guarded([&] {
     require(out != nullptr && out_len >= static_cast<int>(sizeof(ncclUniqueId)),

@@ -82,6 +82,10 @@ void gemm_heads_scaled(const CUtensorMap& tA, const CUtensorMap& tB, const bf16*
                        float* policy, float* wdl, float* moves_left, int m, int d,
                        int policy_size, int policy_storage, int wdl_probs, const float* ss,
                        int ss_parts, float eps, cudaStream_t s);
+// Per position b: probs[i] = softmax over i in [offsets[b], offsets[b+1]) of
+// policy[b, indices[i]] * temperature (legal-move policy of the lc0 backend).
+void policy_softmax(const float* policy, int batch, int policy_size, const int32_t* offsets,
+                    const int32_t* indices, float temperature, float* probs, cudaStream_t s);
 // out[r, c] = bf16(W[r, c] * w[c]) for a row-major [rows, cols] BF16 matrix.
 void fold_columns(const bf16* W, const bf16* w, bf16* out, int64_t rows, int cols, cudaStream_t s);
 

@@ -113,6 +113,9 @@ void Model::plan_workspace() {
     slot.policy = take(r * policy_size * 4);
     slot.wdl = take(r * 3 * 4);
     slot.moves_left = take(r * 4);
+    slot.move_offsets = take((r + 1) * 4);
+    slot.move_indices = take(r * kMaxMovesPerPosition * 4);
+    slot.move_probs = take(r * kMaxMovesPerPosition * 4);
   }
   ws_off.a_in = take(r * in_dim * 2);
   ws_off.x = take(r * d * 2);
@@ -553,6 +556,113 @@ void Model::trace(const char* label, cudaStream_t s) {
   trace_labels.emplace_back(label);
 }
 
+cudaGraphExec_t Model::evaluate_graph(int batch, int slot) {
+  // Expert-parallel models synchronise with the host inside the forward (NCCL segment
+  // sizes), so they run without a graph.
+  if (ep_world > 1) return nullptr;
+  IoSlot& io_slot = io[slot];
+  auto* planes = reinterpret_cast<ce4b_input_plane*>(workspace + io_slot.planes);
+  float* pol = reinterpret_cast<float*>(workspace + io_slot.policy);
+  float* wdl = reinterpret_cast<float*>(workspace + io_slot.wdl);
+  float* ml = reinterpret_cast<float*>(workspace + io_slot.moves_left);
+  const int key = batch * kIoSlots + slot;
+  auto it = graphs.find(key);
+  if (it != graphs.end()) return it->second;
+  // First use of this batch size and slot: run once outside a capture (kernel
+  // attributes), then capture the forward into a graph on the internal stream. Blocks.
+  const std::vector<cudaEvent_t> saved = std::move(trace_events);
+  trace_events.clear();
+  try {
+    check_cuda(cudaStreamWaitEvent(stream, forward_done, 0), "wait previous forward");
+    check_cuda(cudaStreamWaitEvent(stream, io_slot.free, 0), "wait I/O slot");
+    forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
+    check_cuda(cudaStreamSynchronize(stream), "warm-up forward");
+    check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
+    } catch (...) {
+      cudaGraph_t g = nullptr;
+      cudaStreamEndCapture(stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    cudaGraph_t graph = nullptr;
+    check_cuda(cudaStreamEndCapture(stream, &graph), "end capture");
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t st = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    check_cuda(st, "instantiate graph");
+    it = graphs.emplace(key, exec).first;
+  } catch (...) {
+    trace_events = saved;
+    throw;
+  }
+  trace_events = saved;
+  return it->second;
+}
+
+void Model::enqueue_evaluate_legal(const ce4b_input_plane* host_planes, int batch,
+                                   const int32_t* host_offsets, const int32_t* host_indices,
+                                   float temperature, float* host_probs, float* host_wdl,
+                                   float* host_moves_left, cudaStream_t s) {
+  if (!finalized) fail(CE4B_ERR_NOT_READY, "model is not finalized");
+  require(batch >= 1 && batch <= max_batch, "batch size exceeds model capacity");
+  require(host_planes && host_offsets && host_probs && host_wdl && host_moves_left,
+          "null host buffer");
+  require(host_offsets[0] == 0, "move offsets must start at 0");
+  for (int b = 0; b < batch; ++b) {
+    require(host_offsets[b + 1] >= host_offsets[b] &&
+                host_offsets[b + 1] - host_offsets[b] <= kMaxMovesPerPosition,
+            "move offsets must be non-decreasing, at most 256 moves per position");
+  }
+  const int nnz = host_offsets[batch];
+  require(nnz == 0 || host_indices != nullptr, "null move indices");
+  check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  const int slot = static_cast<int>(io_next % kIoSlots);
+  IoSlot& io_slot = io[slot];
+  auto* planes = reinterpret_cast<ce4b_input_plane*>(workspace + io_slot.planes);
+  float* pol = reinterpret_cast<float*>(workspace + io_slot.policy);
+  float* wdl = reinterpret_cast<float*>(workspace + io_slot.wdl);
+  float* ml = reinterpret_cast<float*>(workspace + io_slot.moves_left);
+  auto* offsets = reinterpret_cast<int32_t*>(workspace + io_slot.move_offsets);
+  auto* indices = reinterpret_cast<int32_t*>(workspace + io_slot.move_indices);
+  auto* probs = reinterpret_cast<float*>(workspace + io_slot.move_probs);
+  cudaGraphExec_t graph = evaluate_graph(batch, slot);
+  ++io_next;
+  check_cuda(cudaStreamWaitEvent(s, io_slot.free, 0), "wait I/O slot");
+  check_cuda(cudaMemcpyAsync(planes, host_planes,
+                             static_cast<size_t>(batch) * kInputPlanes * sizeof(ce4b_input_plane),
+                             cudaMemcpyHostToDevice, s),
+             "copy input planes");
+  check_cuda(cudaMemcpyAsync(offsets, host_offsets, (batch + 1) * 4, cudaMemcpyHostToDevice, s),
+             "copy move offsets");
+  if (nnz > 0) {
+    check_cuda(cudaMemcpyAsync(indices, host_indices, static_cast<size_t>(nnz) * 4,
+                               cudaMemcpyHostToDevice, s),
+               "copy move indices");
+  }
+  check_cuda(cudaStreamWaitEvent(s, forward_done, 0), "wait previous forward");
+  if (graph != nullptr) {
+    check_cuda(cudaGraphLaunch(graph, s), "launch graph");
+  } else {
+    forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, s);
+  }
+  policy_softmax(pol, batch, policy_size, offsets, indices, temperature, probs, s);
+  check_cuda(cudaEventRecord(forward_done, s), "record forward");
+  if (nnz > 0) {
+    check_cuda(cudaMemcpyAsync(host_probs, probs, static_cast<size_t>(nnz) * 4,
+                               cudaMemcpyDeviceToHost, s),
+               "copy move probabilities");
+  }
+  check_cuda(cudaMemcpyAsync(host_wdl, wdl, static_cast<size_t>(batch) * 3 * 4,
+                             cudaMemcpyDeviceToHost, s),
+             "copy wdl");
+  check_cuda(cudaMemcpyAsync(host_moves_left, ml, static_cast<size_t>(batch) * 4,
+                             cudaMemcpyDeviceToHost, s),
+             "copy moves left");
+  check_cuda(cudaEventRecord(io_slot.free, s), "record I/O slot");
+}
+
 void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
                              float* host_wdl, float* host_moves_left, cudaStream_t s) {
   if (!finalized) fail(CE4B_ERR_NOT_READY, "model is not finalized");
@@ -565,43 +675,7 @@ void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, flo
   float* pol = reinterpret_cast<float*>(workspace + io_slot.policy);
   float* wdl = reinterpret_cast<float*>(workspace + io_slot.wdl);
   float* ml = reinterpret_cast<float*>(workspace + io_slot.moves_left);
-  // Expert-parallel models synchronise with the host inside the forward (NCCL segment
-  // sizes), so they run without a graph.
-  const bool use_graph = ep_world == 1;
-  const int key = batch * kIoSlots + slot;
-  auto it = graphs.find(key);
-  if (use_graph && it == graphs.end()) {
-    // First use of this batch size and slot: run once outside a capture (kernel
-    // attributes), then capture the forward into a graph on the internal stream. Blocks.
-    const std::vector<cudaEvent_t> saved = std::move(trace_events);
-    trace_events.clear();
-    try {
-      check_cuda(cudaStreamWaitEvent(stream, forward_done, 0), "wait previous forward");
-      check_cuda(cudaStreamWaitEvent(stream, io_slot.free, 0), "wait I/O slot");
-      forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
-      check_cuda(cudaStreamSynchronize(stream), "warm-up forward");
-      check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
-      try {
-        forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
-      } catch (...) {
-        cudaGraph_t g = nullptr;
-        cudaStreamEndCapture(stream, &g);
-        if (g) cudaGraphDestroy(g);
-        throw;
-      }
-      cudaGraph_t graph = nullptr;
-      check_cuda(cudaStreamEndCapture(stream, &graph), "end capture");
-      cudaGraphExec_t exec = nullptr;
-      const cudaError_t st = cudaGraphInstantiate(&exec, graph, 0);
-      cudaGraphDestroy(graph);
-      check_cuda(st, "instantiate graph");
-      it = graphs.emplace(key, exec).first;
-    } catch (...) {
-      trace_events = saved;
-      throw;
-    }
-    trace_events = saved;
-  }
+  cudaGraphExec_t graph = evaluate_graph(batch, slot);
   ++io_next;
   // This slot's previous D2H copies are done before its planes are overwritten; the H2D
   // copy may overlap the previous call's forward, which the graph then waits for.
@@ -611,8 +685,8 @@ void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, flo
                              cudaMemcpyHostToDevice, s),
              "copy input planes");
   check_cuda(cudaStreamWaitEvent(s, forward_done, 0), "wait previous forward");
-  if (use_graph) {
-    check_cuda(cudaGraphLaunch(it->second, s), "launch graph");
+  if (graph != nullptr) {
+    check_cuda(cudaGraphLaunch(graph, s), "launch graph");
   } else {
     forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, s);
   }

@@ -101,8 +101,10 @@ struct Model {
   static constexpr int kIoSlots = 2;
   struct IoSlot {
     size_t planes = 0, policy = 0, wdl = 0, moves_left = 0;  // workspace offsets
+    size_t move_offsets = 0, move_indices = 0, move_probs = 0;  // legal-move policy
     cudaEvent_t free = nullptr;
   };
+  static constexpr int kMaxMovesPerPosition = 256;  // chess has at most 218 legal moves
   IoSlot io[kIoSlots];
   unsigned io_next = 0;
   cudaEvent_t forward_done = nullptr;
@@ -134,6 +136,15 @@ struct Model {
                 float* host_wdl, float* host_moves_left);
   void enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, float* host_policy,
                         float* host_wdl, float* host_moves_left, cudaStream_t s);
+  // As enqueue_evaluate, but returns only legal-move probabilities (softmax of the gathered
+  // logits times temperature) instead of the full policy.
+  void enqueue_evaluate_legal(const ce4b_input_plane* host_planes, int batch,
+                              const int32_t* host_offsets, const int32_t* host_indices,
+                              float temperature, float* host_probs, float* host_wdl,
+                              float* host_moves_left, cudaStream_t s);
+  // Graph of the host-buffer forward for (batch, slot), built on first use (nullptr for
+  // expert-parallel models, which run without a graph).
+  cudaGraphExec_t evaluate_graph(int batch, int slot);
   void trace(const char* label, cudaStream_t s);
   void quantize_weights();
   void forward_mx(int layout, void* input, const void* scalars, int batch, float* policy,

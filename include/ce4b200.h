@@ -158,6 +158,24 @@ int ce4b_model_evaluate_async(ce4b_model* model, const ce4b_input_plane* host_pl
                               float* host_policy, float* host_wdl, float* host_moves_left,
                               void* stream);
 
+/* Legal-move policy (the lc0 backend's post-processing, third_party/lc0/src/neural/
+ * backends/ce4/backend.cc:182-195, on the device): for position b the probabilities of
+ * its legal moves, move_indices[move_offsets[b] .. move_offsets[b+1]) (NN policy indices,
+ * board transform applied by the caller), are softmax((logit - max) * temperature) of the
+ * gathered logits. expf is used (the backend's FastExp approximates it).
+ * ce4b_policy_softmax works on device buffers (policy [batch, policy_size] f32, offsets
+ * [batch + 1], indices and probs [offsets[batch]]) on `stream`.
+ * ce4b_model_evaluate_legal is ce4b_model_evaluate returning move probabilities instead
+ * of the 1858 logits (blocking; host buffers; at most 256 moves per position), so only
+ * ~4 bytes per legal move cross PCIe instead of 7.4 KB per position. */
+int ce4b_policy_softmax(const float* policy_dev, int batch, int policy_size,
+                        const int32_t* move_offsets_dev, const int32_t* move_indices_dev,
+                        float temperature, float* probs_dev, void* stream);
+int ce4b_model_evaluate_legal(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
+                              const int32_t* host_move_offsets, const int32_t* host_move_indices,
+                              float temperature, float* host_move_probs, float* host_wdl,
+                              float* host_moves_left);
+
 /* Per-kernel tracing of ce4b_model_forward: when `count` > 0, forward records
  * events[i] (cudaEvent_t) on its stream after its i-th kernel; count 0 disables.
  * ce4b_model_trace_label names kernel i of the last traced forward. */
