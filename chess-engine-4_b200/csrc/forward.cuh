@@ -9,11 +9,16 @@
 // single-GEMM kernels (warp 0: TMA producer, warp 1: tcgen05.mma issuer, 16 epilogue
 // warps; two accumulators so one tile's epilogue overlaps the next tile's MMAs):
 //
-//   input tile  (rb, j, s): x[rb, j] = bf16(A_in . W_in^T + b) over k-split s of in_dim;
-//                           split partials are FP32 and summed in split order by the
-//                           split that finishes last, so results do not depend on timing.
+//   input tile   (rb, j):    x[rb, j] = bf16(A_in . W_in^T + b)
 //   gate_up tile (l, rb, c): hidden[rb, c] = bf16(silu(bf16(r * x W'_g^T)) * bf16(r * x W'_u^T))
-//   down tile   (l, rb, j): x[rb, j] = bf16(x + bf16(hidden . W_d^T)).
+//   down tile    (l, rb, j): x[rb, j] = bf16(x + bf16(hidden . W_d^T)).
+//
+// Tiles are 128 rows; gate_up tiles are 256 accumulator columns (128 gate + 128 up, one
+// 128-column hidden chunk). Input and down tiles are xw columns of x, chosen per forward:
+// 128 when a layer's down tiles fill less than two waves of SMs (the dependency chain of
+// each row block bounds the forward, and narrower tiles give it more SMs), 256 otherwise
+// (throughput bounds it, and a 128-column tile fed by TMA runs at half the MMA rate). The
+// width changes which CTA computes which columns, not the arithmetic.
 //
 // RMSNorm is folded: W' = bf16(W * diag(norm weight)) is prepared once, and the row scale
 // r = rsqrt(mean(x^2) + eps) multiplies the FP32 accumulator of the gate_up tile, so
@@ -42,24 +47,21 @@ struct FwdTask {
   int type;
   int layer;
   int rb;
-  int col;
-  int ks;
+  int col;  // hidden chunk (gate_up) or x tile of width xw (input, down)
 };
 
 __device__ __forceinline__ FwdTask fwd_decode(const FwdParams& p, int t) {
-  FwdTask k{kTaskEnd, 0, 0, 0, 0};
+  FwdTask k{kTaskEnd, 0, 0, 0};
   if (t < 0 || t >= p.total_tasks) return k;
-  const int n_in = p.nb * p.sj * p.ks;
+  const int n_in = p.nb * p.xt;
   if (t < n_in) {
     k.type = kTaskInput;
-    k.rb = t / (p.sj * p.ks);
-    const int rem = t - k.rb * (p.sj * p.ks);
-    k.col = rem / p.ks;
-    k.ks = rem - k.col * p.ks;
+    k.rb = t / p.xt;
+    k.col = t - k.rb * p.xt;
     return k;
   }
   t -= n_in;
-  const int per_layer = p.nb * (p.nc + p.sj);
+  const int per_layer = p.nb * (p.nc + p.xt);
   k.layer = t / per_layer;
   t -= k.layer * per_layer;
   if (t < p.nb * p.nc) {
@@ -69,8 +71,8 @@ __device__ __forceinline__ FwdTask fwd_decode(const FwdParams& p, int t) {
   } else {
     t -= p.nb * p.nc;
     k.type = kTaskDown;
-    k.rb = t / p.sj;
-    k.col = t - k.rb * p.sj;
+    k.rb = t / p.xt;
+    k.col = t - k.rb * p.xt;
   }
   return k;
 }
@@ -80,13 +82,6 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
   return v;
-}
-
-__device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
-  int old;
-  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v)
-               : "memory");
-  return old;
 }
 
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -210,79 +205,64 @@ __device__ __forceinline__ void fwd_epi_gate_up(const FwdParams& p, const FwdTas
   }
 }
 
-// x slice tile (input or down): stores the BF16 slice and its per-(row, column group)
-// sums of squares, then publishes slice_cnt[rb].
-// `pre` holds this thread's 32 BF16 of the residual slice (down) or of the bias (input),
-// loaded before the accumulator was ready.
+// x tile (input or down), xw columns: thread (r, g) handles xw / 128 chunks of 32 columns,
+// c = g * (xw / 4) + 32 * i. Per chunk it stores the BF16 values and their sum of squares
+// in ss[row][slice * kFwdG + group] (slice = 128-column slice, group = 32-column group in
+// it, the layout the row scale reads); then the tile publishes the xw / 128 slices it
+// covers. `pre0` holds the thread's first chunk of the residual (down) or of the bias
+// (input), loaded before the accumulator was ready; later chunks are loaded after the
+// previous one is stored.
 __device__ __forceinline__ void fwd_epi_slice(const FwdParams& p, const FwdTask& k, int t, int r,
                                               int g, int tid, uint32_t taddr, uint32_t tempty,
-                                              volatile int* flag, const uint4 (&pre)[4]) {
+                                              const uint4 (&pre0)[4]) {
   const int row = k.rb * kBM + r;
-  const int c = g * 32;
-  const int col0 = k.col * 128 + c;
-  __nv_bfloat16* xr = p.x + static_cast<size_t>(row) * p.d + col0;
-  float v[32];
-  load_acc32(taddr + c, v);
-  tc_fence_before();
-  mbar_arrive(tempty);
-  if (k.type == kTaskInput && p.ks > 1) {
-    float* dst = p.part + (static_cast<size_t>(k.ks) * p.rows_cap + row) * p.d + col0;
+  const int nchunk = p.xw / 128;
+  for (int ci = 0; ci < nchunk; ++ci) {
+    const int c = g * (p.xw / 4) + 32 * ci;  // column in the tile
+    const int col0 = k.col * p.xw + c;       // column in x
+    uint4 pre[4];
+    if (ci == 0) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      for (int q = 0; q < 4; ++q) pre[q] = pre0[q];
+    } else {
+      const __nv_bfloat16* src = k.type == kTaskDown
+                                     ? p.x + static_cast<size_t>(row) * p.d + col0
+                                     : p.bias + col0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) pre[q] = ldcg_u4(src + 8 * q);
     }
-    fwd_epi_sync();
-    if (tid == 0) {
-      fence_acq_rel_gpu();
-      const int old = atom_add_acq_rel_gpu(p.part_cnt + k.rb * p.sj + k.col, 1);
-      *flag = old == p.ks - 1;
+    float v[32];
+    load_acc32(taddr + c, v);
+    if (ci == nchunk - 1) {
+      tc_fence_before();
+      mbar_arrive(tempty);
     }
-    fwd_epi_sync();
-    if (*flag == 0) return;
-    // Last split of this tile: sum the splits in split order.
-    for (int sp = 0; sp < p.ks; ++sp) {
-      const float* src = p.part + (static_cast<size_t>(sp) * p.rows_cap + row) * p.d + col0;
+    if (k.type != kTaskInput) round_bf16_inplace(v);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float4 a[4];
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t wq[4] = {pre[q].x, pre[q].y, pre[q].z, pre[q].w};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) a[q] = ldcg_f4(src + 16 * h + 4 * q);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int j = 16 * h + 4 * q;
-          v[j] = sp == 0 ? a[q].x : v[j] + a[q].x;
-          v[j + 1] = sp == 0 ? a[q].y : v[j + 1] + a[q].y;
-          v[j + 2] = sp == 0 ? a[q].z : v[j + 2] + a[q].z;
-          v[j + 3] = sp == 0 ? a[q].w : v[j + 3] + a[q].w;
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(wq[j]);
+        // input: acc + bias (TE's fused bias); down: residual + bf16(acc)
+        v[8 * q + 2 * j] = k.type == kTaskInput ? v[8 * q + 2 * j] + f.x : f.x + v[8 * q + 2 * j];
+        v[8 * q + 2 * j + 1] =
+            k.type == kTaskInput ? v[8 * q + 2 * j + 1] + f.y : f.y + v[8 * q + 2 * j + 1];
       }
     }
+    round_bf16_inplace(v);
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+    store_bf16x32(p.x + static_cast<size_t>(row) * p.d + col0, v);
+    p.ss[static_cast<size_t>(row) * (p.sj * kFwdG) + (col0 >> 7) * kFwdG + ((col0 & 127) >> 5)] = ss;
   }
-  if (k.type != kTaskInput) round_bf16_inplace(v);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t wq[4] = {pre[q].x, pre[q].y, pre[q].z, pre[q].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack_bf16x2(wq[j]);
-      // input: acc + bias (TE's fused bias); down: residual + bf16(acc)
-      v[8 * q + 2 * j] = k.type == kTaskInput ? v[8 * q + 2 * j] + f.x : f.x + v[8 * q + 2 * j];
-      v[8 * q + 2 * j + 1] =
-          k.type == kTaskInput ? v[8 * q + 2 * j + 1] + f.y : f.y + v[8 * q + 2 * j + 1];
-    }
-  }
-  round_bf16_inplace(v);
-  float ss = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
-  store_bf16x32(xr, v);
-  p.ss[static_cast<size_t>(row) * (p.sj * kFwdG) + k.col * kFwdG + g] = ss;
   fwd_epi_sync();
   if (tid == 0) {
     fwd_stamp(p, t, 7);
     fence_acq_rel_gpu();
     fence_proxy_async_global();
-    red_add_relaxed_gpu(p.slice_cnt + k.rb, 1);
+    red_add_relaxed_gpu(p.slice_cnt + k.rb, nchunk);
     fwd_stamp(p, t, 8);
   }
 }
@@ -317,8 +297,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
   const uint32_t drain_bar = bar_base + 8u * (L::kBarriers - 1);
   volatile int* task_slot =
       reinterpret_cast<volatile int*>(smem + L::kRingBytes + L::kBarriers * 8);
-  volatile int* flag = task_slot + kFwdTaskRing;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(flag + 1));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(task_slot + kFwdTaskRing + 1));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -372,7 +351,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         }
         int t = ok ? atomicAdd(p.task_counter, 1) : -1;
         if (t >= p.total_tasks) t = -1;
-        FwdTask k{kTaskEnd, 0, 0, 0, 0};
+        FwdTask k{kTaskEnd, 0, 0, 0};
         const CUtensorMap* ma = nullptr;
         const CUtensorMap* mb = nullptr;
         int kb0 = 0, kb1 = 0, b_row = 0, b_row2 = -1;
@@ -385,9 +364,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
           if (k.type == kTaskInput) {
             ma = &maps->a_in;
             mb = &maps->w_in;
-            kb0 = k.ks * p.kb_in / p.ks;
-            kb1 = (k.ks + 1) * p.kb_in / p.ks;
-            b_row = k.col * 128;
+            kb1 = p.kb_in;
+            b_row = k.col * p.xw;
+            if (p.xw == 256) b_row2 = b_row + 128;
           } else if (k.type == kTaskGateUp) {
             if (!wait_counter(p.slice_cnt + k.rb, (k.layer + 1) * p.sj)) {
               record_error(p.err, kErrTimeoutDependency);
@@ -404,7 +383,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
             ma = &maps->hidden;
             mb = &maps->down[k.layer];
             kb1 = p.h / kBK;
-            b_row = k.col * 128;
+            b_row = k.col * p.xw;
+            if (p.xw == 256) b_row2 = b_row + 128;
           }
         }
         // The task is published once its inputs are complete (the acquire above), so the
@@ -461,13 +441,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         mbar_arrive(task_empty(q));
         if (t < 0) break;
         const FwdTask k = fwd_decode(p, t);
-        int nkb;
-        if (k.type == kTaskInput) {
-          nkb = (k.ks + 1) * p.kb_in / p.ks - k.ks * p.kb_in / p.ks;
-        } else {
-          nkb = (k.type == kTaskGateUp ? p.d : p.h) / kBK;
-        }
-        const uint32_t idesc = idesc_bf16(kBM, k.type == kTaskGateUp ? 256 : 128);
+        const int nkb = k.type == kTaskInput ? p.kb_in : (k.type == kTaskGateUp ? p.d : p.h) / kBK;
+        const uint32_t idesc = idesc_bf16(kBM, k.type == kTaskGateUp ? 256 : p.xw);
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u)) {
           record_error(p.err, kErrTimeoutMma);
           break;
@@ -531,9 +506,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       if (k.type == kTaskGateUp) {
         scale = fwd_row_scale(p, k.rb * kBM + r);
       } else {
+        const int col0 = k.col * p.xw + g * (p.xw / 4);
         const __nv_bfloat16* src = k.type == kTaskDown
-                                       ? p.x + static_cast<size_t>(k.rb * kBM + r) * p.d + k.col * 128 + g * 32
-                                       : p.bias + k.col * 128 + g * 32;
+                                       ? p.x + static_cast<size_t>(k.rb * kBM + r) * p.d + col0
+                                       : p.bias + col0;
 #pragma unroll
         for (int q = 0; q < 4; ++q) pre[q] = ldcg_u4(src + 8 * q);
       }
@@ -548,7 +524,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       if (k.type == kTaskGateUp) {
         fwd_epi_gate_up(p, k, t, r, g, tid, taddr, tempty_bar(acc), scale);
       } else {
-        fwd_epi_slice(p, k, t, r, g, tid, taddr, tempty_bar(acc), flag, pre);
+        fwd_epi_slice(p, k, t, r, g, tid, taddr, tempty_bar(acc), pre);
       }
       if (tid == 0) fwd_stamp(p, t, 6);
       if (++acc == 2) {

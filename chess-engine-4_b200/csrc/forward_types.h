@@ -34,18 +34,17 @@ struct FwdParams {
   __nv_bfloat16* x;           // [rows_cap, d]
   __nv_bfloat16* hidden;      // [rows_cap, h]
   float* ss;                  // [rows_cap, sj * kFwdG] partial sums of squares of x
-  float* part;                // [ks, rows_cap, d] input split partials (ks > 1)
   int* hid_cnt;               // [nb] finished gate_up tiles
-  int* slice_cnt;             // [nb] finished x slices
-  int* part_cnt;              // [nb * sj] finished input splits per slice
+  int* slice_cnt;             // [nb] finished 128-column x slices
   int* task_counter;          // [1]
   int* err;
   int rows_cap;
   int nb;      // row blocks of 128
   int d, h, depth;
-  int sj;      // d / 128 column slices
+  int sj;      // d / 128 column slices (the granularity of slice_cnt and ss)
   int nc;      // h / 128 hidden chunks
-  int ks;      // k splits of the input GEMM
+  int xw;      // column width of the input and down tiles (128 or 256)
+  int xt;      // d / xw input (and down) tiles per row block
   int kb_in;   // k-blocks of the input GEMM (in_dim / 64)
   int total_tasks;
   float eps;

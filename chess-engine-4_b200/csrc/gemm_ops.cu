@@ -353,8 +353,9 @@ void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMa
 
 // ------------------------------------------------------------------ persistent dense forward
 void dense_forward(const FwdParams& p, cudaStream_t s) {
-  require(p.total_tasks >= 1 && p.depth >= 1 && p.depth <= kFwdMaxDepth && p.ks >= 1 &&
-              p.ks <= p.kb_in && p.d % 128 == 0 && p.d / 128 <= kFwdMaxSlices && p.h % 128 == 0,
+  require(p.total_tasks >= 1 && p.depth >= 1 && p.depth <= kFwdMaxDepth && p.kb_in >= 1 &&
+              p.d % 128 == 0 && p.d / 128 <= kFwdMaxSlices && p.h % 128 == 0 &&
+              (p.xw == 128 || p.xw == 256) && p.d % p.xw == 0 && p.xt == p.d / p.xw,
           "persistent forward: unsupported shape");
   auto kernel = dense_forward_kernel;
   ensure_smem(kernel, FwdSmem::kBytes);

@@ -134,8 +134,7 @@ void Model::plan_workspace() {
     const size_t sj = static_cast<size_t>(d / 128);
     const size_t nb = r / 128;
     ws_off.fwd_ss = take(r * sj * kFwdG * 4);
-    ws_off.fwd_part = fwd_ks > 1 ? take(static_cast<size_t>(fwd_ks) * r * d * 4) : 0;
-    fwd_sync_bytes = (2 * nb + nb * sj + 1) * 4;
+    fwd_sync_bytes = (2 * nb + 1) * 4;
     ws_off.fwd_sync = take(fwd_sync_bytes);
   }
   if (cfg.arch == CE4B_ARCH_MOE64A2) {
@@ -204,7 +203,6 @@ void Model::create(const ce4b_model_config& c, int dev, int maxb) {
   rows_cap = (maxb + 127) / 128 * 128;
   fused = c.arch == CE4B_ARCH_DENSE && !mx && c.d_model % 128 == 0 &&
           c.d_model / 128 <= kFwdMaxSlices && dense_hidden % 128 == 0 && c.depth <= kFwdMaxDepth;
-  fwd_ks = 1;  // input GEMM tiles over the full 7168 (FP32 split partials cost more than they save)
   (void)resnorm_bn(c.d_model);  // validates width against the cluster limit
 
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
@@ -423,12 +421,10 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.x = reinterpret_cast<bf16*>(workspace + ws_off.x);
   p.hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);
   p.ss = reinterpret_cast<float*>(workspace + ws_off.fwd_ss);
-  p.part = fwd_ks > 1 ? reinterpret_cast<float*>(workspace + ws_off.fwd_part) : nullptr;
   p.sj = d / 128;
   p.hid_cnt = sync;
   p.slice_cnt = sync + nb_cap;
-  p.part_cnt = sync + 2 * nb_cap;
-  p.task_counter = sync + 2 * nb_cap + nb_cap * p.sj;
+  p.task_counter = sync + 2 * nb_cap;
   p.err = device_error_word();
   p.rows_cap = rows_cap;
   p.nb = (batch + 127) / 128;
@@ -436,7 +432,8 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.h = dense_hidden;
   p.depth = cfg.depth;
   p.nc = dense_hidden / 128;
-  p.ks = fwd_ks;
+  p.xw = fused_xw(batch);
+  p.xt = d / p.xw;
   p.kb_in = in_dim / kFwdKBlock;
   p.total_tasks = fused_task_count(batch);
   p.eps = cfg.rms_norm_eps;

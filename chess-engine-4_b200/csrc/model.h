@@ -46,7 +46,7 @@ struct Model {
     size_t expert_start = 0, m_tiles = 0, num_m_tiles = 0, xperm = 0, pprob = 0, hperm = 0;
     size_t yperm = 0;
     size_t a_codes = 0, a_scales = 0, n_codes = 0, n_scales = 0, h_codes = 0, h_scales = 0;
-    size_t fwd_ss = 0, fwd_part = 0, fwd_sync = 0;  // persistent dense forward
+    size_t fwd_ss = 0, fwd_sync = 0;  // persistent dense forward
   };
 
   ce4b_model_config cfg{};
@@ -67,18 +67,24 @@ struct Model {
   uint8_t* workspace = nullptr;
   bool mx = false;                // precision MXFP8
   // Dense BF16 towers run as one persistent kernel (forward.cuh): its tensor maps and
-  // norm-weight table live in fwd_dev; fwd_ks = k splits of the input GEMM.
+  // norm-weight table live in fwd_dev.
   bool fused = false;
-  int fwd_ks = 1;
   uint8_t* fwd_dev = nullptr;      // FwdMaps
   bf16* fwd_weights = nullptr;     // norm-folded gate_up [depth][2h, d], then heads [Ps + 64, d]
   CUtensorMap tm_heads_folded{};
   size_t fwd_sync_bytes = 0;
   unsigned long long* fwd_trace = nullptr;  // optional per-task timeline (device buffer)
   int fwd_trace_cap = 0;
+  // Column width of the persistent forward's input and down tiles for this batch: 256 once
+  // a layer's 256-wide down tiles fill two waves of SMs (throughput-bound), else 128
+  // (the per-row-block dependency chain bounds the forward; more, narrower tiles help it).
+  int fused_xw(int batch) const {
+    const int nb = (batch + 127) / 128;
+    return cfg.d_model % 256 == 0 && nb * (cfg.d_model / 256) >= 2 * sm_count() ? 256 : 128;
+  }
   int fused_task_count(int batch) const {
-    const int nb = (batch + 127) / 128, sj = cfg.d_model / 128, nc = dense_hidden / 128;
-    return nb * sj * fwd_ks + cfg.depth * nb * (nc + sj);
+    const int nb = (batch + 127) / 128, xt = cfg.d_model / fused_xw(batch), nc = dense_hidden / 128;
+    return nb * xt + cfg.depth * nb * (nc + xt);
   }
   uint8_t* mx_arena = nullptr;    // quantised weights (codes + scales)
   size_t mx_arena_bytes = 0;

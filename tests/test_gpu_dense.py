@@ -160,7 +160,16 @@ def test_forward_normalizes_rule50_in_place_like_reference() -> None:
     torch.testing.assert_close(planes, expected)
 
 
-@pytest.mark.parametrize("d,depth,ratio,batch", [(512, 12, 3.0, 4096), (256, 4, 3.0, 300), (128, 2, 3.0, 7)])
+@pytest.mark.parametrize(
+    "d,depth,ratio,batch",
+    [
+        (512, 12, 3.0, 4096),  # cluster kernel, K-split input/down tiles (the benchmark shape)
+        (512, 3, 3.0, 200),  # cluster kernel, ragged last row block
+        (1024, 2, 3.0, 300),  # cluster kernel, one 256-column block per CTA
+        (256, 4, 3.0, 300),  # task-queue kernel
+        (128, 2, 3.0, 7),  # task-queue kernel, one partial row block
+    ],
+)
 def test_persistent_forward_matches_folded_restatement(d: int, depth: int, ratio: float, batch: int) -> None:
     """Dense BF16 models run as one persistent kernel that folds each RMSNorm weight into
     the next linear (bf16(W * diag(w))) and scales the FP32 accumulator by the row's
@@ -185,3 +194,42 @@ def test_persistent_forward_matches_folded_restatement(d: int, depth: int, ratio
     assert float((ours - policy).abs().max()) <= 2e-2
     assert argmax_agreement(out.policy_logits, policy) >= ARGMAX_AGREEMENT
     torch.testing.assert_close(out.moves_left.cpu(), ml, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("d,depth,batch", [(512, 3, 1000), (256, 2, 300)])
+def test_persistent_forward_is_deterministic(d: int, depth: int, batch: int) -> None:
+    """Both tower kernels fix every summation order (K-split partial tiles are a sum of two
+    terms), so repeated forwards give bit-identical outputs. (The forward normalises its
+    input planes in place, as the reference's does, so every call gets a fresh copy.)"""
+
+    weights, _, planes = _dense_case(d, depth, 3.0, batch)
+    model = dense_model(weights, d=d, depth=depth, ratio=3.0).cuda()
+    x = planes.cuda()
+    first = model(x.clone())
+    torch.cuda.synchronize()
+    ref = [t.clone() for t in (first.policy_logits, first.wdl_logits, first.moves_left)]
+    for _ in range(3):
+        again = model(x.clone())
+        torch.cuda.synchronize()
+        for a, b in zip(ref, (again.policy_logits, again.wdl_logits, again.moves_left)):
+            assert torch.equal(a, b)
+
+
+def test_persistent_forward_tile_width_does_not_change_results() -> None:
+    """Large batches run the input and down tiles 256 columns wide (throughput-bound),
+    small ones 128 wide (chain-bound); only the assignment of columns to CTAs changes, so
+    a position's outputs are the same bits whichever width its batch used."""
+
+    torch.manual_seed(0)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    big = 128 * sms + 256  # 256-wide tiles: (big / 128) * (512 / 256) >= 2 * SMs
+    weights, _, planes = _dense_case(512, 2, 3.0, big)
+    model = dense_model(weights, d=512, depth=2, ratio=3.0).cuda()
+    x = planes.cuda()
+    wide = model(x.clone())
+    torch.cuda.synchronize()
+    wide = [t[:256].clone() for t in (wide.policy_logits, wide.wdl_logits, wide.moves_left)]
+    narrow = model(x[:256].clone())
+    torch.cuda.synchronize()
+    for a, b in zip(wide, (narrow.policy_logits, narrow.wdl_logits, narrow.moves_left)):
+        assert torch.equal(a, b)
