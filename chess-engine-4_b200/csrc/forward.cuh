@@ -9,12 +9,17 @@
 // single-GEMM kernels (warp 0: TMA producer, warp 1: tcgen05.mma issuer, 16 epilogue
 // warps; two accumulators so one tile's epilogue overlaps the next tile's MMAs):
 //
-//   input tile   (rb, j):    x[rb, j] = bf16(A_in . W_in^T + b)
+//   input tile   (rb, j, s): x[rb, j] = bf16((P_0 + P_1) + b), P_s = A_in . W_in^T over K half
+//                            s; both halves store FP32 P_s and the one that finishes second
+//                            sums them (a two-term sum: the same whichever finishes first)
 //   gate_up tile (l, rb, c): hidden[rb, c] = bf16(silu(bf16(r * x W'_g^T)) * bf16(r * x W'_u^T))
 //   down tile    (l, rb, j): x[rb, j] = bf16(x + bf16(hidden . W_d^T)).
 //
 // Tiles are 128 rows; gate_up tiles are 256 accumulator columns (128 gate + 128 up, one
-// 128-column hidden chunk). Input and down tiles are xw columns of x, chosen per forward:
+// 128-column hidden chunk). Input tiles are 256 columns of x where d allows, split into two
+// K halves (K = 7168 is the longest loop of the forward; halving it shortens the first
+// step of every row block's chain and keeps all SMs busy at the start). Down tiles are xw
+// columns of x, chosen per forward:
 // 128 when a layer's down tiles fill less than two waves of SMs (the dependency chain of
 // each row block bounds the forward, and narrower tiles give it more SMs), 256 otherwise
 // (throughput bounds it, and a 128-column tile fed by TMA runs at half the MMA rate). The
@@ -47,17 +52,20 @@ struct FwdTask {
   int type;
   int layer;
   int rb;
-  int col;  // hidden chunk (gate_up) or x tile of width xw (input, down)
+  int col;  // hidden chunk (gate_up), x tile of width xwi (input) or xw (down)
+  int kh;   // K half (input)
 };
 
 __device__ __forceinline__ FwdTask fwd_decode(const FwdParams& p, int t) {
-  FwdTask k{kTaskEnd, 0, 0, 0};
+  FwdTask k{kTaskEnd, 0, 0, 0, 0};
   if (t < 0 || t >= p.total_tasks) return k;
-  const int n_in = p.nb * p.xt;
+  const int n_in = p.nb * p.xti * 2;
   if (t < n_in) {
     k.type = kTaskInput;
-    k.rb = t / p.xt;
-    k.col = t - k.rb * p.xt;
+    k.rb = t / (p.xti * 2);
+    const int rem = t - k.rb * (p.xti * 2);
+    k.col = rem >> 1;
+    k.kh = rem & 1;
     return k;
   }
   t -= n_in;
@@ -78,6 +86,13 @@ __device__ __forceinline__ FwdTask fwd_decode(const FwdParams& p, int t) {
 }
 
 // ------------------------------------------------------------------ global synchronisation
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v)
+               : "memory");
+  return old;
+}
+
 __device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
   int v;
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
@@ -140,6 +155,12 @@ __device__ __forceinline__ void fwd_stamp(const FwdParams& p, int t, int slot) {
 
 __device__ __forceinline__ void fwd_epi_sync() { named_bar_sync(kEpiBarrierId, kFwdEpiThreads); }
 
+// Epilogue barrier that ORs the threads' `failed` flags (a timed-out wait): all epilogue
+// threads reach the same barriers and take the same decision to stop.
+__device__ __forceinline__ bool fwd_epi_sync_or(bool failed) {
+  return named_bar_or(kEpiBarrierId, kFwdEpiThreads, failed);
+}
+
 // ------------------------------------------------------------------ epilogues
 // Publishing: all epilogue threads store, pass the epilogue barrier, then one thread
 // issues a GPU-scope acq_rel fence (which also releases the other threads' stores made
@@ -174,97 +195,236 @@ __device__ __forceinline__ float fwd_row_scale(const FwdParams& p, int row) {
   return 1.0f / sqrtf(total / static_cast<float>(p.d) + p.eps);
 }
 
-// gate_up tile: accumulator columns [0, 128) gate, [128, 256) up; A was the raw x, and
-// `scale` is the row's RMSNorm scale.
-__device__ __forceinline__ void fwd_epi_gate_up(const FwdParams& p, const FwdTask& k, int t, int r,
-                                                int g, int tid, uint32_t taddr, uint32_t tempty,
-                                                float scale) {
-  const int row = k.rb * kBM + r;
-  const int c = g * 32;
-  float gv[32], uv[32];
-  load_acc32x2(taddr + c, taddr + 128 + c, gv, uv);
-  tc_fence_before();
-  mbar_arrive(tempty);
+// ------------------------------------------------------------------ staged tile output
+// Epilogues write their BF16 tiles through a 32 KB staging tile in shared memory (two
+// 64-column TMA boxes of 128 rows, 128-byte swizzle: row r's 16-byte unit u sits at
+// r * 128 + ((u ^ (r & 7)) * 16)) and one thread stores it with TMA. A thread owns one row
+// and 32 consecutive columns, so writing global memory directly would touch 32 lines per
+// warp instruction; the swizzled staging writes are conflict-free and the TMA store is
+// fully coalesced. Down tiles also load their residual into the staging tile with TMA and
+// overwrite it in place with the result.
+struct FwdEpi {
+  uint32_t stage;    // staging tile
+  uint32_t x_bar;    // mbarrier of the residual load into the staging tile
+  uint32_t x_phase;  // parity of its next phase
+  int r, g, tid;     // row in the tile, 32-column group, epilogue thread index
+  bool x_pending;    // (thread 0) a residual load was issued and not yet waited for
+};
+
+__device__ __forceinline__ uint32_t fwd_stage_addr(uint32_t stage, int r, int c) {
+  return stage + static_cast<uint32_t>((c >> 6) * 16384 + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void fwd_stage_write32(uint32_t stage, int r, int c, const float (&v)[32]) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    gv[j] = __fmul_rn(gv[j], scale);
-    uv[j] = __fmul_rn(uv[j], scale);
-  }
-  round_bf16_inplace(gv);
-  round_bf16_inplace(uv);
-#pragma unroll
-  for (int j = 0; j < 32; ++j) gv[j] = swiglu_f32(gv[j], uv[j]);
-  store_bf16x32(p.hidden + static_cast<size_t>(row) * p.h + k.col * 128 + c, gv);
-  fwd_epi_sync();
-  if (tid == 0) {
-    fwd_stamp(p, t, 7);
-    fence_acq_rel_gpu();
-    fence_proxy_async_global();
-    red_add_relaxed_gpu(p.hid_cnt + k.rb, 1);
-    fwd_stamp(p, t, 8);
+  for (int u = 0; u < 4; ++u) {
+    st_shared_v4(fwd_stage_addr(stage, r, c + 8 * u),
+                 make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
+                            pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7])));
   }
 }
 
-// x tile (input or down), xw columns: thread (r, g) handles xw / 128 chunks of 32 columns,
-// c = g * (xw / 4) + 32 * i. Per chunk it stores the BF16 values and their sum of squares
-// in ss[row][slice * kFwdG + group] (slice = 128-column slice, group = 32-column group in
-// it, the layout the row scale reads); then the tile publishes the xw / 128 slices it
-// covers. `pre0` holds the thread's first chunk of the residual (down) or of the bias
-// (input), loaded before the accumulator was ready; later chunks are loaded after the
-// previous one is stored.
-__device__ __forceinline__ void fwd_epi_slice(const FwdParams& p, const FwdTask& k, int t, int r,
-                                              int g, int tid, uint32_t taddr, uint32_t tempty,
-                                              const uint4 (&pre0)[4]) {
-  const int row = k.rb * kBM + r;
-  const int nchunk = p.xw / 128;
-  for (int ci = 0; ci < nchunk; ++ci) {
-    const int c = g * (p.xw / 4) + 32 * ci;  // column in the tile
-    const int col0 = k.col * p.xw + c;       // column in x
-    uint4 pre[4];
-    if (ci == 0) {
+// TMA-store the staging tile to columns [x0, x0 + 128) of rows [y0, y0 + 128).
+__device__ __forceinline__ void fwd_stage_store(const CUtensorMap* map, uint32_t stage, int x0, int y0) {
+  tma_store_2d(map, stage, x0, y0);
+  tma_store_2d(map, stage + 16384, x0 + 64, y0);
+  bulk_commit();
+}
+
+// Load columns [x0, x0 + 128) of rows [y0, y0 + 128) into the staging tile.
+__device__ __forceinline__ void fwd_stage_load(const CUtensorMap* map, uint32_t stage, uint32_t bar, int x0,
+                                               int y0) {
+  mbar_arrive_expect_tx(bar, 32768);
+  tma_load_2d(stage, map, bar, x0, y0);
+  tma_load_2d(stage + 16384, map, bar, x0 + 64, y0);
+}
+
+// Publish after this thread's TMA stores: wait until they are complete, order them before
+// the GPU-scope release, and count the tile.
+__device__ __forceinline__ void fwd_publish_stored(int* counter, int v) {
+  bulk_wait_all();
+  fence_proxy_async_global();
+  fence_acq_rel_gpu();
+  red_add_relaxed_gpu(counter, v);
+}
+
+// Sum of squares of 32 finished BF16 values of x, stored per (row, 128-column slice,
+// 32-column group): the layout the row scale reads.
+__device__ __forceinline__ void fwd_store_ss32(const FwdParams& p, int row, int col0, const float (&v)[32]) {
+  float ss = 0.0f;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) pre[q] = pre0[q];
-    } else {
-      const __nv_bfloat16* src = k.type == kTaskDown
-                                     ? p.x + static_cast<size_t>(row) * p.d + col0
-                                     : p.bias + col0;
+  for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+  p.ss[static_cast<size_t>(row) * (p.sj * kFwdG) + (col0 >> 7) * kFwdG + ((col0 & 127) >> 5)] = ss;
+}
+
+__device__ __forceinline__ void fwd_add_bf16x32(float (&v)[32], const uint4 (&w)[4], bool acc_first) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) pre[q] = ldcg_u4(src + 8 * q);
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t wq[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(wq[j]);
+      v[8 * q + 2 * j] = acc_first ? v[8 * q + 2 * j] + f.x : f.x + v[8 * q + 2 * j];
+      v[8 * q + 2 * j + 1] = acc_first ? v[8 * q + 2 * j + 1] + f.y : f.y + v[8 * q + 2 * j + 1];
     }
+  }
+}
+
+// Each epilogue returns true when some epilogue thread's wait timed out (`failed`): a
+// failed thread skips the work but reaches the same barriers, and nothing is published.
+
+// gate_up tile: accumulator columns [0, 128) gate, [128, 256) up; A was the raw x, and
+// `scale` is the row's RMSNorm scale.
+__device__ __forceinline__ bool fwd_epi_gate_up(const FwdParams& p, const FwdTask& k, int t, FwdEpi& e,
+                                                uint32_t taddr, uint32_t tempty, float scale, bool failed) {
+  const int c = e.g * 32;
+  float gv[32];
+  if (!failed) {
+    float uv[32];
+    load_acc32x2(taddr + c, taddr + 128 + c, gv, uv);
+    tc_fence_before();
+    mbar_arrive(tempty);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      gv[j] = __fmul_rn(gv[j], scale);
+      uv[j] = __fmul_rn(uv[j], scale);
+    }
+    round_bf16_inplace(gv);
+    round_bf16_inplace(uv);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) gv[j] = swiglu_f32(gv[j], uv[j]);
+  }
+  if (e.tid == 0) bulk_wait_read_all();  // the previous tile's store has read the staging tile
+  if (fwd_epi_sync_or(failed)) return true;
+  fwd_stage_write32(e.stage, e.r, c, gv);
+  fence_proxy_async_smem();
+  fwd_epi_sync();
+  if (e.tid == 0) {
+    fwd_stamp(p, t, 7);
+    fwd_stage_store(&p.maps->hidden, e.stage, k.col * 128, k.rb * kBM);
+    fwd_publish_stored(p.hid_cnt + k.rb, 1);
+    fwd_stamp(p, t, 8);
+  }
+  return false;
+}
+
+// Down tile, xw columns, in 128-column halves: x = bf16(x + bf16(acc)) on the residual the
+// staging tile holds (half 0 was loaded when the task started), stored with its sums of
+// squares; then the tile publishes the xw / 128 slices it covers.
+__device__ __forceinline__ bool fwd_epi_down(const FwdParams& p, const FwdTask& k, int t, FwdEpi& e,
+                                             uint32_t taddr, uint32_t tempty, bool failed) {
+  const int row = k.rb * kBM + e.r;
+  const int nh = p.xw / 128;
+  for (int h = 0; h < nh; ++h) {
+    const int x0 = k.col * p.xw + h * 128;
+    if (h > 0 && e.tid == 0) {
+      bulk_wait_read_all();
+      fwd_stage_load(&p.maps->x, e.stage, e.x_bar, x0, k.rb * kBM);
+      e.x_pending = true;
+    }
+    bool f = failed || !mbar_wait(e.x_bar, e.x_phase);
+    if (!f) e.x_pending = false;
+    if (!f || !e.x_pending) e.x_phase ^= 1u;  // a load still in flight keeps its phase
+    if (!f) {
+      float v[32];
+      load_acc32(taddr + h * 128 + e.g * 32, v);
+      if (h == nh - 1) {
+        tc_fence_before();
+        mbar_arrive(tempty);
+      }
+      round_bf16_inplace(v);
+      uint4 res[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) res[u] = ld_shared_v4(fwd_stage_addr(e.stage, e.r, e.g * 32 + 8 * u));
+      fwd_add_bf16x32(v, res, false);  // residual + bf16(acc)
+      round_bf16_inplace(v);
+      fwd_store_ss32(p, row, x0 + e.g * 32, v);
+      fwd_stage_write32(e.stage, e.r, e.g * 32, v);
+      fence_proxy_async_smem();
+    }
+    if (fwd_epi_sync_or(f)) return true;
+    if (e.tid == 0) fwd_stage_store(&p.maps->x, e.stage, x0, k.rb * kBM);
+  }
+  if (e.tid == 0) {
+    fwd_stamp(p, t, 7);
+    fwd_publish_stored(p.slice_cnt + k.rb, nh);
+    fwd_stamp(p, t, 8);
+  }
+  return false;
+}
+
+// Input tile K half: stores its FP32 sums in part[kh]; the half that checks in second
+// reads both halves back, adds them (P_0 + P_1, then the bias, TE's fused bias) and
+// finishes and publishes the x tile. The partial sums are stored in epilogue-thread order
+// (128-column half, float4 index q, thread) so that every warp access covers 512
+// contiguous bytes; both halves use the same thread mapping, so each thread reads back
+// its own fragments.
+__device__ __forceinline__ float4* fwd_part_frag(const FwdParams& p, const FwdTask& k, int kh, int h,
+                                                 int tid) {
+  const size_t tile = static_cast<size_t>(k.rb) * p.xti + k.col;
+  const size_t chunk = (tile * 2 + kh) * (p.xwi / 128) + h;
+  return reinterpret_cast<float4*>(p.part) + chunk * (8 * kFwdEpiThreads) + tid;
+}
+
+__device__ __forceinline__ bool fwd_epi_input(const FwdParams& p, const FwdTask& k, int t, FwdEpi& e,
+                                              uint32_t taddr, uint32_t tempty, volatile int* flag,
+                                              bool failed) {
+  const int row = k.rb * kBM + e.r;
+  const int nh = p.xwi / 128;
+  for (int h = 0; h < nh && !failed; ++h) {
     float v[32];
-    load_acc32(taddr + c, v);
-    if (ci == nchunk - 1) {
+    load_acc32(taddr + h * 128 + e.g * 32, v);
+    if (h == nh - 1) {
       tc_fence_before();
       mbar_arrive(tempty);
     }
-    if (k.type != kTaskInput) round_bf16_inplace(v);
+    float4* dst = fwd_part_frag(p, k, k.kh, h, e.tid);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint32_t wq[4] = {pre[q].x, pre[q].y, pre[q].z, pre[q].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack_bf16x2(wq[j]);
-        // input: acc + bias (TE's fused bias); down: residual + bf16(acc)
-        v[8 * q + 2 * j] = k.type == kTaskInput ? v[8 * q + 2 * j] + f.x : f.x + v[8 * q + 2 * j];
-        v[8 * q + 2 * j + 1] =
-            k.type == kTaskInput ? v[8 * q + 2 * j + 1] + f.y : f.y + v[8 * q + 2 * j + 1];
-      }
+    for (int q = 0; q < 8; ++q) {
+      dst[q * kFwdEpiThreads] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     }
-    round_bf16_inplace(v);
-    float ss = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
-    store_bf16x32(p.x + static_cast<size_t>(row) * p.d + col0, v);
-    p.ss[static_cast<size_t>(row) * (p.sj * kFwdG) + (col0 >> 7) * kFwdG + ((col0 & 127) >> 5)] = ss;
+  }
+  if (fwd_epi_sync_or(failed)) return true;
+  if (e.tid == 0) {
+    fence_acq_rel_gpu();
+    const int old = atom_add_acq_rel_gpu(p.part_cnt + k.rb * p.xti + k.col, 1);
+    *flag = old == 1;
   }
   fwd_epi_sync();
-  if (tid == 0) {
+  if (*flag == 0) return false;
+  for (int h = 0; h < nh; ++h) {
+    const int col0 = k.col * p.xwi + h * 128 + e.g * 32;
+    const float4* s0 = fwd_part_frag(p, k, 0, h, e.tid);
+    const float4* s1 = fwd_part_frag(p, k, 1, h, e.tid);
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 a = __ldcg(s0 + q * kFwdEpiThreads);
+      const float4 b = __ldcg(s1 + q * kFwdEpiThreads);
+      v[4 * q] = a.x + b.x;
+      v[4 * q + 1] = a.y + b.y;
+      v[4 * q + 2] = a.z + b.z;
+      v[4 * q + 3] = a.w + b.w;
+    }
+    uint4 bias[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) bias[q] = *reinterpret_cast<const uint4*>(p.bias + col0 + 8 * q);
+    fwd_add_bf16x32(v, bias, true);
+    round_bf16_inplace(v);
+    fwd_store_ss32(p, row, col0, v);
+    if (e.tid == 0) bulk_wait_read_all();
+    fwd_epi_sync();
+    fwd_stage_write32(e.stage, e.r, e.g * 32, v);
+    fence_proxy_async_smem();
+    fwd_epi_sync();
+    if (e.tid == 0) fwd_stage_store(&p.maps->x, e.stage, k.col * p.xwi + h * 128, k.rb * kBM);
+  }
+  if (e.tid == 0) {
     fwd_stamp(p, t, 7);
-    fence_acq_rel_gpu();
-    fence_proxy_async_global();
-    red_add_relaxed_gpu(p.slice_cnt + k.rb, nchunk);
+    fwd_publish_stored(p.slice_cnt + k.rb, nh);
     fwd_stamp(p, t, 8);
   }
+  return false;
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -273,9 +433,11 @@ struct FwdSmem {
   static constexpr int kBBytesMax = 256 * kBK * 2;       // 32 KB (gate + up boxes)
   static constexpr int kStageBytes = kABytes + kBBytesMax;
   static constexpr int kRingBytes = kFwdNStage * kStageBytes;
-  static constexpr int kBarriers = 2 * kFwdNStage + 4 + 2 * kFwdTaskRing + 1;
+  static constexpr int kOutBytes = kBM * 128 * 2;         // 32 KB staging tile
+  // full[s], empty[s], tfull[2], tempty[2], task_full[q], task_empty[q], drain, x_bar
+  static constexpr int kBarriers = 2 * kFwdNStage + 4 + 2 * kFwdTaskRing + 2;
   static constexpr int kMiscBytes = kBarriers * 8 + kFwdTaskRing * 4 + 16;
-  static constexpr int kBytes = 1024 + kRingBytes + kMiscBytes;
+  static constexpr int kBytes = 1024 + kRingBytes + kOutBytes + kMiscBytes;
   static_assert(kBytes <= 232448, "shared memory budget exceeded");
 };
 
@@ -287,17 +449,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
   uint8_t* smem = smem_raw + pad;
   base += pad;
 
-  const uint32_t bar_base = base + L::kRingBytes;
+  const uint32_t stage_out = base + L::kRingBytes;
+  const uint32_t bar_base = stage_out + L::kOutBytes;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (kFwdNStage + s); };
   auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * kFwdNStage + a); };
   auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * kFwdNStage + 2 + a); };
   auto task_full = [&](int q) { return bar_base + 8u * (2 * kFwdNStage + 4 + q); };
   auto task_empty = [&](int q) { return bar_base + 8u * (2 * kFwdNStage + 4 + kFwdTaskRing + q); };
-  const uint32_t drain_bar = bar_base + 8u * (L::kBarriers - 1);
+  const uint32_t drain_bar = bar_base + 8u * (L::kBarriers - 2);
+  const uint32_t x_bar = bar_base + 8u * (L::kBarriers - 1);
   volatile int* task_slot =
-      reinterpret_cast<volatile int*>(smem + L::kRingBytes + L::kBarriers * 8);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(task_slot + kFwdTaskRing + 1));
+      reinterpret_cast<volatile int*>(smem + L::kRingBytes + L::kOutBytes + L::kBarriers * 8);
+  volatile int* flag = task_slot + kFwdTaskRing;  // input-tile check-in result
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(flag + 1));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -316,6 +481,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       mbar_init(task_empty(q), 1 + kFwdEpiThreads);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(x_bar, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -364,9 +530,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
           if (k.type == kTaskInput) {
             ma = &maps->a_in;
             mb = &maps->w_in;
-            kb1 = p.kb_in;
-            b_row = k.col * p.xw;
-            if (p.xw == 256) b_row2 = b_row + 128;
+            kb0 = k.kh * p.kb_in / 2;
+            kb1 = (k.kh + 1) * p.kb_in / 2;
+            b_row = k.col * p.xwi;
+            if (p.xwi == 256) b_row2 = b_row + 128;
           } else if (k.type == kTaskGateUp) {
             if (!wait_counter(p.slice_cnt + k.rb, (k.layer + 1) * p.sj)) {
               record_error(p.err, kErrTimeoutDependency);
@@ -441,8 +608,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         mbar_arrive(task_empty(q));
         if (t < 0) break;
         const FwdTask k = fwd_decode(p, t);
-        const int nkb = k.type == kTaskInput ? p.kb_in : (k.type == kTaskGateUp ? p.d : p.h) / kBK;
-        const uint32_t idesc = idesc_bf16(kBM, k.type == kTaskGateUp ? 256 : p.xw);
+        const int nkb = k.type == kTaskInput ? (k.kh + 1) * p.kb_in / 2 - k.kh * p.kb_in / 2
+                                             : (k.type == kTaskGateUp ? p.d : p.h) / kBK;
+        const int n_mma = k.type == kTaskGateUp ? 256 : (k.type == kTaskInput ? p.xwi : p.xw);
+        const uint32_t idesc = idesc_bf16(kBM, n_mma);
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u)) {
           record_error(p.err, kErrTimeoutMma);
           break;
@@ -484,53 +653,64 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
     __syncwarp();
   } else {
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const int g = (warp - 2) >> 2;
-    const int tid = threadIdx.x - 64;
+    FwdEpi e{stage_out, x_bar, 0u, quarter * 32 + lane, (warp - 2) >> 2, static_cast<int>(threadIdx.x) - 64,
+             false};
+    const FwdMaps* maps = p.maps;
     int acc = 0;
     uint32_t acc_phase = 0;
+    // Every epilogue thread takes the same branches and barriers; a timed-out wait is
+    // ORed into the next barrier, after which all epilogue threads stop together.
     for (int i = 0;; ++i) {
       const int q = i % kFwdTaskRing;
-      if (!mbar_wait(task_full(q), (i / kFwdTaskRing) & 1)) {
+      bool failed = !mbar_wait(task_full(q), (i / kFwdTaskRing) & 1);
+      const int t = failed ? -1 : task_slot[q];
+      if (!failed) mbar_arrive(task_empty(q));
+      if (fwd_epi_sync_or(failed)) {
         record_error(p.err, kErrTimeoutEpilogue);
         break;
       }
-      const int t = task_slot[q];
-      mbar_arrive(task_empty(q));
       if (t < 0) break;
       const FwdTask k = fwd_decode(p, t);
       // Global inputs of the epilogue, fetched while the MMAs run (the producer published
-      // the task after its dependencies completed).
+      // the task after its dependencies completed): the row scale, or the first 128
+      // columns of the residual into the staging tile once the previous store read it.
       float scale = 1.0f;
-      uint4 pre[4];
       if (k.type == kTaskGateUp) {
-        scale = fwd_row_scale(p, k.rb * kBM + r);
-      } else {
-        const int col0 = k.col * p.xw + g * (p.xw / 4);
-        const __nv_bfloat16* src = k.type == kTaskDown
-                                       ? p.x + static_cast<size_t>(k.rb * kBM + r) * p.d + col0
-                                       : p.bias + col0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) pre[q] = ldcg_u4(src + 8 * q);
+        scale = fwd_row_scale(p, k.rb * kBM + e.r);
+      } else if (k.type == kTaskDown && e.tid == 0) {
+        bulk_wait_read_all();
+        fence_proxy_async_global();
+        fwd_stage_load(&maps->x, e.stage, e.x_bar, k.col * p.xw, k.rb * kBM);
+        e.x_pending = true;
       }
-      if (!mbar_wait(tfull_bar(acc), acc_phase)) {
+      failed = !mbar_wait(tfull_bar(acc), acc_phase);
+      tc_fence_after();
+      if (e.tid == 0) fwd_stamp(p, t, 5);
+      const uint32_t taddr =
+          tmem_base + static_cast<uint32_t>(acc * 256) + (static_cast<uint32_t>(quarter * 32) << 16);
+      bool abort;
+      if (k.type == kTaskGateUp) {
+        abort = fwd_epi_gate_up(p, k, t, e, taddr, tempty_bar(acc), scale, failed);
+      } else if (k.type == kTaskDown) {
+        abort = fwd_epi_down(p, k, t, e, taddr, tempty_bar(acc), failed);
+      } else {
+        abort = fwd_epi_input(p, k, t, e, taddr, tempty_bar(acc), flag, failed);
+      }
+      if (abort) {
         record_error(p.err, kErrTimeoutEpilogue);
         break;
       }
-      tc_fence_after();
-      if (tid == 0) fwd_stamp(p, t, 5);
-      const uint32_t taddr =
-          tmem_base + static_cast<uint32_t>(acc * 256) + (static_cast<uint32_t>(quarter * 32) << 16);
-      if (k.type == kTaskGateUp) {
-        fwd_epi_gate_up(p, k, t, r, g, tid, taddr, tempty_bar(acc), scale);
-      } else {
-        fwd_epi_slice(p, k, t, r, g, tid, taddr, tempty_bar(acc), pre);
-      }
-      if (tid == 0) fwd_stamp(p, t, 6);
+      if (e.tid == 0) fwd_stamp(p, t, 6);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    // The last tile's stores complete before the CTA retires; a residual load issued for a
+    // task that then timed out lands before the shared memory is released.
+    if (e.tid == 0) {
+      bulk_wait_all();
+      if (e.x_pending) mbar_wait(e.x_bar, e.x_phase);
     }
   }
 

@@ -34,8 +34,10 @@ struct FwdParams {
   __nv_bfloat16* x;           // [rows_cap, d]
   __nv_bfloat16* hidden;      // [rows_cap, h]
   float* ss;                  // [rows_cap, sj * kFwdG] partial sums of squares of x
+  float* part;                // [2, rows_cap, d] FP32 K-half sums of the input tiles
   int* hid_cnt;               // [nb] finished gate_up tiles
   int* slice_cnt;             // [nb] finished 128-column x slices
+  int* part_cnt;              // [nb * xti] K halves of each input tile that finished
   int* task_counter;          // [1]
   int* err;
   int rows_cap;
@@ -43,8 +45,10 @@ struct FwdParams {
   int d, h, depth;
   int sj;      // d / 128 column slices (the granularity of slice_cnt and ss)
   int nc;      // h / 128 hidden chunks
-  int xw;      // column width of the input and down tiles (128 or 256)
-  int xt;      // d / xw input (and down) tiles per row block
+  int xw;      // column width of the down tiles (128 or 256, per forward)
+  int xt;      // d / xw down tiles per row block
+  int xwi;     // column width of the input tiles (256 where d allows, else 128)
+  int xti;     // d / xwi input tiles per row block (each computed as two K halves)
   int kb_in;   // k-blocks of the input GEMM (in_dim / 64)
   int total_tasks;
   float eps;

@@ -355,7 +355,9 @@ void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMa
 void dense_forward(const FwdParams& p, cudaStream_t s) {
   require(p.total_tasks >= 1 && p.depth >= 1 && p.depth <= kFwdMaxDepth && p.kb_in >= 1 &&
               p.d % 128 == 0 && p.d / 128 <= kFwdMaxSlices && p.h % 128 == 0 &&
-              (p.xw == 128 || p.xw == 256) && p.d % p.xw == 0 && p.xt == p.d / p.xw,
+              (p.xw == 128 || p.xw == 256) && p.d % p.xw == 0 && p.xt == p.d / p.xw &&
+              (p.xwi == 128 || p.xwi == 256) && p.d % p.xwi == 0 && p.xti == p.d / p.xwi &&
+              p.kb_in >= 2,
           "persistent forward: unsupported shape");
   auto kernel = dense_forward_kernel;
   ensure_smem(kernel, FwdSmem::kBytes);

@@ -134,7 +134,8 @@ void Model::plan_workspace() {
     const size_t sj = static_cast<size_t>(d / 128);
     const size_t nb = r / 128;
     ws_off.fwd_ss = take(r * sj * kFwdG * 4);
-    fwd_sync_bytes = (2 * nb + 1) * 4;
+    ws_off.fwd_part = take(2 * r * d * 4);
+    fwd_sync_bytes = (2 * nb + nb * sj + 1) * 4;
     ws_off.fwd_sync = take(fwd_sync_bytes);
   }
   if (cfg.arch == CE4B_ARCH_MOE64A2) {
@@ -422,9 +423,11 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);
   p.ss = reinterpret_cast<float*>(workspace + ws_off.fwd_ss);
   p.sj = d / 128;
+  p.part = reinterpret_cast<float*>(workspace + ws_off.fwd_part);
   p.hid_cnt = sync;
   p.slice_cnt = sync + nb_cap;
-  p.task_counter = sync + 2 * nb_cap;
+  p.part_cnt = sync + 2 * nb_cap;
+  p.task_counter = sync + 2 * nb_cap + nb_cap * p.sj;
   p.err = device_error_word();
   p.rows_cap = rows_cap;
   p.nb = (batch + 127) / 128;
@@ -434,6 +437,8 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.nc = dense_hidden / 128;
   p.xw = fused_xw(batch);
   p.xt = d / p.xw;
+  p.xwi = fused_xwi();
+  p.xti = d / p.xwi;
   p.kb_in = in_dim / kFwdKBlock;
   p.total_tasks = fused_task_count(batch);
   p.eps = cfg.rms_norm_eps;

@@ -46,7 +46,7 @@ struct Model {
     size_t expert_start = 0, m_tiles = 0, num_m_tiles = 0, xperm = 0, pprob = 0, hperm = 0;
     size_t yperm = 0;
     size_t a_codes = 0, a_scales = 0, n_codes = 0, n_scales = 0, h_codes = 0, h_scales = 0;
-    size_t fwd_ss = 0, fwd_sync = 0;  // persistent dense forward
+    size_t fwd_ss = 0, fwd_part = 0, fwd_sync = 0;  // persistent dense forward
   };
 
   ce4b_model_config cfg{};
@@ -82,9 +82,11 @@ struct Model {
     const int nb = (batch + 127) / 128;
     return cfg.d_model % 256 == 0 && nb * (cfg.d_model / 256) >= 2 * sm_count() ? 256 : 128;
   }
+  // Input tiles: 256 columns where d allows (each computed as two K halves).
+  int fused_xwi() const { return cfg.d_model % 256 == 0 ? 256 : 128; }
   int fused_task_count(int batch) const {
     const int nb = (batch + 127) / 128, xt = cfg.d_model / fused_xw(batch), nc = dense_hidden / 128;
-    return nb * xt + cfg.depth * nb * (nc + xt);
+    return nb * (cfg.d_model / fused_xwi()) * 2 + cfg.depth * nb * (nc + xt);
   }
   uint8_t* mx_arena = nullptr;    // quantised weights (codes + scales)
   size_t mx_arena_bytes = 0;

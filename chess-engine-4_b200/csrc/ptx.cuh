@@ -369,6 +369,21 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ORs a predicate over its `count` threads: every thread gets the
+// same result, so a decision taken on it (e.g. to stop after a timed-out wait) is uniform.
+__device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA with
 // 128-byte swizzling: rows of 64 BF16 (128 B), 8-row core groups 1024 B apart.
 // Fields: start address >> 4 (bits 0-13), leading byte offset >> 4 (16-29, unused for
