@@ -198,18 +198,50 @@ __device__ __forceinline__ float fwd_row_scale(const FwdParams& p, int row) {
 // ------------------------------------------------------------------ staged tile output
 // Epilogues write their BF16 tiles through a 32 KB staging tile in shared memory (two
 // 64-column TMA boxes of 128 rows, 128-byte swizzle: row r's 16-byte unit u sits at
-// r * 128 + ((u ^ (r & 7)) * 16)) and one thread stores it with TMA. A thread owns one row
-// and 32 consecutive columns, so writing global memory directly would touch 32 lines per
-// warp instruction; the swizzled staging writes are conflict-free and the TMA store is
-// fully coalesced. Down tiles also load their residual into the staging tile with TMA and
-// overwrite it in place with the result.
+// r * 128 + ((u ^ (r & 7)) * 16)). A thread owns one row and 32 consecutive columns, so
+// writing global memory directly would touch 32 lines per warp instruction; the swizzled
+// staging writes are conflict-free and the TMA store is fully coalesced. Down tiles also
+// load their residual into the staging tile with TMA and overwrite it in place.
+//
+// A store warp takes each filled staging tile (stage_full, with a job record: tensor map,
+// coordinates, counter to publish), issues its TMA store, returns the buffer as soon as
+// the store has read it (stage_free), then waits for the store to complete and publishes.
+// The epilogue warps go on to the next tile meanwhile.
 struct FwdEpi {
-  uint32_t stage;    // staging tile
-  uint32_t x_bar;    // mbarrier of the residual load into the staging tile
-  uint32_t x_phase;  // parity of its next phase
-  int r, g, tid;     // row in the tile, 32-column group, epilogue thread index
-  bool x_pending;    // (thread 0) a residual load was issued and not yet waited for
+  uint32_t stage;      // staging tile
+  uint32_t x_bar;      // mbarrier of the residual load into the staging tile
+  uint32_t full_bar;   // stage_full (count 1: epilogue thread 0)
+  uint32_t free_bar;   // stage_free (count 1: the store thread)
+  uint32_t x_phase;    // parity of x_bar's next phase
+  uint32_t uses;       // staging tiles handed over so far
+  int r, g, tid;       // row in the tile, 32-column group, epilogue thread index
+  bool x_pending;      // (thread 0) a residual load was issued and not yet waited for
+  volatile int* job;   // job record: map, x0, y0, counter kind, row block, increment, task
 };
+
+enum FwdStoreMap : int { kStoreStop = -1, kStoreHidden = 0, kStoreX = 1 };
+enum FwdCounter : int { kCounterNone = 0, kCounterHidden = 1, kCounterSlice = 2 };
+
+// All epilogue threads: wait until the store warp has read the staging tile of the
+// previous hand-over. Returns true on a timed-out wait.
+__device__ __forceinline__ bool fwd_stage_acquire(FwdEpi& e, bool failed) {
+  const bool f = failed || !mbar_wait(e.free_bar, (e.uses & 1u) ^ 1u);
+  return f;
+}
+
+// Epilogue thread 0, after the barrier that follows the staging writes: hand the tile to
+// the store warp.
+__device__ __forceinline__ void fwd_stage_post(FwdEpi& e, int map, int x0, int y0, int counter, int rb,
+                                               int inc, int t) {
+  e.job[0] = map;
+  e.job[1] = x0;
+  e.job[2] = y0;
+  e.job[3] = counter;
+  e.job[4] = rb;
+  e.job[5] = inc;
+  e.job[6] = t;
+  mbar_arrive(e.full_bar);
+}
 
 __device__ __forceinline__ uint32_t fwd_stage_addr(uint32_t stage, int r, int c) {
   return stage + static_cast<uint32_t>((c >> 6) * 16384 + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4));
@@ -224,28 +256,12 @@ __device__ __forceinline__ void fwd_stage_write32(uint32_t stage, int r, int c, 
   }
 }
 
-// TMA-store the staging tile to columns [x0, x0 + 128) of rows [y0, y0 + 128).
-__device__ __forceinline__ void fwd_stage_store(const CUtensorMap* map, uint32_t stage, int x0, int y0) {
-  tma_store_2d(map, stage, x0, y0);
-  tma_store_2d(map, stage + 16384, x0 + 64, y0);
-  bulk_commit();
-}
-
 // Load columns [x0, x0 + 128) of rows [y0, y0 + 128) into the staging tile.
 __device__ __forceinline__ void fwd_stage_load(const CUtensorMap* map, uint32_t stage, uint32_t bar, int x0,
                                                int y0) {
   mbar_arrive_expect_tx(bar, 32768);
   tma_load_2d(stage, map, bar, x0, y0);
   tma_load_2d(stage + 16384, map, bar, x0 + 64, y0);
-}
-
-// Publish after this thread's TMA stores: wait until they are complete, order them before
-// the GPU-scope release, and count the tile.
-__device__ __forceinline__ void fwd_publish_stored(int* counter, int v) {
-  bulk_wait_all();
-  fence_proxy_async_global();
-  fence_acq_rel_gpu();
-  red_add_relaxed_gpu(counter, v);
 }
 
 // Sum of squares of 32 finished BF16 values of x, stored per (row, 128-column slice,
@@ -294,17 +310,17 @@ __device__ __forceinline__ bool fwd_epi_gate_up(const FwdParams& p, const FwdTas
 #pragma unroll
     for (int j = 0; j < 32; ++j) gv[j] = swiglu_f32(gv[j], uv[j]);
   }
-  if (e.tid == 0) bulk_wait_read_all();  // the previous tile's store has read the staging tile
+  failed = fwd_stage_acquire(e, failed);
+  if (!failed) {
+    fwd_stage_write32(e.stage, e.r, c, gv);
+    fence_proxy_async_smem();
+  }
   if (fwd_epi_sync_or(failed)) return true;
-  fwd_stage_write32(e.stage, e.r, c, gv);
-  fence_proxy_async_smem();
-  fwd_epi_sync();
   if (e.tid == 0) {
     fwd_stamp(p, t, 7);
-    fwd_stage_store(&p.maps->hidden, e.stage, k.col * 128, k.rb * kBM);
-    fwd_publish_stored(p.hid_cnt + k.rb, 1);
-    fwd_stamp(p, t, 8);
+    fwd_stage_post(e, kStoreHidden, k.col * 128, k.rb * kBM, kCounterHidden, k.rb, 1, t);
   }
+  ++e.uses;
   return false;
 }
 
@@ -317,12 +333,17 @@ __device__ __forceinline__ bool fwd_epi_down(const FwdParams& p, const FwdTask& 
   const int nh = p.xw / 128;
   for (int h = 0; h < nh; ++h) {
     const int x0 = k.col * p.xw + h * 128;
-    if (h > 0 && e.tid == 0) {
-      bulk_wait_read_all();
-      fwd_stage_load(&p.maps->x, e.stage, e.x_bar, x0, k.rb * kBM);
-      e.x_pending = true;
+    bool f = failed;
+    if (h > 0) {
+      // Half 0 was handed over: wait for the buffer, then load this half's residual.
+      f = fwd_stage_acquire(e, f);
+      if (e.tid == 0 && !f) {
+        fence_proxy_async_global();
+        fwd_stage_load(&p.maps->x, e.stage, e.x_bar, x0, k.rb * kBM);
+        e.x_pending = true;
+      }
     }
-    bool f = failed || !mbar_wait(e.x_bar, e.x_phase);
+    f = f || !mbar_wait(e.x_bar, e.x_phase);
     if (!f) e.x_pending = false;
     if (!f || !e.x_pending) e.x_phase ^= 1u;  // a load still in flight keeps its phase
     if (!f) {
@@ -343,12 +364,11 @@ __device__ __forceinline__ bool fwd_epi_down(const FwdParams& p, const FwdTask& 
       fence_proxy_async_smem();
     }
     if (fwd_epi_sync_or(f)) return true;
-    if (e.tid == 0) fwd_stage_store(&p.maps->x, e.stage, x0, k.rb * kBM);
-  }
-  if (e.tid == 0) {
-    fwd_stamp(p, t, 7);
-    fwd_publish_stored(p.slice_cnt + k.rb, nh);
-    fwd_stamp(p, t, 8);
+    if (e.tid == 0) {
+      if (h == nh - 1) fwd_stamp(p, t, 7);
+      fwd_stage_post(e, kStoreX, x0, k.rb * kBM, h == nh - 1 ? kCounterSlice : kCounterNone, k.rb, nh, t);
+    }
+    ++e.uses;
   }
   return false;
 }
@@ -412,17 +432,18 @@ __device__ __forceinline__ bool fwd_epi_input(const FwdParams& p, const FwdTask&
     fwd_add_bf16x32(v, bias, true);
     round_bf16_inplace(v);
     fwd_store_ss32(p, row, col0, v);
-    if (e.tid == 0) bulk_wait_read_all();
-    fwd_epi_sync();
-    fwd_stage_write32(e.stage, e.r, e.g * 32, v);
-    fence_proxy_async_smem();
-    fwd_epi_sync();
-    if (e.tid == 0) fwd_stage_store(&p.maps->x, e.stage, k.col * p.xwi + h * 128, k.rb * kBM);
-  }
-  if (e.tid == 0) {
-    fwd_stamp(p, t, 7);
-    fwd_publish_stored(p.slice_cnt + k.rb, nh);
-    fwd_stamp(p, t, 8);
+    const bool f = fwd_stage_acquire(e, false);
+    if (!f) {
+      fwd_stage_write32(e.stage, e.r, e.g * 32, v);
+      fence_proxy_async_smem();
+    }
+    if (fwd_epi_sync_or(f)) return true;
+    if (e.tid == 0) {
+      if (h == nh - 1) fwd_stamp(p, t, 7);
+      fwd_stage_post(e, kStoreX, k.col * p.xwi + h * 128, k.rb * kBM,
+                     h == nh - 1 ? kCounterSlice : kCounterNone, k.rb, nh, t);
+    }
+    ++e.uses;
   }
   return false;
 }
@@ -434,9 +455,11 @@ struct FwdSmem {
   static constexpr int kStageBytes = kABytes + kBBytesMax;
   static constexpr int kRingBytes = kFwdNStage * kStageBytes;
   static constexpr int kOutBytes = kBM * 128 * 2;         // 32 KB staging tile
-  // full[s], empty[s], tfull[2], tempty[2], task_full[q], task_empty[q], drain, x_bar
-  static constexpr int kBarriers = 2 * kFwdNStage + 4 + 2 * kFwdTaskRing + 2;
-  static constexpr int kMiscBytes = kBarriers * 8 + kFwdTaskRing * 4 + 16;
+  // full[s], empty[s], tfull[2], tempty[2], task_full[q], task_empty[q], drain, x_bar,
+  // stage_full, stage_free
+  static constexpr int kBarriers = 2 * kFwdNStage + 4 + 2 * kFwdTaskRing + 4;
+  static constexpr int kJobInts = 8;  // store job record
+  static constexpr int kMiscBytes = kBarriers * 8 + kFwdTaskRing * 4 + 16 + kJobInts * 4;
   static constexpr int kBytes = 1024 + kRingBytes + kOutBytes + kMiscBytes;
   static_assert(kBytes <= 232448, "shared memory budget exceeded");
 };
@@ -457,12 +480,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
   auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * kFwdNStage + 2 + a); };
   auto task_full = [&](int q) { return bar_base + 8u * (2 * kFwdNStage + 4 + q); };
   auto task_empty = [&](int q) { return bar_base + 8u * (2 * kFwdNStage + 4 + kFwdTaskRing + q); };
-  const uint32_t drain_bar = bar_base + 8u * (L::kBarriers - 2);
-  const uint32_t x_bar = bar_base + 8u * (L::kBarriers - 1);
+  const uint32_t drain_bar = bar_base + 8u * (L::kBarriers - 4);
+  const uint32_t x_bar = bar_base + 8u * (L::kBarriers - 3);
+  const uint32_t stage_full = bar_base + 8u * (L::kBarriers - 2);
+  const uint32_t stage_free = bar_base + 8u * (L::kBarriers - 1);
   volatile int* task_slot =
       reinterpret_cast<volatile int*>(smem + L::kRingBytes + L::kOutBytes + L::kBarriers * 8);
   volatile int* flag = task_slot + kFwdTaskRing;  // input-tile check-in result
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(flag + 1));
+  volatile int* job = flag + 4;                   // store job record (kJobInts)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -482,6 +508,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
     }
     mbar_init(drain_bar, 1);
     mbar_init(x_bar, 1);
+    mbar_init(stage_full, 1);
+    mbar_init(stage_free, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -651,10 +679,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       if (!mbar_wait(drain_bar, 0)) record_error(p.err, kErrTimeoutDrain);
     }
     __syncwarp();
-  } else {
+  } else if (warp < kFwdStoreWarp) {
     const int quarter = warp & 3;
-    FwdEpi e{stage_out, x_bar, 0u, quarter * 32 + lane, (warp - 2) >> 2, static_cast<int>(threadIdx.x) - 64,
-             false};
+    FwdEpi e{stage_out, x_bar, stage_full, stage_free, 0u, 0u, quarter * 32 + lane, (warp - 2) >> 2,
+             static_cast<int>(threadIdx.x) - 64, false, job};
     const FwdMaps* maps = p.maps;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -677,13 +705,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       float scale = 1.0f;
       if (k.type == kTaskGateUp) {
         scale = fwd_row_scale(p, k.rb * kBM + e.r);
-      } else if (k.type == kTaskDown && e.tid == 0) {
-        bulk_wait_read_all();
-        fence_proxy_async_global();
-        fwd_stage_load(&maps->x, e.stage, e.x_bar, k.col * p.xw, k.rb * kBM);
-        e.x_pending = true;
+      } else if (k.type == kTaskDown) {
+        failed = fwd_stage_acquire(e, false);
+        if (e.tid == 0 && !failed) {
+          fence_proxy_async_global();
+          fwd_stage_load(&maps->x, e.stage, e.x_bar, k.col * p.xw, k.rb * kBM);
+          e.x_pending = true;
+        }
       }
-      failed = !mbar_wait(tfull_bar(acc), acc_phase);
+      failed = !mbar_wait(tfull_bar(acc), acc_phase) || failed;
       tc_fence_after();
       if (e.tid == 0) fwd_stamp(p, t, 5);
       const uint32_t taddr =
@@ -706,12 +736,41 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         acc_phase ^= 1u;
       }
     }
-    // The last tile's stores complete before the CTA retires; a residual load issued for a
+    // Stop the store warp once it has taken the last tile; a residual load issued for a
     // task that then timed out lands before the shared memory is released.
     if (e.tid == 0) {
-      bulk_wait_all();
+      if (mbar_wait(e.free_bar, (e.uses & 1u) ^ 1u)) fwd_stage_post(e, kStoreStop, 0, 0, 0, 0, 0, -1);
       if (e.x_pending) mbar_wait(e.x_bar, e.x_phase);
     }
+  } else if (warp == kFwdStoreWarp) {
+    if (lane == 0) {
+      const FwdMaps* maps = p.maps;
+      for (uint32_t n = 0;; ++n) {
+        if (!mbar_wait(stage_full, n & 1u)) {
+          record_error(p.err, kErrTimeoutEpilogue);
+          break;
+        }
+        const int map = job[0];
+        if (map == kStoreStop) break;
+        const int x0 = job[1], y0 = job[2], counter = job[3], rb = job[4], inc = job[5], t = job[6];
+        const CUtensorMap* m = map == kStoreHidden ? &maps->hidden : &maps->x;
+        tma_store_2d(m, stage_out, x0, y0);
+        tma_store_2d(m, stage_out + 16384, x0 + 64, y0);
+        bulk_commit();
+        bulk_wait_read_all();
+        mbar_arrive(stage_free);
+        if (counter != kCounterNone) {
+          // Every store of the tile is complete before the GPU-scope release.
+          bulk_wait_all();
+          fence_proxy_async_global();
+          fence_acq_rel_gpu();
+          red_add_relaxed_gpu((counter == kCounterHidden ? p.hid_cnt : p.slice_cnt) + rb, inc);
+          fwd_stamp(p, t, 8);
+        }
+      }
+      bulk_wait_all();
+    }
+    __syncwarp();
   }
 
   __syncthreads();

@@ -12,8 +12,10 @@ constexpr int kFwdMaxSlices = 8;  // d / 128 <= 8 (d <= 1024)
 constexpr int kFwdNStage = 4;
 constexpr int kFwdTaskRing = 4;
 constexpr int kFwdG = 4;
-constexpr int kFwdThreads = 64 + 128 * kFwdG;
+// warp 0 TMA producer, warp 1 MMA issuer, 16 epilogue warps, then one store warp
 constexpr int kFwdEpiThreads = 128 * kFwdG;
+constexpr int kFwdStoreWarp = 2 + 4 * kFwdG;
+constexpr int kFwdThreads = 64 + kFwdEpiThreads + 32;
 constexpr int kErrTimeoutDependency = 7;
 
 enum FwdTaskType : int { kTaskEnd = -1, kTaskInput = 0, kTaskGateUp = 1, kTaskDown = 2 };
