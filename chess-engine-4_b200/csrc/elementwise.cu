@@ -16,29 +16,49 @@ __device__ __forceinline__ int source_plane(int p, int history_planes) {
 }
 
 // Blocks take positions; a thread writes 8 squares (one 16-byte BF16 chunk) of one selected
-// plane (32-bit in-position indexing; consecutive threads write consecutive chunks).
+// plane, for up to kExpandPer chunks of the position, blockDim apart (consecutive threads
+// write consecutive chunks). All of a thread's record loads are issued before its stores,
+// so that each thread keeps several independent loads in flight (32-bit in-position
+// indexing).
+constexpr int kExpandPer = 4;
+
 __global__ void expand_lc0_kernel(const ce4b_input_plane* __restrict__ planes, bf16* __restrict__ out,
                                   int batch, int history) {
+  static_assert(sizeof(ce4b_input_plane) == 16, "InputPlane is 16 bytes");
   const int sel = selected_planes(history);
   const int hp = history * kPlanesPerHistory;
-  for (int64_t b = blockIdx.x; b < batch; b += gridDim.x)
-  for (int c = threadIdx.x; c < sel * 8; c += blockDim.x) {
-    const int chunk = c & 7;
-    const int p = c >> 3;
-    const int64_t i = b * sel * 8 + c;
-    const ce4b_input_plane pl = planes[b * kInputPlanes + source_plane(p, hp)];
-    float v = pl.value;
-    if (p == hp + 5) v = v / 99.0f;
-    const uint32_t bits = static_cast<uint32_t>(pl.mask >> (chunk * 8)) & 0xFFu;
-    float f[8];
+  const int nchunk = sel * 8;
+  for (int64_t b = blockIdx.x; b < batch; b += gridDim.x) {
+    const uint4* rec = reinterpret_cast<const uint4*>(planes + b * kInputPlanes);
+    uint4* dst = reinterpret_cast<uint4*>(out) + b * nchunk;
+    for (int c0 = 0; c0 < nchunk; c0 += kExpandPer * blockDim.x) {
+      uint4 pl[kExpandPer];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = ((bits >> j) & 1u) ? v : 0.0f;
-    uint4 o;
-    o.x = pack_bf16x2(f[0], f[1]);
-    o.y = pack_bf16x2(f[2], f[3]);
-    o.z = pack_bf16x2(f[4], f[5]);
-    o.w = pack_bf16x2(f[6], f[7]);
-    reinterpret_cast<uint4*>(out)[i] = o;
+      for (int u = 0; u < kExpandPer; ++u) {
+        const int c = c0 + u * blockDim.x + threadIdx.x;
+        if (c < nchunk) pl[u] = __ldg(rec + source_plane(c >> 3, hp));
+      }
+#pragma unroll
+      for (int u = 0; u < kExpandPer; ++u) {
+        const int c = c0 + u * blockDim.x + threadIdx.x;
+        if (c >= nchunk) continue;
+        const int chunk = c & 7;
+        const int p = c >> 3;
+        const uint64_t mask = static_cast<uint64_t>(pl[u].x) | (static_cast<uint64_t>(pl[u].y) << 32);
+        float v = __uint_as_float(pl[u].z);
+        if (p == hp + 5) v = v / 99.0f;
+        const uint32_t bits = static_cast<uint32_t>(mask >> (chunk * 8)) & 0xFFu;
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = ((bits >> j) & 1u) ? v : 0.0f;
+        uint4 o;
+        o.x = pack_bf16x2(f[0], f[1]);
+        o.y = pack_bf16x2(f[2], f[3]);
+        o.z = pack_bf16x2(f[4], f[5]);
+        o.w = pack_bf16x2(f[6], f[7]);
+        dst[c] = o;
+      }
+    }
   }
 }
 
@@ -264,8 +284,8 @@ void expand_input(int layout, const void* input, const void* scalars, int batch,
   const int grid = std::max(1, std::min(batch, sm_count() * 16));
   switch (layout) {
     case CE4B_INPUT_LC0:
-      expand_lc0_kernel<<<grid, threads, 0, s>>>(static_cast<const ce4b_input_plane*>(input), out,
-                                                 batch, history);
+      expand_lc0_kernel<<<std::max(1, std::min(batch, sm_count() * 8)), threads, 0, s>>>(
+          static_cast<const ce4b_input_plane*>(input), out, batch, history);
       break;
     case CE4B_INPUT_F32_PLANES:
       expand_dense_kernel<float><<<grid, threads, 0, s>>>(

@@ -163,11 +163,11 @@ def test_forward_normalizes_rule50_in_place_like_reference() -> None:
 @pytest.mark.parametrize(
     "d,depth,ratio,batch",
     [
-        (512, 12, 3.0, 4096),  # cluster kernel, K-split input/down tiles (the benchmark shape)
-        (512, 3, 3.0, 200),  # cluster kernel, ragged last row block
-        (1024, 2, 3.0, 300),  # cluster kernel, one 256-column block per CTA
-        (256, 4, 3.0, 300),  # task-queue kernel
-        (128, 2, 3.0, 7),  # task-queue kernel, one partial row block
+        (512, 12, 3.0, 4096),  # the benchmark shape
+        (512, 3, 3.0, 200),  # ragged last row block
+        (1024, 2, 3.0, 300),  # four 256-column input tiles per row block
+        (256, 4, 3.0, 300),
+        (128, 2, 3.0, 7),  # 128-column input tiles, one partial row block
     ],
 )
 def test_persistent_forward_matches_folded_restatement(d: int, depth: int, ratio: float, batch: int) -> None:
