@@ -93,27 +93,6 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
   return old;
 }
 
-__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
-// Waits until *ptr >= target (bounded). Returns false after kWaitLimitNs.
-__device__ __forceinline__ bool wait_counter(const int* ptr, int target) {
-  if (ld_acquire_gpu(ptr) >= target) return true;
-  const unsigned long long start = global_timer_ns();
-  while (true) {
-    __nanosleep(64);
-    if (ld_acquire_gpu(ptr) >= target) return true;
-    if (global_timer_ns() - start > kWaitLimitNs) return false;
-  }
-}
-
 __device__ __forceinline__ uint4 ldcg_u4(const void* ptr) {
   return __ldcg(reinterpret_cast<const uint4*>(ptr));
 }

@@ -446,8 +446,11 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.trace_cap = fwd_trace_cap;
   dense_forward(p, s);
   trace("dense_tower", s);
+  // The heads start on each row block as soon as its last layer is published, while the
+  // tower finishes the others (the tower never waits on the heads).
   gemm_heads_scaled(tm_x, tm_heads_folded, w("policy.bias"), policy, wdl, moves_left, batch, d,
-                    policy_size, policy_storage, wdl_probs, p.ss, p.sj * kFwdG, cfg.rms_norm_eps, s);
+                    policy_size, policy_storage, wdl_probs, p.ss, p.sj * kFwdG, cfg.rms_norm_eps, s,
+                    p.slice_cnt, (cfg.depth + 1) * p.sj);
   trace("heads", s);
 }
 

@@ -434,6 +434,29 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- counters across CTAs
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+// Order generic-proxy accesses to global memory with later TMA (async-proxy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Waits until *ptr >= target (acquire, bounded). Returns false after kWaitLimitNs.
+__device__ __forceinline__ bool wait_counter(const int* ptr, int target) {
+  if (ld_acquire_gpu(ptr) >= target) return true;
+  const unsigned long long start = global_timer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(ptr) >= target) return true;
+    if (global_timer_ns() - start > kWaitLimitNs) return false;
+  }
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // A kernel launched with programmatic stream serialisation may start while the previous
 // kernel of its stream is still running. grid_dependency_wait() returns once that kernel
