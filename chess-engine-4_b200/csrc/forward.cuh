@@ -35,12 +35,12 @@
 // Tasks are numbered input tiles first, then per layer all gate_up tiles and all down
 // tiles, each row-block-major. A CTA only ever waits on tasks with smaller numbers, which
 // running CTAs already hold, so the schedule cannot deadlock. Row block rb's dependencies
-// are counters in global memory: slice_cnt[rb] (finished x slices) and hid_cnt[rb]
-// (finished gate_up tiles). Writers publish with an epilogue barrier, then one thread's
-// GPU-scope acq_rel fence (which also releases the other threads' stores) and a relaxed
-// increment; readers acquire the counter, and issue a proxy fence before TMA reads the
-// data. Every wait is bounded (a timed-out wait records an error code and the kernel
-// runs to its end).
+// are counters in global memory: slice_cnt[rb] (finished 128-column x slices) and
+// hid_cnt[rb] (finished gate_up tiles). Tiles are written by TMA stores from a staging
+// tile; the store warp waits for a tile's stores to complete, then issues a proxy fence, a
+// GPU-scope acq_rel fence and a relaxed increment. Readers acquire the counter and issue a
+// proxy fence before TMA reads the data. Every wait is bounded (a timed-out wait records an
+// error code and its role stops; the epilogue warps stop together).
 #pragma once
 
 #include "forward_types.h"
