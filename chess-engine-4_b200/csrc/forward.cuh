@@ -93,39 +93,6 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* ptr, int v) {
   return old;
 }
 
-__device__ __forceinline__ uint4 ldcg_u4(const void* ptr) {
-  return __ldcg(reinterpret_cast<const uint4*>(ptr));
-}
-
-__device__ __forceinline__ float4 ldcg_f4(const float* ptr) {
-  return __ldcg(reinterpret_cast<const float4*>(ptr));
-}
-
-// 32 FP32 values -> 32 BF16 at dst (64 contiguous bytes, 16-byte aligned).
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    d[k] = make_uint4(pack_bf16x2(v[8 * k + 0], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
-                      pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
-  }
-}
-
-// 32 BF16 at src (L2, bypassing L1: the data was written by other SMs) -> FP32.
-__device__ __forceinline__ void load_bf16x32_cg(const __nv_bfloat16* src, float (&v)[32]) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint4 q = ldcg_u4(src + 8 * k);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack_bf16x2(w[j]);
-      v[8 * k + 2 * j] = f.x;
-      v[8 * k + 2 * j + 1] = f.y;
-    }
-  }
-}
-
 __device__ __forceinline__ void fwd_stamp(const FwdParams& p, int t, int slot) {
   if (p.trace != nullptr && t < p.trace_cap) {
     p.trace[static_cast<size_t>(t) * kFwdTraceWords + slot] = global_timer_ns();
