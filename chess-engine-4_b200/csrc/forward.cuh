@@ -9,9 +9,10 @@
 // single-GEMM kernels (warp 0: TMA producer, warp 1: tcgen05.mma issuer, 16 epilogue
 // warps; two accumulators so one tile's epilogue overlaps the next tile's MMAs):
 //
-//   input tile   (rb, j, s): x[rb, j] = bf16((P_0 + P_1) + b), P_s = A_in . W_in^T over K half
-//                            s; both halves store FP32 P_s and the one that finishes second
-//                            sums them (a two-term sum: the same whichever finishes first)
+//   input tile   (rb, j, s): x[rb, j] = bf16((P_0 + P_1 + ...) + b), P_s = A_in . W_in^T over
+//                            K part s of kis; every part stores FP32 P_s and the part that
+//                            checks in last sums them in index order (the same whichever
+//                            finishes last)
 //   gate_up tile (l, rb, c): hidden[rb, c] = bf16(silu(bf16(r * x W'_g^T)) * bf16(r * x W'_u^T))
 //   down tile    (l, rb, j): x[rb, j] = bf16(x + bf16(hidden . W_d^T)).
 //
@@ -53,23 +54,23 @@ struct FwdTask {
   int layer;
   int rb;
   int col;  // hidden chunk (gate_up), x tile of width xwi (input) or xw (down)
-  int kh;   // K half (input)
+  int kh;   // K part (input, of kis; down, of dks)
 };
 
 __device__ __forceinline__ FwdTask fwd_decode(const FwdParams& p, int t) {
   FwdTask k{kTaskEnd, 0, 0, 0, 0};
   if (t < 0 || t >= p.total_tasks) return k;
-  const int n_in = p.nb * p.xti * 2;
+  const int n_in = p.nb * p.xti * p.kis;
   if (t < n_in) {
     k.type = kTaskInput;
-    k.rb = t / (p.xti * 2);
-    const int rem = t - k.rb * (p.xti * 2);
-    k.col = rem >> 1;
-    k.kh = rem & 1;
+    k.rb = t / (p.xti * p.kis);
+    const int rem = t - k.rb * (p.xti * p.kis);
+    k.col = rem / p.kis;
+    k.kh = rem - k.col * p.kis;
     return k;
   }
   t -= n_in;
-  const int per_layer = p.nb * (p.nc + p.xt);
+  const int per_layer = p.nb * (p.nc + p.xt * p.dks);
   k.layer = t / per_layer;
   t -= k.layer * per_layer;
   if (t < p.nb * p.nc) {
@@ -79,8 +80,10 @@ __device__ __forceinline__ FwdTask fwd_decode(const FwdParams& p, int t) {
   } else {
     t -= p.nb * p.nc;
     k.type = kTaskDown;
-    k.rb = t / p.xt;
-    k.col = t - k.rb * p.xt;
+    k.rb = t / (p.xt * p.dks);
+    const int rem = t - k.rb * (p.xt * p.dks);
+    k.col = rem / p.dks;
+    k.kh = rem - k.col * p.dks;
   }
   return k;
 }
@@ -319,19 +322,57 @@ __device__ __forceinline__ bool fwd_epi_down(const FwdParams& p, const FwdTask& 
   return false;
 }
 
-// Input tile K half: stores its FP32 sums in part[kh]; the half that checks in second
-// reads both halves back, adds them (P_0 + P_1, then the bias, TE's fused bias) and
-// finishes and publishes the x tile. The partial sums are stored in epilogue-thread order
-// (128-column half, float4 index q, thread) so that every warp access covers 512
-// contiguous bytes; both halves use the same thread mapping, so each thread reads back
-// its own fragments.
-__device__ __forceinline__ float4* fwd_part_frag(const FwdParams& p, const FwdTask& k, int kh, int h,
-                                                 int tid) {
-  const size_t tile = static_cast<size_t>(k.rb) * p.xti + k.col;
-  const size_t chunk = (tile * 2 + kh) * (p.xwi / 128) + h;
+// K-part partial sums of an input or down tile (`width` columns, `tiles` tiles per row
+// block, `parts` K parts) are stored in epilogue-thread order (128-column half h, float4
+// index q, thread) so that every warp access covers 512 contiguous bytes; all parts use the
+// same thread mapping, so each thread reads back exactly its own fragments. A row block's
+// region holds part_rb_chunks = (d / 128) * max(kis, dks) chunks of 64 KB, enough for
+// either tile kind; its input tiles have finished before its first down tile starts, so
+// both share the buffer.
+__device__ __forceinline__ float4* fwd_part_frag(const FwdParams& p, int rb, int col, int tiles, int width,
+                                                 int parts, int kh, int h, int tid) {
+  (void)tiles;
+  const size_t chunk = static_cast<size_t>(rb) * p.part_rb_chunks +
+                       ((static_cast<size_t>(col) * parts + kh) * (width / 128) + h);
   return reinterpret_cast<float4*>(p.part) + chunk * (8 * kFwdEpiThreads) + tid;
 }
 
+// Store a thread's 32 FP32 sums of K part kh.
+__device__ __forceinline__ void fwd_part_store(float4* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) dst[q * kFwdEpiThreads] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+// Sum of all K parts of a thread's 32 columns, in part order (whichever part finished last).
+__device__ __forceinline__ void fwd_part_sum(const FwdParams& p, int rb, int col, int tiles, int width,
+                                             int parts, int h, int tid, float (&v)[32]) {
+  const float4* src = fwd_part_frag(p, rb, col, tiles, width, parts, 0, h, tid);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 a = __ldcg(src + q * kFwdEpiThreads);
+    v[4 * q] = a.x;
+    v[4 * q + 1] = a.y;
+    v[4 * q + 2] = a.z;
+    v[4 * q + 3] = a.w;
+  }
+  const size_t part_stride = static_cast<size_t>(width / 128) * 8 * kFwdEpiThreads;  // float4s
+#pragma unroll 1
+  for (int s = 1; s < parts; ++s) {
+    src += part_stride;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 a = __ldcg(src + q * kFwdEpiThreads);
+      v[4 * q] += a.x;
+      v[4 * q + 1] += a.y;
+      v[4 * q + 2] += a.z;
+      v[4 * q + 3] += a.w;
+    }
+  }
+}
+
+// Input tile K part: stores its FP32 sums; the part that checks in last reads all parts
+// back, adds them in part order, then the bias (TE's fused bias), and finishes and
+// publishes the x tile.
 __device__ __forceinline__ bool fwd_epi_input(const FwdParams& p, const FwdTask& k, int t, FwdEpi& e,
                                               uint32_t taddr, uint32_t tempty, volatile int* flag,
                                               bool failed) {
@@ -344,34 +385,20 @@ __device__ __forceinline__ bool fwd_epi_input(const FwdParams& p, const FwdTask&
       tc_fence_before();
       mbar_arrive(tempty);
     }
-    float4* dst = fwd_part_frag(p, k, k.kh, h, e.tid);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      dst[q * kFwdEpiThreads] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-    }
+    fwd_part_store(fwd_part_frag(p, k.rb, k.col, p.xti, p.xwi, p.kis, k.kh, h, e.tid), v);
   }
   if (fwd_epi_sync_or(failed)) return true;
   if (e.tid == 0) {
     fence_acq_rel_gpu();
     const int old = atom_add_acq_rel_gpu(p.part_cnt + k.rb * p.xti + k.col, 1);
-    *flag = old == 1;
+    *flag = old == p.kis - 1;
   }
   fwd_epi_sync();
   if (*flag == 0) return false;
   for (int h = 0; h < nh; ++h) {
     const int col0 = k.col * p.xwi + h * 128 + e.g * 32;
-    const float4* s0 = fwd_part_frag(p, k, 0, h, e.tid);
-    const float4* s1 = fwd_part_frag(p, k, 1, h, e.tid);
     float v[32];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 a = __ldcg(s0 + q * kFwdEpiThreads);
-      const float4 b = __ldcg(s1 + q * kFwdEpiThreads);
-      v[4 * q] = a.x + b.x;
-      v[4 * q + 1] = a.y + b.y;
-      v[4 * q + 2] = a.z + b.z;
-      v[4 * q + 3] = a.w + b.w;
-    }
+    fwd_part_sum(p, k.rb, k.col, p.xti, p.xwi, p.kis, h, e.tid, v);
     uint4 bias[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) bias[q] = *reinterpret_cast<const uint4*>(p.bias + col0 + 8 * q);
@@ -391,6 +418,56 @@ __device__ __forceinline__ bool fwd_epi_input(const FwdParams& p, const FwdTask&
     }
     ++e.uses;
   }
+  return false;
+}
+
+// Down tile (128 columns) with its K split in dks parts (small batches): each part stores
+// its FP32 sums; the part that checks in last adds all parts in part order and finishes
+// the tile like an unsplit one. The residual was loaded into the staging tile when the
+// task started (for every part, so that all parts keep the same barrier sequence).
+__device__ __forceinline__ bool fwd_epi_down_split(const FwdParams& p, const FwdTask& k, int t, FwdEpi& e,
+                                                   uint32_t taddr, uint32_t tempty, volatile int* flag,
+                                                   bool failed) {
+  const int row = k.rb * kBM + e.r;
+  if (!failed) {
+    float v[32];
+    load_acc32(taddr + e.g * 32, v);
+    tc_fence_before();
+    mbar_arrive(tempty);
+    fwd_part_store(fwd_part_frag(p, k.rb, k.col, p.xt, 128, p.dks, k.kh, 0, e.tid), v);
+  }
+  if (fwd_epi_sync_or(failed)) return true;
+  if (e.tid == 0) {
+    fence_acq_rel_gpu();
+    const int old = atom_add_acq_rel_gpu(p.dpart_cnt + k.rb * p.xt + k.col, 1);
+    *flag = old % p.dks == p.dks - 1;  // dks check-ins a layer: the last one finishes
+  }
+  fwd_epi_sync();
+  const bool last = *flag != 0;
+  // The residual load lands whichever part this is.
+  bool f = !mbar_wait(e.x_bar, e.x_phase);
+  if (!f) e.x_pending = false;
+  if (!f || !e.x_pending) e.x_phase ^= 1u;
+  if (!last) return fwd_epi_sync_or(f);
+  if (!f) {
+    float v[32];
+    fwd_part_sum(p, k.rb, k.col, p.xt, 128, p.dks, 0, e.tid, v);
+    round_bf16_inplace(v);
+    uint4 res[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) res[u] = ld_shared_v4(fwd_stage_addr(e.stage, e.r, e.g * 32 + 8 * u));
+    fwd_add_bf16x32(v, res, false);  // residual + bf16(acc)
+    round_bf16_inplace(v);
+    fwd_store_ss32(p, row, k.col * 128 + e.g * 32, v);
+    fwd_stage_write32(e.stage, e.r, e.g * 32, v);
+    fence_proxy_async_smem();
+  }
+  if (fwd_epi_sync_or(f)) return true;
+  if (e.tid == 0) {
+    fwd_stamp(p, t, 7);
+    fwd_stage_post(e, kStoreX, k.col * 128, k.rb * kBM, kCounterSlice, k.rb, 1, t);
+  }
+  ++e.uses;
   return false;
 }
 
@@ -504,8 +581,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
           if (k.type == kTaskInput) {
             ma = &maps->a_in;
             mb = &maps->w_in;
-            kb0 = k.kh * p.kb_in / 2;
-            kb1 = (k.kh + 1) * p.kb_in / 2;
+            kb0 = k.kh * p.kb_in / p.kis;
+            kb1 = (k.kh + 1) * p.kb_in / p.kis;
             b_row = k.col * p.xwi;
             if (p.xwi == 256) b_row2 = b_row + 128;
           } else if (k.type == kTaskGateUp) {
@@ -523,7 +600,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
             }
             ma = &maps->hidden;
             mb = &maps->down[k.layer];
-            kb1 = p.h / kBK;
+            kb0 = k.kh * (p.h / kBK) / p.dks;
+            kb1 = (k.kh + 1) * (p.h / kBK) / p.dks;
             b_row = k.col * p.xw;
             if (p.xw == 256) b_row2 = b_row + 128;
           }
@@ -582,8 +660,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         mbar_arrive(task_empty(q));
         if (t < 0) break;
         const FwdTask k = fwd_decode(p, t);
-        const int nkb = k.type == kTaskInput ? (k.kh + 1) * p.kb_in / 2 - k.kh * p.kb_in / 2
-                                             : (k.type == kTaskGateUp ? p.d : p.h) / kBK;
+        const int kbh = p.h / kBK;
+        const int nkb = k.type == kTaskInput  ? (k.kh + 1) * p.kb_in / p.kis - k.kh * p.kb_in / p.kis
+                        : k.type == kTaskDown ? (k.kh + 1) * kbh / p.dks - k.kh * kbh / p.dks
+                                              : p.d / kBK;
         const int n_mma = k.type == kTaskGateUp ? 256 : (k.type == kTaskInput ? p.xwi : p.xw);
         const uint32_t idesc = idesc_bf16(kBM, n_mma);
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u)) {
@@ -668,7 +748,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       if (k.type == kTaskGateUp) {
         abort = fwd_epi_gate_up(p, k, t, e, taddr, tempty_bar(acc), scale, failed);
       } else if (k.type == kTaskDown) {
-        abort = fwd_epi_down(p, k, t, e, taddr, tempty_bar(acc), failed);
+        abort = p.dks > 1 ? fwd_epi_down_split(p, k, t, e, taddr, tempty_bar(acc), flag, failed)
+                          : fwd_epi_down(p, k, t, e, taddr, tempty_bar(acc), failed);
       } else {
         abort = fwd_epi_input(p, k, t, e, taddr, tempty_bar(acc), flag, failed);
       }

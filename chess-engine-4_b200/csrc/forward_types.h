@@ -36,10 +36,11 @@ struct FwdParams {
   __nv_bfloat16* x;           // [rows_cap, d]
   __nv_bfloat16* hidden;      // [rows_cap, h]
   float* ss;                  // [rows_cap, sj * kFwdG] partial sums of squares of x
-  float* part;                // [2, rows_cap, d] FP32 K-half sums of the input tiles
+  float* part;                // FP32 partial sums of the K parts of input (and down) tiles
   int* hid_cnt;               // [nb] finished gate_up tiles
   int* slice_cnt;             // [nb] finished 128-column x slices
-  int* part_cnt;              // [nb * xti] K halves of each input tile that finished
+  int* part_cnt;              // [nb * xti] K parts of each input tile that finished
+  int* dpart_cnt;             // [nb * xt] K parts of each down tile that finished (dks a layer)
   int* task_counter;          // [1]
   int* err;
   int rows_cap;
@@ -50,7 +51,10 @@ struct FwdParams {
   int xw;      // column width of the down tiles (128 or 256, per forward)
   int xt;      // d / xw down tiles per row block
   int xwi;     // column width of the input tiles (256 where d allows, else 128)
-  int xti;     // d / xwi input tiles per row block (each computed as two K halves)
+  int xti;     // d / xwi input tiles per row block
+  int kis;     // K parts of an input tile: 2, or 8 for batches that leave most SMs idle
+  int dks;     // K parts of a down tile: 1, or 4 for batches that leave most SMs idle
+  int part_rb_chunks;  // 64 KB partial-sum chunks per row block: (d / 128) * max(kis, dks)
   int kb_in;   // k-blocks of the input GEMM (in_dim / 64)
   int total_tasks;
   float eps;

@@ -357,7 +357,9 @@ void dense_forward(const FwdParams& p, cudaStream_t s) {
               p.d % 128 == 0 && p.d / 128 <= kFwdMaxSlices && p.h % 128 == 0 &&
               (p.xw == 128 || p.xw == 256) && p.d % p.xw == 0 && p.xt == p.d / p.xw &&
               (p.xwi == 128 || p.xwi == 256) && p.d % p.xwi == 0 && p.xti == p.d / p.xwi &&
-              p.kb_in >= 2,
+              p.kis >= 2 && p.kis <= 8 && p.kb_in >= p.kis && p.dks >= 1 && p.dks <= 4 &&
+              (p.dks == 1 || (p.xw == 128 && (p.h / kFwdKBlock) % p.dks == 0)) &&
+              p.part_rb_chunks == (p.d / 128) * std::max(p.kis, p.dks),
           "persistent forward: unsupported shape");
   auto kernel = dense_forward_kernel;
   ensure_smem(kernel, FwdSmem::kBytes);

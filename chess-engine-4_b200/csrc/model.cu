@@ -134,8 +134,10 @@ void Model::plan_workspace() {
     const size_t sj = static_cast<size_t>(d / 128);
     const size_t nb = r / 128;
     ws_off.fwd_ss = take(r * sj * kFwdG * 4);
-    ws_off.fwd_part = take(2 * r * d * 4);
-    fwd_sync_bytes = (2 * nb + nb * sj + 1) * 4;
+    // K-part partial sums: 2 parts for every row block, or 8 for the small-batch schedule.
+    const size_t chunk = 64 * 1024;
+    ws_off.fwd_part = take(std::max(nb * sj * 2, static_cast<size_t>(fused_small_nb()) * sj * 8) * chunk);
+    fwd_sync_bytes = (2 * nb + 2 * nb * sj + 1) * 4;
     ws_off.fwd_sync = take(fwd_sync_bytes);
   }
   if (cfg.arch == CE4B_ARCH_MOE64A2) {
@@ -427,7 +429,8 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.hid_cnt = sync;
   p.slice_cnt = sync + nb_cap;
   p.part_cnt = sync + 2 * nb_cap;
-  p.task_counter = sync + 2 * nb_cap + nb_cap * p.sj;
+  p.dpart_cnt = p.part_cnt + nb_cap * p.sj;
+  p.task_counter = p.dpart_cnt + nb_cap * p.sj;
   p.err = device_error_word();
   p.rows_cap = rows_cap;
   p.nb = (batch + 127) / 128;
@@ -438,6 +441,9 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.xw = fused_xw(batch);
   p.xt = d / p.xw;
   p.xwi = fused_xwi();
+  p.kis = fused_kis(batch);
+  p.dks = fused_dks(batch);
+  p.part_rb_chunks = (d / 128) * std::max(p.kis, p.dks);
   p.xti = d / p.xwi;
   p.kb_in = in_dim / kFwdKBlock;
   p.total_tasks = fused_task_count(batch);

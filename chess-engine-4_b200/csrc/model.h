@@ -1,6 +1,7 @@
 // Model handle behind the opaque ce4b_model of the C ABI.
 #pragma once
 
+#include <algorithm>
 #include <map>
 #include <memory>
 #include <string>
@@ -82,11 +83,25 @@ struct Model {
     const int nb = (batch + 127) / 128;
     return cfg.d_model % 256 == 0 && nb * (cfg.d_model / 256) >= 2 * sm_count() ? 256 : 128;
   }
-  // Input tiles: 256 columns where d allows (each computed as two K halves).
+  // Input tiles: 256 columns where d allows.
   int fused_xwi() const { return cfg.d_model % 256 == 0 ? 256 : 128; }
+  // Small batches leave most SMs idle while each row block's chain runs: the input tiles
+  // are then split into 8 K parts and the (128-wide) down tiles into 4, the parts summed
+  // in fixed order by the last finisher. Row blocks up to which this applies:
+  int fused_small_nb() const {
+    const int per_rb = std::max((cfg.d_model / fused_xwi()) * 8, (cfg.d_model / 128) * 4);
+    return std::max(0, std::min(rows_cap / 128, sm_count() / per_rb));
+  }
+  bool fused_small(int batch) const {
+    const int nb = (batch + 127) / 128;
+    return nb <= fused_small_nb() && fused_xw(batch) == 128 && (dense_hidden / 64) % 4 == 0;
+  }
+  int fused_kis(int batch) const { return fused_small(batch) ? 8 : 2; }
+  int fused_dks(int batch) const { return fused_small(batch) ? 4 : 1; }
   int fused_task_count(int batch) const {
     const int nb = (batch + 127) / 128, xt = cfg.d_model / fused_xw(batch), nc = dense_hidden / 128;
-    return nb * (cfg.d_model / fused_xwi()) * 2 + cfg.depth * nb * (nc + xt);
+    return nb * (cfg.d_model / fused_xwi()) * fused_kis(batch) +
+           cfg.depth * nb * (nc + xt * fused_dks(batch));
   }
   uint8_t* mx_arena = nullptr;    // quantised weights (codes + scales)
   size_t mx_arena_bytes = 0;

@@ -215,21 +215,33 @@ def test_persistent_forward_is_deterministic(d: int, depth: int, batch: int) -> 
             assert torch.equal(a, b)
 
 
-def test_persistent_forward_tile_width_does_not_change_results() -> None:
-    """Large batches run the input and down tiles 256 columns wide (throughput-bound),
-    small ones 128 wide (chain-bound); only the assignment of columns to CTAs changes, so
-    a position's outputs are the same bits whichever width its batch used."""
+def test_persistent_forward_schedules_and_batch_size() -> None:
+    """The persistent forward picks a schedule by batch size: small batches (at most ~9 row
+    blocks) split the input tiles into 8 K parts and the down tiles into 4, larger ones use
+    2 and 1, and large ones make the down tiles 256 columns wide. Within a K split the
+    parts are summed in fixed order and the tile width only assigns columns to CTAs, so a
+    position's outputs are the same bits for every batch with the same K split; across
+    K splits they agree to FP32 accumulation order."""
 
     torch.manual_seed(0)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    big = 128 * sms + 256  # 256-wide tiles: (big / 128) * (512 / 256) >= 2 * SMs
+    big = 128 * sms + 256  # 256-wide down tiles: (big / 128) * (512 / 256) >= 2 * SMs
     weights, _, planes = _dense_case(512, 2, 3.0, big)
     model = dense_model(weights, d=512, depth=2, ratio=3.0).cuda()
     x = planes.cuda()
-    wide = model(x.clone())
-    torch.cuda.synchronize()
-    wide = [t[:256].clone() for t in (wide.policy_logits, wide.wdl_logits, wide.moves_left)]
-    narrow = model(x[:256].clone())
-    torch.cuda.synchronize()
-    for a, b in zip(wide, (narrow.policy_logits, narrow.wdl_logits, narrow.moves_left)):
+
+    def run(rows):
+        out = model(x[:rows].clone())
+        torch.cuda.synchronize()
+        return [t[:200].clone() for t in (out.policy_logits, out.wdl_logits, out.moves_left)]
+
+    small_a, small_b = run(200), run(700)  # 8 input / 4 down K parts
+    medium_a, medium_b = run(1536), run(2048)  # 2 / 1, 128-wide down tiles
+    wide = run(big)  # 2 / 1, 256-wide down tiles
+    for a, b in zip(small_a, small_b):
         assert torch.equal(a, b)
+    for a, b, c in zip(medium_a, medium_b, wide):
+        assert torch.equal(a, b)
+        assert torch.equal(a, c)
+    for a, b in zip(small_a, medium_a):
+        torch.testing.assert_close(a.float(), b.float(), atol=2e-2, rtol=1e-2)
