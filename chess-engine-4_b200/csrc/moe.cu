@@ -17,25 +17,44 @@ namespace {
 
 constexpr int kExperts = 64;
 
-// One CTA of 64 threads (one per expert).
-__global__ void moe_scan_kernel(const int* __restrict__ block_hist, int ntiles,
-                                int* __restrict__ expert_start, int* __restrict__ block_off,
-                                int4* __restrict__ m_tiles, int* __restrict__ num_m_tiles,
-                                int* __restrict__ counts_out) {
+// One CTA of 1024 threads. The per-tile histograms are staged in shared memory 64 tiles at
+// a time by all threads (coalesced), thread e < 64 runs expert e's prefix over them there,
+// and the offsets go back to global memory coalesced; the tile table follows.
+constexpr int kScanThreads = 1024;
+constexpr int kScanChunk = 64;  // tiles per staged chunk (16 KB)
+
+__global__ void __launch_bounds__(kScanThreads)
+    moe_scan_kernel(const int* __restrict__ block_hist, int ntiles, int* __restrict__ expert_start,
+                    int* __restrict__ block_off, int4* __restrict__ m_tiles,
+                    int* __restrict__ num_m_tiles, int* __restrict__ counts_out) {
+  __shared__ int hist[kScanChunk * kExperts];
   __shared__ int padded[kExperts];
   __shared__ int tiles[kExperts];
-  const int e = threadIdx.x;
+  const int tid = threadIdx.x;
+  const int e = tid;  // expert of the scanning threads (tid < 64)
   int run = 0;
-#pragma unroll 4
-  for (int b = 0; b < ntiles; ++b) {
-    const int c = block_hist[b * kExperts + e];
-    block_off[b * kExperts + e] = run;
-    run += c;
+  for (int b0 = 0; b0 < ntiles; b0 += kScanChunk) {
+    const int n = min(kScanChunk, ntiles - b0) * kExperts;
+    for (int i = tid; i < n; i += kScanThreads) hist[i] = block_hist[b0 * kExperts + i];
+    __syncthreads();
+    if (tid < kExperts) {
+      for (int b = 0; b < n / kExperts; ++b) {
+        const int c = hist[b * kExperts + e];
+        hist[b * kExperts + e] = run;
+        run += c;
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < n; i += kScanThreads) block_off[b0 * kExperts + i] = hist[i];
+    __syncthreads();
   }
   const int nt = (run + kBM - 1) / kBM;
-  padded[e] = nt * kBM;
-  tiles[e] = nt;
+  if (tid < kExperts) {
+    padded[e] = nt * kBM;
+    tiles[e] = nt;
+  }
   __syncthreads();
+  if (tid >= kExperts) return;
   int start = 0, tstart = 0;
   for (int j = 0; j < e; ++j) {
     start += padded[j];
@@ -49,7 +68,15 @@ __global__ void moe_scan_kernel(const int* __restrict__ block_hist, int ntiles,
   if (e == kExperts - 1) *num_m_tiles = tstart + nt;
 }
 
-// One CTA per router tile (128 tokens = 256 routes), 256 threads (one per route).
+// kDispatchParts CTAs per router tile (128 tokens = 256 routes), 256 threads (one per
+// route). Every CTA of a tile computes the tile's 256 destinations (cheap); the first
+// writes the route positions and probabilities, and each copies a quarter of the rows.
+// A copy is a flat list of (row, 16-byte chunk) items, consecutive threads on
+// consecutive chunks of a row, each thread issuing kDispatchBatch loads before their
+// stores so that enough bytes are in flight.
+constexpr int kDispatchParts = 4;
+constexpr int kDispatchBatch = 8;
+
 __global__ void __launch_bounds__(256)
     moe_dispatch_kernel(const bf16* __restrict__ n, const int2* __restrict__ route_expert,
                         const float2* __restrict__ route_prob, const int* __restrict__ expert_start,
@@ -57,7 +84,8 @@ __global__ void __launch_bounds__(256)
                         float* __restrict__ pprob, int* __restrict__ route_pos, int tokens, int d) {
   __shared__ int warp_cnt[8][kExperts];
   __shared__ int pos_s[256];
-  const int b = blockIdx.x;
+  const int b = blockIdx.x / kDispatchParts;
+  const int part = blockIdx.x - b * kDispatchParts;
   const int i = threadIdx.x;
   const int warp = i >> 5;
   const int lane = i & 31;
@@ -83,23 +111,46 @@ __global__ void __launch_bounds__(256)
     int prefix = 0;
     for (int w = 0; w < warp; ++w) prefix += warp_cnt[w][e];
     pos = expert_start[e] + block_off[b * kExperts + e] + prefix + rank;
-    pprob[pos] = prob;
-    route_pos[2 * token + k] = pos;
+    if (part == 0) {
+      pprob[pos] = prob;
+      route_pos[2 * token + k] = pos;
+    }
   }
   pos_s[i] = pos;
   __syncthreads();
   const int chunks = d / 8;  // 16-byte chunks per row
-  for (int r = warp; r < 256; r += 8) {
-    const int p = pos_s[r];
-    if (p < 0) continue;
-    const int t = b * kBM + (r >> 1);
-    const uint4* src = reinterpret_cast<const uint4*>(n + static_cast<size_t>(t) * d);
-    uint4* dst = reinterpret_cast<uint4*>(xperm + static_cast<size_t>(p) * d);
-    for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
+  constexpr int kRows = 256 / kDispatchParts;
+  const int r0 = part * kRows;
+  const int items = kRows * chunks;
+  for (int base = 0; base < items; base += 256 * kDispatchBatch) {
+    uint4 v[kDispatchBatch];
+    int dst_off[kDispatchBatch];
+#pragma unroll
+    for (int u = 0; u < kDispatchBatch; ++u) {
+      const int it = base + u * 256 + i;
+      dst_off[u] = -1;
+      if (it < items) {
+        const int r = r0 + it / chunks;
+        const int c = it - (it / chunks) * chunks;
+        const int p = pos_s[r];
+        if (p >= 0) {
+          const int t = b * kBM + (r >> 1);
+          v[u] = reinterpret_cast<const uint4*>(n + static_cast<size_t>(t) * d)[c];
+          dst_off[u] = p * chunks + c;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kDispatchBatch; ++u) {
+      if (dst_off[u] >= 0) reinterpret_cast<uint4*>(xperm)[dst_off[u]] = v[u];
+    }
   }
 }
 
 // One warp per token: x = bf16(x + bf16(y0 + y1)); n = bf16((x * rsqrt(mean(x^2)+eps)) * w).
+// A lane holds up to kMaxC 16-byte chunks of the row (d <= 256 * kMaxC); all of its loads
+// (x, the norm weight, then both expert outputs) are issued before the arithmetic.
+template <int kMaxC>
 __global__ void moe_combine_norm_kernel(bf16* __restrict__ x, const bf16* __restrict__ y,
                                         const int2* __restrict__ route_pos,
                                         const bf16* __restrict__ w, bf16* __restrict__ nout,
@@ -107,53 +158,69 @@ __global__ void moe_combine_norm_kernel(bf16* __restrict__ x, const bf16* __rest
   const int t = static_cast<int>((blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= tokens) return;
-  const int2 rp = route_pos[t];
   const int chunks = d / 8;
   bf16* xr = x + static_cast<size_t>(t) * d;
-  const bf16* y0 = y + static_cast<size_t>(rp.x) * d;
-  const bf16* y1 = y + static_cast<size_t>(rp.y) * d;
-  float v[8][8];
-  float ss = 0.0f;
+  uint4 xa[kMaxC], wa[kMaxC], ya[kMaxC], yb[kMaxC];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < kMaxC; ++j) {
     const int c = lane + 32 * j;
     if (c < chunks) {
-      float xa[8], ya[8], yb[8];
-      load_bf16<8>(xr + 8 * c, xa);
-      load_bf16<8>(y0 + 8 * c, ya);
-      load_bf16<8>(y1 + 8 * c, yb);
-      uint4 o;
-      uint32_t* ow = &o.x;
+      xa[j] = reinterpret_cast<const uint4*>(xr)[c];
+      wa[j] = __ldg(reinterpret_cast<const uint4*>(w) + c);
+    }
+  }
+  const int2 rp = route_pos[t];
+  const uint4* y0 = reinterpret_cast<const uint4*>(y + static_cast<size_t>(rp.x) * d);
+  const uint4* y1 = reinterpret_cast<const uint4*>(y + static_cast<size_t>(rp.y) * d);
 #pragma unroll
-      for (int q = 0; q < 8; q += 2) {
-        const float r0 = bf16_round(ya[q] + yb[q]);
-        const float r1 = bf16_round(ya[q + 1] + yb[q + 1]);
-        v[j][q] = bf16_round(xa[q] + r0);
-        v[j][q + 1] = bf16_round(xa[q + 1] + r1);
-        ss = fmaf(v[j][q], v[j][q], ss);
-        ss = fmaf(v[j][q + 1], v[j][q + 1], ss);
-        ow[q / 2] = pack_bf16x2(v[j][q], v[j][q + 1]);
+  for (int j = 0; j < kMaxC; ++j) {
+    const int c = lane + 32 * j;
+    if (c < chunks) {
+      ya[j] = y0[c];
+      yb[j] = y1[c];
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kMaxC; ++j) {
+    const int c = lane + 32 * j;
+    if (c < chunks) {
+      const uint32_t xw[4] = {xa[j].x, xa[j].y, xa[j].z, xa[j].w};
+      const uint32_t aw[4] = {ya[j].x, ya[j].y, ya[j].z, ya[j].w};
+      const uint32_t bw[4] = {yb[j].x, yb[j].y, yb[j].z, yb[j].w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 xf = unpack_bf16x2(xw[q]), af = unpack_bf16x2(aw[q]), bf = unpack_bf16x2(bw[q]);
+        const float r0 = bf16_round(af.x + bf.x);
+        const float r1 = bf16_round(af.y + bf.y);
+        const float v0 = bf16_round(xf.x + r0);
+        const float v1 = bf16_round(xf.y + r1);
+        ss = fmaf(v0, v0, ss);
+        ss = fmaf(v1, v1, ss);
+        ow[q] = pack_bf16x2(v0, v1);
       }
-      reinterpret_cast<uint4*>(xr)[c] = o;
+      xa[j] = make_uint4(ow[0], ow[1], ow[2], ow[3]);  // the new x (BF16)
+      reinterpret_cast<uint4*>(xr)[c] = xa[j];
     }
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
-  bf16* nr = nout + static_cast<size_t>(t) * d;
+  uint4* nr = reinterpret_cast<uint4*>(nout + static_cast<size_t>(t) * d);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < kMaxC; ++j) {
     const int c = lane + 32 * j;
     if (c < chunks) {
-      float wa[8];
-      load_bf16<8>(w + 8 * c, wa);
-      uint4 o;
-      uint32_t* ow = &o.x;
+      const uint32_t vw[4] = {xa[j].x, xa[j].y, xa[j].z, xa[j].w};
+      const uint32_t ww[4] = {wa[j].x, wa[j].y, wa[j].z, wa[j].w};
+      uint32_t ow[4];
 #pragma unroll
-      for (int q = 0; q < 8; q += 2) {
-        ow[q / 2] = pack_bf16x2((v[j][q] * inv) * wa[q], (v[j][q + 1] * inv) * wa[q + 1]);
+      for (int q = 0; q < 4; ++q) {
+        const float2 vf = unpack_bf16x2(vw[q]), wf = unpack_bf16x2(ww[q]);
+        ow[q] = pack_bf16x2((vf.x * inv) * wf.x, (vf.y * inv) * wf.y);
       }
-      reinterpret_cast<uint4*>(nr)[c] = o;
+      nr[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
     }
   }
 }
@@ -208,8 +275,8 @@ __global__ void bf16_to_f32_kernel(const bf16* __restrict__ in, float* __restric
 
 void moe_scan(const int* block_hist, int ntiles, int* expert_start, int* block_off,
               int4* m_tiles, int* num_m_tiles, int* counts_out, cudaStream_t s) {
-  moe_scan_kernel<<<1, kExperts, 0, s>>>(block_hist, ntiles, expert_start, block_off, m_tiles,
-                                         num_m_tiles, counts_out);
+  moe_scan_kernel<<<1, kScanThreads, 0, s>>>(block_hist, ntiles, expert_start, block_off, m_tiles,
+                                             num_m_tiles, counts_out);
   check_cuda(cudaGetLastError(), "moe_scan launch");
 }
 
@@ -218,8 +285,8 @@ void moe_dispatch(const bf16* n, const int2* route_expert, const float2* route_p
                   int* route_pos, int tokens, int d, cudaStream_t s) {
   require(d % 8 == 0, "MoE width must be a multiple of 8");
   const int tiles = (tokens + kBM - 1) / kBM;
-  moe_dispatch_kernel<<<tiles, 256, 0, s>>>(n, route_expert, route_prob, expert_start, block_off,
-                                            xperm, pprob, route_pos, tokens, d);
+  moe_dispatch_kernel<<<tiles * kDispatchParts, 256, 0, s>>>(n, route_expert, route_prob, expert_start,
+                                                             block_off, xperm, pprob, route_pos, tokens, d);
   check_cuda(cudaGetLastError(), "moe_dispatch launch");
 }
 
@@ -228,8 +295,14 @@ void moe_combine_norm(bf16* x, const bf16* yperm, const int* route_pos, const bf
   require(d % 8 == 0 && d <= 2048, "MoE width must be a multiple of 8 and at most 2048");
   const int warps_per_block = 8;
   const int blocks = (tokens + warps_per_block - 1) / warps_per_block;
-  moe_combine_norm_kernel<<<blocks, warps_per_block * 32, 0, s>>>(
-      x, yperm, reinterpret_cast<const int2*>(route_pos), norm_w, nout, tokens, d, eps);
+  const int2* rp = reinterpret_cast<const int2*>(route_pos);
+  if (d <= 1024) {
+    moe_combine_norm_kernel<4><<<blocks, warps_per_block * 32, 0, s>>>(x, yperm, rp, norm_w, nout, tokens,
+                                                                      d, eps);
+  } else {
+    moe_combine_norm_kernel<8><<<blocks, warps_per_block * 32, 0, s>>>(x, yperm, rp, norm_w, nout, tokens,
+                                                                      d, eps);
+  }
   check_cuda(cudaGetLastError(), "moe_combine launch");
 }
 
