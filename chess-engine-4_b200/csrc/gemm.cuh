@@ -1097,9 +1097,14 @@ struct EpiSwiGLU {
       if (et.tid == 0) bulk_wait_read_all();  // previous tile's store has read the staging
       epi_bar_sync<G>();
     }
+    // With one 32-column chunk per thread (HC == 32 * G) the accumulator is released right
+    // after it has been read, so the next tile's MMAs overlap the SwiGLU (and the MXFP8
+    // quantisation) of this one even with a single accumulator.
+    constexpr bool kOneChunk = HC == 32 * G;
     for (int c = et.g * 32; c < HC; c += G * 32) {
       float g[32], u[32];
       load_acc32x2(et.taddr + c, et.taddr + HC + c, g, u);
+      if constexpr (kOneChunk) release_accumulator(ctx);
       round_bf16_inplace(g);
       round_bf16_inplace(u);
 #pragma unroll
@@ -1116,7 +1121,7 @@ struct EpiSwiGLU {
         stage_bf16x32(ctx.smem, et.r, c, g);
       }
     }
-    release_accumulator(ctx);
+    if constexpr (!kOneChunk) release_accumulator(ctx);
     fence_proxy_async_smem();
     epi_bar_sync<G>();
     if (et.tid == 0 && tc.rows > 0) {
