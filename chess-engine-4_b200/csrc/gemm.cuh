@@ -1146,13 +1146,15 @@ struct EpiSwiGLU {
 // exactly one tile per CTA (the stage ring is reused as the n staging buffer).
 // With MX, n is written as MXFP8 (BF16-rounded, then E4M3 codes through tmO2 as a byte
 // map with 128-code boxes, one E8M0 scale per row and 32 columns into n_scales).
-template <int BN, bool MX = false>
+// MAXC bounds the CTAs per row (cluster_n), which sizes the partial-sum receive buffer.
+template <int BN, bool MX = false, int MAXC = kMaxClusterN>
 struct EpiResNorm {
   static_assert(BN % 64 == 0, "64-column boxes");
   static_assert(!MX || BN % 128 == 0, "MXFP8 output needs 128-column slices");
+  static_assert(MAXC >= 1 && MAXC <= kMaxClusterN, "cluster bound");
   enum Mode : int { kBias = 0, kResidual = 1 };
   static constexpr int kXBytes = kBM * BN * 2;
-  static constexpr int kRecvFloats = kMaxClusterN * kMaxG * kBM;
+  static constexpr int kRecvFloats = MAXC * kMaxG * kBM;
   static constexpr int kSmemBytes = kXBytes + kRecvFloats * 4;
   struct Params {
     const __nv_bfloat16* bias;

@@ -200,6 +200,23 @@ void gemm_mx_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtenso
                      float eps, cudaStream_t s) {
   require(d % 128 == 0 && d / 128 <= kMaxClusterN && k % 128 == 0,
           "MXFP8 residual GEMM needs d a multiple of 128 up to 1024 and K a multiple of 128");
+  if (d % 256 == 0 && d / 256 <= 4) {
+    // 128 x 256 tiles (B as two 128-row boxes): a 256-column MMA keeps the tensor core busy
+    // per ring stage where a 128-column one runs at half rate, and half as many CTAs.
+    constexpr int BN = 256, NS = 3, NA = 1;
+    using Epi = EpiResNorm<BN, true, 4>;
+    auto kernel = gemm_mx_kernel<BN, NS, NA, 2, kG, true, DenseSched, Epi>;
+    constexpr int smem = GemmMxSmem<BN, NS, NA, Epi>::kBytes;
+    ensure_smem(kernel, smem);
+    const int cn = d / BN;
+    DenseSched sched{m, cn, ceil_div(m, kBM) * cn, BN, 128};
+    typename Epi::Params ep{bias,     norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
+                            cn,       eps,    n_scales};
+    const MxScales sf{sfa, sfb, k / 128};
+    launch(kernel, dim3(sched.num_tiles), gemm_threads(kG), smem, cn, s, tA, tB, tX, tN, sched, ep,
+           sf, k / 128, device_error_word());
+    return;
+  }
   constexpr int BN = 128, NS = 5, NA = 1;
   using Epi = EpiResNorm<BN, true>;
   auto kernel = gemm_mx_kernel<BN, NS, NA, 1, kG, true, DenseSched, Epi>;
