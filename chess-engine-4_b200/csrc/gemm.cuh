@@ -1476,7 +1476,10 @@ struct EpiRouter {
 template <int BN>
 struct EpiScaleStore {
   static_assert(BN % 64 == 0, "64-column boxes");
-  static constexpr int kSmemBytes = kBM * BN * 2;
+  // The output is staged at most 128 columns at a time (32 KB), leaving the shared memory
+  // of a fourth operand stage to a 256-column tile.
+  static constexpr int kPart = BN < 128 ? BN : 128;
+  static constexpr int kSmemBytes = kBM * kPart * 2;
   struct Params {
     const float* row_scale;  // [rows] per permuted row
   };
@@ -1493,17 +1496,23 @@ struct EpiScaleStore {
       epi_bar_sync<G>();
     }
     const float scale = et.r < tc.rows ? __ldg(p.row_scale + tc.out_row + et.r) : 0.0f;
-    for (int c = et.g * 32; c < BN; c += G * 32) {
-      float v[32];
-      load_acc32(et.taddr + c, v);
+    for (int c0 = 0; c0 < BN; c0 += kPart) {
+      if (c0 > 0) {
+        if (et.tid == 0) bulk_wait_read_all();  // the previous part's store has read the staging
+        epi_bar_sync<G>();
+      }
+      for (int c = et.g * 32; c < kPart; c += G * 32) {
+        float v[32];
+        load_acc32(et.taddr + c0 + c, v);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] *= scale;
-      stage_bf16x32(ctx.smem, et.r, c, v);
+        for (int j = 0; j < 32; ++j) v[j] *= scale;
+        stage_bf16x32(ctx.smem, et.r, c, v);
+      }
+      if (c0 + kPart >= BN) release_accumulator(ctx);
+      fence_proxy_async_smem();
+      epi_bar_sync<G>();
+      if (et.tid == 0) store_staged(ctx.tmO1, ctx.smem, kPart, tc.n_tile * BN + c0, tc.out_row);
     }
-    release_accumulator(ctx);
-    fence_proxy_async_smem();
-    epi_bar_sync<G>();
-    if (et.tid == 0) store_staged(ctx.tmO1, ctx.smem, BN, tc.n_tile * BN, tc.out_row);
   }
 };
 

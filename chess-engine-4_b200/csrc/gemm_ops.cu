@@ -487,7 +487,7 @@ void gemm_grouped_scale(const CUtensorMap& tA, const CUtensorMap& tB, const CUte
                         const int4* m_tiles, const int* num_m_tiles, const float* row_scale, int n,
                         int k, cudaStream_t s) {
   switch (grouped_bn(n)) {
-    case 256: gemm_grouped_scale_bn<256, 3>(tA, tB, tY, m_tiles, num_m_tiles, row_scale, n, k, s); break;
+    case 256: gemm_grouped_scale_bn<256, 4>(tA, tB, tY, m_tiles, num_m_tiles, row_scale, n, k, s); break;
     case 128: gemm_grouped_scale_bn<128, 5>(tA, tB, tY, m_tiles, num_m_tiles, row_scale, n, k, s); break;
     default: gemm_grouped_scale_bn<64, 7>(tA, tB, tY, m_tiles, num_m_tiles, row_scale, n, k, s); break;
   }
