@@ -572,6 +572,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         const CUtensorMap* ma = nullptr;
         const CUtensorMap* mb = nullptr;
         int kb0 = 0, kb1 = 0, b_row = 0, b_row2 = -1;
+        const int* dep = nullptr;  // counter the task's A operand waits for
+        int dep_target = 0;
         if (t >= 0) {
           fwd_stamp(p, t, 0);
           if (p.trace != nullptr && t < p.trace_cap) {
@@ -586,18 +588,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
             b_row = k.col * p.xwi;
             if (p.xwi == 256) b_row2 = b_row + 128;
           } else if (k.type == kTaskGateUp) {
-            if (!wait_counter(p.slice_cnt + k.rb, (k.layer + 1) * p.sj)) {
-              record_error(p.err, kErrTimeoutDependency);
-            }
+            dep = p.slice_cnt + k.rb;
+            dep_target = (k.layer + 1) * p.sj;
             ma = &maps->x;
             mb = &maps->gate_up[k.layer];
             kb1 = p.d / kBK;
             b_row = k.col * 128;
             b_row2 = p.h + k.col * 128;
           } else {
-            if (!wait_counter(p.hid_cnt + k.rb, (k.layer + 1) * p.nc)) {
-              record_error(p.err, kErrTimeoutDependency);
-            }
+            dep = p.hid_cnt + k.rb;
+            dep_target = (k.layer + 1) * p.nc;
             ma = &maps->hidden;
             mb = &maps->down[k.layer];
             kb0 = k.kh * (p.h / kBK) / p.dks;
@@ -605,6 +605,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
             b_row = k.col * p.xw;
             if (p.xw == 256) b_row2 = b_row + 128;
           }
+        }
+        const uint32_t bytes = L::kABytes + (b_row2 >= 0 ? 2 : 1) * 128 * kBK * 2;
+        // While the task's inputs are still being produced, its first k-blocks' weight (B)
+        // boxes go into the stages that are already free; their A boxes follow once the
+        // inputs are complete. (The stage's full barrier expects both.)
+        int pre = 0;
+        const int pre_stage = stage;
+        if (dep != nullptr && ld_acquire_gpu(dep) < dep_target) {
+          while (pre < kb1 - kb0 && pre < kFwdNStage && mbar_test_wait(empty_bar(stage), phase ^ 1u)) {
+            const uint32_t sb = base + stage * L::kStageBytes + L::kABytes;
+            const int kb = kb0 + pre;
+            mbar_arrive_expect_tx(full_bar(stage), bytes);
+            tma_load_2d(sb, mb, full_bar(stage), kb * kBK, b_row);
+            if (b_row2 >= 0) tma_load_2d(sb + 128 * kBK * 2, mb, full_bar(stage), kb * kBK, b_row2);
+            issued_mask |= 1u << stage;
+            issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+            if (++stage == kFwdNStage) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            ++pre;
+          }
+          if (!wait_counter(dep, dep_target)) record_error(p.err, kErrTimeoutDependency);
         }
         // The task is published once its inputs are complete (the acquire above), so the
         // MMA thread and the epilogue warps may read its inputs as soon as they see it.
@@ -614,8 +637,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         // Data written by other SMs' generic stores is read below by TMA (async proxy).
         fence_proxy_async_global();
         fwd_stamp(p, t, 1);
-        const uint32_t bytes = L::kABytes + (b_row2 >= 0 ? 2 : 1) * 128 * kBK * 2;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int i = 0, st = pre_stage; i < pre; ++i, st = (st + 1) % kFwdNStage) {
+          tma_load_2d(base + st * L::kStageBytes, ma, full_bar(st), (kb0 + i) * kBK, k.rb * kBM);
+        }
+        for (int kb = kb0 + pre; kb < kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
             record_error(p.err, kErrTimeoutProducer);
             ok = false;
