@@ -805,6 +805,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         const int map = job[0];
         if (map == kStoreStop) break;
         const int x0 = job[1], y0 = job[2], counter = job[3], rb = job[4], inc = job[5], t = job[6];
+        fwd_stamp(p, t, 9);
         const CUtensorMap* m = map == kStoreHidden ? &maps->hidden : &maps->x;
         tma_store_2d(m, stage_out, x0, y0);
         tma_store_2d(m, stage_out + 16384, x0 + 64, y0);
@@ -814,6 +815,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         if (counter != kCounterNone) {
           // Every store of the tile is complete before the GPU-scope release.
           bulk_wait_all();
+          fwd_stamp(p, t, 11);
           fence_proxy_async_global();
           fence_acq_rel_gpu();
           red_add_relaxed_gpu((counter == kCounterHidden ? p.hid_cnt : p.slice_cnt) + rb, inc);

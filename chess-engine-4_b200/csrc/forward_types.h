@@ -61,7 +61,8 @@ struct FwdParams {
   // Optional per-task timeline (nullptr: off): kFwdTraceWords u64 per task id < trace_cap,
   // %globaltimer ns of {0 fetched, 1 dependencies met, 2 last load issued, 3 first MMA
   // issued, 4 accumulator committed, 5 epilogue started, 6 epilogue done, 7 epilogue
-  // results stored, 8 epilogue published}, then the CTA index in word 10 (9, 11 unused).
+  // results staged, 8 results published, 9 store warp took the staged tile, 11 its stores
+  // completed}, and the CTA index in word 10.
   unsigned long long* trace;
   int trace_cap;
 };

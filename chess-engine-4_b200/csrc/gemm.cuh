@@ -840,15 +840,17 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
           for (int j = 0; j < kNSub; ++j) {
             tmem_cp_32x128b_x4(sfa_t + 4u * (1 + j), sdesc_sf32x16(ssf + 512u * (1 + j)));
           }
+          // One MMA covers all BN columns: the B rows of the 128-row boxes are contiguous
+          // 8-row swizzle atoms, and their scales sit in consecutive 4-column groups (rows
+          // 32q..32q+31 of each 128-row group in column 4 * group + q), the layout the
+          // block-scaled MMA reads for N > 128. (Two N = 128 MMAs per K step cost ~1.4x
+          // the issue time of one N = 256 MMA on the same operands.)
           const uint64_t adesc = sdesc_k128(sa);
+          const uint64_t bdesc = sdesc_k128(sb);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-#pragma unroll
-            for (int j = 0; j < kNSub; ++j) {
-              const uint64_t bdesc = sdesc_k128(sb + static_cast<uint32_t>(j) * (128u * 128u));
-              umma_mxf8(d_tmem + 128u * j, adesc + 2u * k, bdesc + 2u * k, idesc_mxf8(kBM, 128, k),
-                        sfa_t, sfa_t + 4u * (1 + j), (kb | k) != 0 ? 1u : 0u);
-            }
+            umma_mxf8(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc_mxf8(kBM, BN, k), sfa_t,
+                      sfa_t + 4u, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(empty_bar(stage));
           if (++stage == NSTAGE) {

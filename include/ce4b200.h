@@ -206,9 +206,9 @@ int ce4b_expert_parallel_plan(int world, int rank, const int32_t* meta_send, con
  * capacity_tasks > 0, each forward writes 12 uint64 per task id < capacity_tasks into the
  * device buffer: %globaltimer ns when the task was fetched, its inputs were ready, its
  * last load was issued, its first MMA was issued, its accumulator was committed, its
- * epilogue started and finished, its epilogue results were stored and published, and
- * (last slice of a row block) its RMSNorm pass finished; then the CTA index and one
- * unused word. 0 disables. Task ids are numbered
+ * epilogue started and finished, its results were staged in shared memory and published,
+ * the store warp took the staged tile; then the CTA index; then the tile's global stores
+ * completed. 0 disables. Task ids are numbered
  * input-GEMM tiles first (row block, slice, k split), then per layer the gate_up tiles
  * (row block, hidden chunk) and the down tiles (row block, slice).
  * ce4b_model_task_count gives the number of tasks of a forward at `batch` (0 when the
