@@ -485,6 +485,8 @@ struct FwdSmem {
   static constexpr int kMiscBytes = kBarriers * 8 + kFwdTaskRing * 4 + 16 + kJobInts * 4;
   static constexpr int kBytes = 1024 + kRingBytes + kOutBytes + kMiscBytes;
   static_assert(kBytes <= 232448, "shared memory budget exceeded");
+  static_assert(kFwdD96B1 + 128 * (kFwdDownStep - kBK) * 2 <= kStageBytes,
+                "a 96-deep down stage must fit one ring stage");
 };
 
 __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const FwdParams p) {
@@ -555,6 +557,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       tma_prefetch_desc(&maps->a_in);
       tma_prefetch_desc(&maps->x);
       tma_prefetch_desc(&maps->hidden);
+      tma_prefetch_desc(&maps->hidden32);
       tma_prefetch_desc(&maps->w_in);
       int stage = 0;
       uint32_t phase = 0;
@@ -571,6 +574,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         FwdTask k{kTaskEnd, 0, 0, 0};
         const CUtensorMap* ma = nullptr;
         const CUtensorMap* mb = nullptr;
+        const CUtensorMap* mb32 = nullptr;  // 96-deep down stages: 32-wide B box
+        bool d96 = false;
         int kb0 = 0, kb1 = 0, b_row = 0, b_row2 = -1;
         const int* dep = nullptr;  // counter the task's A operand waits for
         int dep_target = 0;
@@ -600,13 +605,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
             dep_target = (k.layer + 1) * p.nc;
             ma = &maps->hidden;
             mb = &maps->down[k.layer];
-            kb0 = k.kh * (p.h / kBK) / p.dks;
-            kb1 = (k.kh + 1) * (p.h / kBK) / p.dks;
+            mb32 = &maps->down32[k.layer];
+            d96 = p.d96 != 0 && p.xw == 128;
+            const int steps = p.h / (d96 ? kFwdDownStep : kBK);
+            kb0 = k.kh * steps / p.dks;
+            kb1 = (k.kh + 1) * steps / p.dks;
             b_row = k.col * p.xw;
             if (p.xw == 256) b_row2 = b_row + 128;
           }
         }
-        const uint32_t bytes = L::kABytes + (b_row2 >= 0 ? 2 : 1) * 128 * kBK * 2;
+        const uint32_t bytes =
+            d96 ? 2u * 128u * kFwdDownStep * 2u : L::kABytes + (b_row2 >= 0 ? 2 : 1) * 128 * kBK * 2;
+        // Weight (B) and activation (A) boxes of step kb into stage address sa.
+        auto load_b = [&](uint32_t sa, uint32_t bar, int kb) {
+          if (d96) {
+            tma_load_2d(sa + kFwdD96B0, mb, bar, kb * kFwdDownStep, b_row);
+            tma_load_2d(sa + kFwdD96B1, mb32, bar, kb * kFwdDownStep + kBK, b_row);
+          } else {
+            tma_load_2d(sa + L::kABytes, mb, bar, kb * kBK, b_row);
+            if (b_row2 >= 0) tma_load_2d(sa + L::kABytes + 128 * kBK * 2, mb, bar, kb * kBK, b_row2);
+          }
+        };
+        auto load_a = [&](uint32_t sa, uint32_t bar, int kb) {
+          if (d96) {
+            tma_load_2d(sa, ma, bar, kb * kFwdDownStep, k.rb * kBM);
+            tma_load_2d(sa + kFwdD96A1, &maps->hidden32, bar, kb * kFwdDownStep + kBK, k.rb * kBM);
+          } else {
+            tma_load_2d(sa, ma, bar, kb * kBK, k.rb * kBM);
+          }
+        };
         // While the task's inputs are still being produced, its first k-blocks' weight (B)
         // boxes go into the stages that are already free; their A boxes follow once the
         // inputs are complete. (The stage's full barrier expects both.)
@@ -614,11 +641,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         const int pre_stage = stage;
         if (dep != nullptr && ld_acquire_gpu(dep) < dep_target) {
           while (pre < kb1 - kb0 && pre < kFwdNStage && mbar_test_wait(empty_bar(stage), phase ^ 1u)) {
-            const uint32_t sb = base + stage * L::kStageBytes + L::kABytes;
-            const int kb = kb0 + pre;
             mbar_arrive_expect_tx(full_bar(stage), bytes);
-            tma_load_2d(sb, mb, full_bar(stage), kb * kBK, b_row);
-            if (b_row2 >= 0) tma_load_2d(sb + 128 * kBK * 2, mb, full_bar(stage), kb * kBK, b_row2);
+            load_b(base + stage * L::kStageBytes, full_bar(stage), kb0 + pre);
             issued_mask |= 1u << stage;
             issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
             if (++stage == kFwdNStage) {
@@ -638,7 +662,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         fence_proxy_async_global();
         fwd_stamp(p, t, 1);
         for (int i = 0, st = pre_stage; i < pre; ++i, st = (st + 1) % kFwdNStage) {
-          tma_load_2d(base + st * L::kStageBytes, ma, full_bar(st), (kb0 + i) * kBK, k.rb * kBM);
+          load_a(base + st * L::kStageBytes, full_bar(st), kb0 + i);
         }
         for (int kb = kb0 + pre; kb < kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
@@ -647,11 +671,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
             break;
           }
           const uint32_t sa = base + stage * L::kStageBytes;
-          const uint32_t sb = sa + L::kABytes;
           mbar_arrive_expect_tx(full_bar(stage), bytes);
-          tma_load_2d(sa, ma, full_bar(stage), kb * kBK, k.rb * kBM);
-          tma_load_2d(sb, mb, full_bar(stage), kb * kBK, b_row);
-          if (b_row2 >= 0) tma_load_2d(sb + 128 * kBK * 2, mb, full_bar(stage), kb * kBK, b_row2);
+          load_a(sa, full_bar(stage), kb);
+          load_b(sa, full_bar(stage), kb);
           issued_mask |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == kFwdNStage) {
@@ -685,7 +707,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         mbar_arrive(task_empty(q));
         if (t < 0) break;
         const FwdTask k = fwd_decode(p, t);
-        const int kbh = p.h / kBK;
+        const bool d96 = k.type == kTaskDown && p.d96 != 0 && p.xw == 128;
+        const int kbh = p.h / (d96 ? kFwdDownStep : kBK);
         const int nkb = k.type == kTaskInput  ? (k.kh + 1) * p.kb_in / p.kis - k.kh * p.kb_in / p.kis
                         : k.type == kTaskDown ? (k.kh + 1) * kbh / p.dks - k.kh * kbh / p.dks
                                               : p.d / kBK;
@@ -706,11 +729,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
           tc_fence_after();
           if (kb == 0) fwd_stamp(p, t, 3);
           const uint32_t sa = base + stage * L::kStageBytes;
-          const uint64_t adesc = sdesc_k128(sa);
-          const uint64_t bdesc = sdesc_k128(sa + L::kABytes);
+          if (d96) {
+            const uint64_t adesc = sdesc_k128(sa), bdesc = sdesc_k128(sa + kFwdD96B0);
+            const uint64_t adesc1 = sdesc_k64(sa + kFwdD96A1), bdesc1 = sdesc_k64(sa + kFwdD96B1);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            umma_bf16(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              umma_bf16(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
+#pragma unroll
+            for (int kk = 0; kk < (kFwdDownStep - kBK) / 16; ++kk) {
+              umma_bf16(d_tmem, adesc1 + 2u * kk, bdesc1 + 2u * kk, idesc, 1u);
+            }
+          } else {
+            const uint64_t adesc = sdesc_k128(sa);
+            const uint64_t bdesc = sdesc_k128(sa + L::kABytes);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              umma_bf16(d_tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
           }
           umma_commit(empty_bar(stage));
           if (++stage == kFwdNStage) {

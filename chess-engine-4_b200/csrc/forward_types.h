@@ -28,7 +28,20 @@ struct FwdMaps {
   CUtensorMap w_in;    // input.weight [d, in_dim], box 64 x 128
   CUtensorMap gate_up[kFwdMaxDepth];  // bf16(gate_up.weight * norm.weight) [2h, d], box 64 x 128
   CUtensorMap down[kFwdMaxDepth];     // [d, h], box 64 x 128
+  // 64-byte-swizzled maps (box 32 x 128) of hidden and down.weight: the second box of a
+  // 96-deep down-tile stage.
+  CUtensorMap hidden32;
+  CUtensorMap down32[kFwdMaxDepth];
 };
+
+// 128-column down tiles move K in steps of 96 when h allows: a 48 KB ring stage holds A
+// and B as a 64-wide (128-byte swizzle) and a 32-wide (64-byte swizzle) box each, so each
+// wait for a stage feeds 6 MMAs instead of 4. (A stage costs the MMA thread a roughly fixed
+// ~520 cycles when its MMAs take less, so 128-column MMAs run at half rate with 4 per stage.)
+constexpr int kFwdDownStep = 96;
+constexpr uint32_t kFwdD96A1 = 16384;  // stage offsets: A 64-wide @0, A 32-wide, B 64-wide, B 32-wide
+constexpr uint32_t kFwdD96B0 = 24576;
+constexpr uint32_t kFwdD96B1 = 40960;
 
 struct FwdParams {
   const FwdMaps* maps;
@@ -56,6 +69,7 @@ struct FwdParams {
   int dks;     // K parts of a down tile: 1, or 4 for batches that leave most SMs idle
   int part_rb_chunks;  // 64 KB partial-sum chunks per row block: (d / 128) * max(kis, dks)
   int kb_in;   // k-blocks of the input GEMM (in_dim / 64)
+  int d96;     // 1: 128-column down tiles use 96-deep stages (h % 96 == 0)
   int total_tasks;
   float eps;
   // Optional per-task timeline (nullptr: off): kFwdTraceWords u64 per task id < trace_cap,

@@ -120,6 +120,31 @@ const CUtensorMap& null_map() {
 
 }  // namespace
 
+namespace {
+CUtensorMap encode_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                        uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  require(ptr != nullptr, "tensor map: null pointer");
+  require((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0, "tensor map: base not 16-byte aligned");
+  require((ld_elems * 2) % 16 == 0, "tensor map: row stride not a multiple of 16 bytes");
+  require(rows >= 1 && cols >= 1 && box_rows >= 1 && box_rows <= 256, "tensor map: bad extent");
+  CUtensorMap map;
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {ld_elems * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+                                 gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(CE4B_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return map;
+}
+}  // namespace
+
+CUtensorMap make_tmap_bf16_sw64(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                                uint32_t box_rows) {
+  return encode_bf16(ptr, rows, cols, ld_elems, 32, box_rows, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                            uint32_t box_rows) {
   require(ptr != nullptr, "tensor map: null pointer");

@@ -49,6 +49,9 @@ int sm_count();
 // 2-D BF16 tensor map, 128-byte swizzle, box = 64 (K) x box_rows. Throws on bad alignment.
 CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                            uint32_t box_rows);
+// Same with a 64-byte swizzle and box = 32 (K) x box_rows.
+CUtensorMap make_tmap_bf16_sw64(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                                uint32_t box_rows);
 
 // ---------------------------------------------------------------- GEMM launchers
 // Every map is a BF16 map from make_tmap_bf16 (box 64 columns x box_rows rows); output

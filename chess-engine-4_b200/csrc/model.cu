@@ -294,6 +294,7 @@ void Model::finalize() {
     maps.a_in = make_tmap_bf16(ws_a_in, rows_cap, in_dim, in_dim, 128);
     maps.x = make_tmap_bf16(workspace + ws_off.x, rows_cap, d, d, 128);
     maps.hidden = make_tmap_bf16(ws_hidden, rows_cap, dense_hidden, dense_hidden, 128);
+    maps.hidden32 = make_tmap_bf16_sw64(ws_hidden, rows_cap, dense_hidden, dense_hidden, 128);
     maps.w_in = make_tmap_bf16(w("input.weight"), d, in_dim, in_dim, 128);
     for (int l = 0; l < cfg.depth; ++l) {
       const std::string p = "blocks." + std::to_string(l);
@@ -301,6 +302,7 @@ void Model::finalize() {
       fold_columns(w(p + ".gate_up.weight"), w(p + ".norm.weight"), gu, 2 * dense_hidden, d, stream);
       maps.gate_up[l] = make_tmap_bf16(gu, 2 * dense_hidden, d, d, 128);
       maps.down[l] = make_tmap_bf16(w(p + ".down.weight"), d, dense_hidden, dense_hidden, 128);
+      maps.down32[l] = make_tmap_bf16_sw64(w(p + ".down.weight"), d, dense_hidden, dense_hidden, 128);
     }
     bf16* heads = fwd_weights + cfg.depth * gu_elems;
     fold_columns(w("policy.weight"), w("final_norm.weight"), heads, static_cast<int64_t>(heads_rows), d,
@@ -446,6 +448,7 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.part_rb_chunks = (d / 128) * std::max(p.kis, p.dks);
   p.xti = d / p.xwi;
   p.kb_in = in_dim / kFwdKBlock;
+  p.d96 = dense_hidden % kFwdDownStep == 0 && dense_hidden / kFwdDownStep >= p.dks ? 1 : 0;
   p.total_tasks = fused_task_count(batch);
   p.eps = cfg.rms_norm_eps;
   p.trace = fwd_trace;

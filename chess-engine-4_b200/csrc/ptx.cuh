@@ -402,6 +402,21 @@ __device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t count, bool p
 // Fields: start address >> 4 (bits 0-13), leading byte offset >> 4 (16-29, unused for
 // swizzled K-major), stride byte offset >> 4 (32-45), descriptor version 1 (bit 46),
 // swizzle mode 2 = 128B (bits 61-63).
+__device__ __forceinline__ uint64_t sdesc_k128(uint32_t smem_addr);
+
+// Same for 64-byte swizzling: rows of 32 BF16 (64 B), 8-row core groups 512 B apart,
+// swizzle mode 4 = 64B. The K offset inside a row advances the start address by 32 B per
+// 16 elements, as with 128-byte swizzling.
+__device__ __forceinline__ uint64_t sdesc_k64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;
+  return d;
+}
+
 __device__ __forceinline__ uint64_t sdesc_k128(uint32_t smem_addr) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
