@@ -45,6 +45,7 @@ import torch  # noqa: E402
 
 IN_DIM = 112 * 64
 POLICY = 1858
+HEAD_COLS = POLICY + 3 + 1  # useful head columns: policy, WDL, moves-left
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -86,10 +87,10 @@ class Config:
         return f + half * 2 * 3 * d * self.dense_hidden + half * (2 * 64 * d + 2 * (3 * d * self.hidden * 2))
 
     def tower_flop(self, batch: int) -> float:
-        """FLOPs of the persistent dense tower kernel (input GEMM + all layers; the heads
-        run in their own kernel)."""
+        """Algorithmic FLOPs of the persistent dense forward kernel: input GEMM, all layers
+        and the heads' 1862 useful columns (policy 1858, WDL 3, moves-left 1)."""
 
-        return 2.0 * batch * (IN_DIM * self.d + self.depth * 3 * self.d * self.hidden)
+        return 2.0 * batch * (IN_DIM * self.d + self.depth * 3 * self.d * self.hidden + HEAD_COLS * self.d)
 
     def gate_up_flop(self, batch: int) -> float:
         """FLOPs of one launch of the gate_up + SwiGLU GEMM."""
@@ -622,7 +623,7 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
             },
             "roofline": {
                 "kernel": (f"{dominant} (persistent tcgen05 kernel: input GEMM, every layer's gate_up+SwiGLU "
-                           "and down+residual tiles, RMSNorm passes)") if dominant == "dense_tower" else
+                           "and down+residual tiles, heads)") if dominant == "dense_tower" else
                           f"{dominant} (tcgen05 GEMM + fused SwiGLU epilogue)",
                 "bound": "tensor",
                 "achieved": achieved,

@@ -72,6 +72,14 @@ __device__ __forceinline__ FwdTask fwd_decode(const FwdParams& p, int t) {
   t -= n_in;
   const int per_layer = p.nb * (p.nc + p.xt * p.dks);
   k.layer = t / per_layer;
+  if (k.layer >= p.depth) {
+    t -= p.depth * per_layer;
+    k.type = kTaskHeads;
+    k.layer = p.depth;
+    k.rb = t / p.nht;
+    k.col = t - k.rb * p.nht;
+    return k;
+  }
   t -= k.layer * per_layer;
   if (t < p.nb * p.nc) {
     k.type = kTaskGateUp;
@@ -168,7 +176,9 @@ struct FwdEpi {
   volatile int* job;   // job record: map, x0, y0, counter kind, row block, increment, task
 };
 
-enum FwdStoreMap : int { kStoreStop = -1, kStoreHidden = 0, kStoreX = 1 };
+// kStoreNone: nothing to store (the staging tile was used and read back by the epilogue
+// itself); the store warp only frees the tile.
+enum FwdStoreMap : int { kStoreStop = -1, kStoreHidden = 0, kStoreX = 1, kStoreNone = 2 };
 enum FwdCounter : int { kCounterNone = 0, kCounterHidden = 1, kCounterSlice = 2 };
 
 // All epilogue threads: wait until the store warp has read the staging tile of the
@@ -471,6 +481,97 @@ __device__ __forceinline__ bool fwd_epi_down_split(const FwdParams& p, const Fwd
   return false;
 }
 
+// Heads tile: accumulator columns [0, 256) are head columns col * 256 + [0, 256) of the
+// folded [policy | wdl | moves-left] matrix; thread (r, g) reads columns g * 32 and
+// 128 + g * 32. Logits = bf16(acc * r + bias) with r the final RMSNorm scale (the norm
+// weight is folded into the matrix), as the heads GEMM computes them
+// (src/chess_engine_4/model/dense.py:167-199; kernels/src/inference/runtime.cu:630-643).
+// Policy columns leave as FP32: each warp transposes its 32 rows x 32 columns through its
+// own 2 KB of the staging tile, 16 rows at a time, and stores each row's 32 values with one
+// coalesced instruction. The WDL (softmax or logits) and moves-left columns are written by
+// the threads that hold them.
+__device__ __forceinline__ bool fwd_epi_heads(const FwdParams& p, const FwdTask& k, int t, FwdEpi& e,
+                                              uint32_t taddr, uint32_t tempty, float scale, bool failed) {
+  const int row = k.rb * kBM + e.r;
+  const int lane = e.tid & 31;
+  const int row0 = k.rb * kBM + (e.r & ~31);  // first row of this warp
+  const uint32_t area = e.stage + static_cast<uint32_t>((e.tid >> 5) * 2048);
+  failed = fwd_stage_acquire(e, failed);
+  if (!failed) {
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      const int c = h * 128 + e.g * 32;
+      const int c0 = k.col * 256 + c;  // uniform across the warp
+      if (c0 >= p.head_cols) continue;
+      float v[32];
+      {
+        float b[32];
+        load_acc32(taddr + c, v);
+        load_bf16<32>(p.head_bias + c0, b);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(__fmul_rn(v[j], scale), b[j]);
+        round_bf16_inplace(v);
+      }
+      if (c0 == p.policy_storage) {
+        if (row < p.batch) {
+          float* w = p.wdl + static_cast<size_t>(row) * 3;
+          if (p.wdl_probs) {
+            const float mx = fmaxf(fmaxf(v[0], v[1]), v[2]);
+            const float e0 = expf(v[0] - mx), e1 = expf(v[1] - mx), e2 = expf(v[2] - mx);
+            const float total = e0 + e1 + e2;
+            w[0] = e0 / total;
+            w[1] = e1 / total;
+            w[2] = e2 / total;
+          } else {
+            w[0] = v[0];
+            w[1] = v[1];
+            w[2] = v[2];
+          }
+        }
+        continue;
+      }
+      if (c0 == p.policy_storage + 32) {
+        if (row < p.batch) p.moves_left[row] = v[0];
+        continue;
+      }
+      if (c0 >= p.policy_size) continue;
+      // 16 rows at a time: [16][32] FP32, 16-byte chunk q of row i at q ^ (i % 8).
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        if ((lane >> 4) == half) {
+          const int i = lane & 15;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            st_shared_v4(area + static_cast<uint32_t>(i * 128 + ((u ^ (i & 7)) << 4)),
+                         make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
+                                    __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3])));
+          }
+        }
+        __syncwarp();
+        const bool col_ok = c0 + lane < p.policy_size;
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+          const int grow = row0 + half * 16 + i;
+          const float val =
+              ld_shared_f32(area + static_cast<uint32_t>(i * 128 + (((lane >> 2) ^ (i & 7)) << 4) + (lane & 3) * 4));
+          if (col_ok && grow < p.batch) p.policy[static_cast<size_t>(grow) * p.policy_size + c0 + lane] = val;
+        }
+        __syncwarp();
+      }
+    }
+    fence_proxy_async_smem();  // these generic accesses precede the tile's next TMA write
+    tc_fence_before();
+    mbar_arrive(tempty);
+  }
+  if (fwd_epi_sync_or(failed)) return true;
+  if (e.tid == 0) {
+    fwd_stamp(p, t, 7);
+    fwd_stage_post(e, kStoreNone, 0, 0, kCounterNone, 0, 0, t);
+  }
+  ++e.uses;
+  return false;
+}
+
 // ------------------------------------------------------------------ the kernel
 struct FwdSmem {
   static constexpr int kABytes = kBM * kBK * 2;          // 16 KB
@@ -600,6 +701,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
             kb1 = p.d / kBK;
             b_row = k.col * 128;
             b_row2 = p.h + k.col * 128;
+          } else if (k.type == kTaskHeads) {
+            dep = p.slice_cnt + k.rb;
+            dep_target = (p.depth + 1) * p.sj;
+            ma = &maps->x;
+            mb = &maps->heads;
+            kb1 = p.d / kBK;
+            b_row = k.col * 256;
+            b_row2 = b_row + 128;
           } else {
             dep = p.hid_cnt + k.rb;
             dep_target = (k.layer + 1) * p.nc;
@@ -712,7 +821,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         const int nkb = k.type == kTaskInput  ? (k.kh + 1) * p.kb_in / p.kis - k.kh * p.kb_in / p.kis
                         : k.type == kTaskDown ? (k.kh + 1) * kbh / p.dks - k.kh * kbh / p.dks
                                               : p.d / kBK;
-        const int n_mma = k.type == kTaskGateUp ? 256 : (k.type == kTaskInput ? p.xwi : p.xw);
+        const int n_mma = (k.type == kTaskGateUp || k.type == kTaskHeads) ? 256
+                          : (k.type == kTaskInput ? p.xwi : p.xw);
         const uint32_t idesc = idesc_bf16(kBM, n_mma);
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u)) {
           record_error(p.err, kErrTimeoutMma);
@@ -790,7 +900,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       // the task after its dependencies completed): the row scale, or the first 128
       // columns of the residual into the staging tile once the previous store read it.
       float scale = 1.0f;
-      if (k.type == kTaskGateUp) {
+      if (k.type == kTaskGateUp || k.type == kTaskHeads) {
         scale = fwd_row_scale(p, k.rb * kBM + e.r);
       } else if (k.type == kTaskDown) {
         failed = fwd_stage_acquire(e, false);
@@ -811,6 +921,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
       } else if (k.type == kTaskDown) {
         abort = p.dks > 1 ? fwd_epi_down_split(p, k, t, e, taddr, tempty_bar(acc), flag, failed)
                           : fwd_epi_down(p, k, t, e, taddr, tempty_bar(acc), failed);
+      } else if (k.type == kTaskHeads) {
+        abort = fwd_epi_heads(p, k, t, e, taddr, tempty_bar(acc), scale, failed);
       } else {
         abort = fwd_epi_input(p, k, t, e, taddr, tempty_bar(acc), flag, failed);
       }
@@ -842,6 +954,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
         if (map == kStoreStop) break;
         const int x0 = job[1], y0 = job[2], counter = job[3], rb = job[4], inc = job[5], t = job[6];
         fwd_stamp(p, t, 9);
+        if (map == kStoreNone) {
+          mbar_arrive(stage_free);
+          continue;
+        }
         const CUtensorMap* m = map == kStoreHidden ? &maps->hidden : &maps->x;
         tma_store_2d(m, stage_out, x0, y0);
         tma_store_2d(m, stage_out + 16384, x0 + 64, y0);

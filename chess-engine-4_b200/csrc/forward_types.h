@@ -18,7 +18,7 @@ constexpr int kFwdStoreWarp = 2 + 4 * kFwdG;
 constexpr int kFwdThreads = 64 + kFwdEpiThreads + 32;
 constexpr int kErrTimeoutDependency = 7;
 
-enum FwdTaskType : int { kTaskEnd = -1, kTaskInput = 0, kTaskGateUp = 1, kTaskDown = 2 };
+enum FwdTaskType : int { kTaskEnd = -1, kTaskInput = 0, kTaskGateUp = 1, kTaskDown = 2, kTaskHeads = 3 };
 
 // Tensor maps in global memory (64-byte aligned), written once by the host.
 struct FwdMaps {
@@ -32,6 +32,9 @@ struct FwdMaps {
   // 96-deep down-tile stage.
   CUtensorMap hidden32;
   CUtensorMap down32[kFwdMaxDepth];
+  // bf16(final_norm.weight * [policy.weight | wdl.weight | moves_left.weight]) rows
+  // [head_cols, d], box 64 x 128.
+  CUtensorMap heads;
 };
 
 // 128-column down tiles move K in steps of 96 when h allows: a 48 KB ring stage holds A
@@ -56,6 +59,18 @@ struct FwdParams {
   int* dpart_cnt;             // [nb * xt] K parts of each down tile that finished (dks a layer)
   int* task_counter;          // [1]
   int* err;
+  // Heads (the tasks after the last layer): [policy | wdl | moves-left] logits of each row
+  // block, 256 head columns a task.
+  const __nv_bfloat16* head_bias;  // [head_cols] (policy, wdl, moves-left biases back to back)
+  float* policy;                   // [batch, policy_size]
+  float* wdl;                      // [batch, 3] probabilities (wdl_probs) or logits
+  float* moves_left;               // [batch]
+  int batch;
+  int policy_size;                 // 1858
+  int policy_storage;              // 1888: first wdl column; moves-left at policy_storage + 32
+  int head_cols;                   // policy_storage + 64
+  int nht;                         // head tasks per row block (head_cols / 256, rounded up)
+  int wdl_probs;
   int rows_cap;
   int nb;      // row blocks of 128
   int d, h, depth;

@@ -401,7 +401,11 @@ void dense_forward(const FwdParams& p, cudaStream_t s) {
               (p.xwi == 128 || p.xwi == 256) && p.d % p.xwi == 0 && p.xti == p.d / p.xwi &&
               p.kis >= 2 && p.kis <= 8 && p.kb_in >= p.kis && p.dks >= 1 && p.dks <= 4 &&
               (p.dks == 1 || (p.xw == 128 && (p.h / kFwdKBlock) % p.dks == 0)) &&
-              p.part_rb_chunks == (p.d / 128) * std::max(p.kis, p.dks),
+              p.part_rb_chunks == (p.d / 128) * std::max(p.kis, p.dks) && p.batch >= 1 &&
+              p.batch <= p.nb * 128 && p.policy != nullptr && p.wdl != nullptr &&
+              p.moves_left != nullptr && p.head_bias != nullptr && p.policy_size <= p.policy_storage &&
+              p.policy_storage % 32 == 0 && p.head_cols == p.policy_storage + 64 &&
+              p.nht == (p.head_cols + 255) / 256,
           "persistent forward: unsupported shape");
   auto kernel = dense_forward_kernel;
   ensure_smem(kernel, FwdSmem::kBytes);

@@ -308,6 +308,7 @@ void Model::finalize() {
     fold_columns(w("policy.weight"), w("final_norm.weight"), heads, static_cast<int64_t>(heads_rows), d,
                  stream);
     tm_heads_folded = make_tmap_bf16(heads, heads_rows, d, d, 256);
+    maps.heads = make_tmap_bf16(heads, heads_rows, d, d, 128);
     check_cuda(cudaStreamSynchronize(stream), "fold norm weights");
     if (fwd_dev == nullptr) {
       check_cuda(cudaMalloc(&fwd_dev, sizeof(FwdMaps)), "cudaMalloc forward tensor maps");
@@ -407,7 +408,8 @@ void Model::forward_mx(int layout, void* input, const void* scalars, int batch, 
   trace("heads", s);
 }
 
-// Dense BF16 tower as one persistent kernel between the plane expansion and the heads.
+// Dense BF16 forward as one persistent kernel (input GEMM, every layer, heads) after the
+// plane expansion.
 void Model::forward_fused(int layout, void* input, const void* scalars, int batch, float* policy,
                           float* wdl, float* moves_left, int wdl_probs, int write_back,
                           cudaStream_t s) {
@@ -449,18 +451,24 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   p.xti = d / p.xwi;
   p.kb_in = in_dim / kFwdKBlock;
   p.d96 = dense_hidden % kFwdDownStep == 0 && dense_hidden / kFwdDownStep >= p.dks ? 1 : 0;
+  p.head_bias = w("policy.bias");
+  p.policy = policy;
+  p.wdl = wdl;
+  p.moves_left = moves_left;
+  p.batch = batch;
+  p.policy_size = policy_size;
+  p.policy_storage = policy_storage;
+  p.head_cols = policy_storage + 64;
+  p.nht = fused_head_tasks();
+  p.wdl_probs = wdl_probs;
   p.total_tasks = fused_task_count(batch);
   p.eps = cfg.rms_norm_eps;
   p.trace = fwd_trace;
   p.trace_cap = fwd_trace_cap;
+  // One launch: input GEMM, every layer, and the heads of each row block as soon as its
+  // last layer is published.
   dense_forward(p, s);
   trace("dense_tower", s);
-  // The heads start on each row block as soon as its last layer is published, while the
-  // tower finishes the others (the tower never waits on the heads).
-  gemm_heads_scaled(tm_x, tm_heads_folded, w("policy.bias"), policy, wdl, moves_left, batch, d,
-                    policy_size, policy_storage, wdl_probs, p.ss, p.sj * kFwdG, cfg.rms_norm_eps, s,
-                    p.slice_cnt, (cfg.depth + 1) * p.sj);
-  trace("heads", s);
 }
 
 void Model::forward(int layout, void* input, const void* scalars, int batch, float* policy,

@@ -98,10 +98,11 @@ struct Model {
   }
   int fused_kis(int batch) const { return fused_small(batch) ? 8 : 2; }
   int fused_dks(int batch) const { return fused_small(batch) ? 4 : 1; }
+  int fused_head_tasks() const { return (policy_storage + 64 + 255) / 256; }
   int fused_task_count(int batch) const {
     const int nb = (batch + 127) / 128, xt = cfg.d_model / fused_xw(batch), nc = dense_hidden / 128;
     return nb * (cfg.d_model / fused_xwi()) * fused_kis(batch) +
-           cfg.depth * nb * (nc + xt * fused_dks(batch));
+           cfg.depth * nb * (nc + xt * fused_dks(batch)) + nb * fused_head_tasks();
   }
   uint8_t* mx_arena = nullptr;    // quantised weights (codes + scales)
   size_t mx_arena_bytes = 0;
