@@ -210,9 +210,9 @@ int ce4b_expert_parallel_plan(int world, int rank, const int32_t* meta_send, con
  * the store warp took the staged tile; then the CTA index; then the tile's global stores
  * completed. 0 disables. Task ids are numbered
  * input-GEMM tiles first (row block, slice, k split), then per layer the gate_up tiles
- * (row block, hidden chunk) and the down tiles (row block, slice).
- * ce4b_model_task_count gives the number of tasks of a forward at `batch` (0 when the
- * model does not use the persistent forward). */
+ * (row block, hidden chunk) and the down tiles (row block, slice), then the head tiles
+ * (row block, 256 head columns). ce4b_model_task_count gives the number of tasks of a
+ * forward at `batch` (0 when the model does not use the persistent forward). */
 int ce4b_model_set_task_trace(ce4b_model* model, void* device_buffer, int capacity_tasks);
 int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks);
 
