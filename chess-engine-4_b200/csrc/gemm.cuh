@@ -915,6 +915,243 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
   }
 }
 
+// Weight-stationary MXFP8 SwiGLU GEMM for short K (K <= 128 * KBMAX): every CTA keeps the
+// whole B tile of one 128-column hidden chunk (gate and up rows, all k-blocks, with their
+// scale tiles) in shared memory and its B scales in tensor memory, and streams only A
+// (128-row code tiles + scale tiles) through the stage ring for row blocks t = blockIdx.x,
+// + gridDim.x, ... The grid is a multiple of the chunk count, so a CTA's chunk never
+// changes (DenseSched is chunk-fastest). Per tile that moves 64 KB of A at K = 512
+// instead of A + B = 192 KB.
+template <int KBMAX, int NSTAGE, class Epi>
+struct GemmMxBStatSmem {
+  static constexpr int BN = 256;
+  static constexpr int kBBytes = BN * 128 * KBMAX;        // B codes, k-block-major
+  static constexpr int kSfbBytes = 2 * 512 * KBMAX;        // B scale tiles [k-block][half]
+  static constexpr int kABytes = kBM * 128;                // one A code tile
+  static constexpr int kStageBytes = kABytes + 1024;       // + its scale tile (512 B, padded)
+  static constexpr int kRingBytes = NSTAGE * kStageBytes;
+  static constexpr int kEpiBytes = (Epi::kSmemBytes + 1023) / 1024 * 1024;
+  static constexpr int kBarrierBytes = (2 * NSTAGE + 6) * 8 + 8;
+  static constexpr int kBytes = 1024 + kBBytes + kSfbBytes + kRingBytes + kEpiBytes + kBarrierBytes;
+  static constexpr int kSfbCol = BN;                       // TMEM: accumulator, B scales, A scales
+  static constexpr int kSfaCol = BN + 8 * KBMAX;
+  static_assert(kSfaCol + 4 * NSTAGE <= 512, "TMEM overflow");
+  static_assert(kBytes <= 232448, "shared memory budget exceeded");
+};
+
+template <int KBMAX, int NSTAGE, int G, class Epi>
+__global__ void __launch_bounds__(gemm_threads(G), 1)
+    gemm_mx_bstat_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmO1, const DenseSched sched,
+                         const typename Epi::Params ep, const MxScales sf, const int kblocks, int* err) {
+  using L = GemmMxBStatSmem<KBMAX, NSTAGE, Epi>;
+  constexpr int BN = L::BN;
+  constexpr uint32_t kEpiThreads = 128 * G;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint32_t base = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  base += pad;
+
+  const uint32_t b_base = base;
+  const uint32_t sfb_base = b_base + L::kBBytes;
+  const uint32_t ring = sfb_base + L::kSfbBytes;
+  const uint32_t epi_base = ring + L::kRingBytes;
+  const uint32_t bar_base = epi_base + L::kEpiBytes;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (NSTAGE + s); };
+  const uint32_t tfull_bar = bar_base + 8u * (2 * NSTAGE);
+  const uint32_t tempty_bar = tfull_bar + 8u;
+  const uint32_t drain_bar = tfull_bar + 16u;
+  const uint32_t epi_bar = tfull_bar + 24u;
+  const uint32_t x_bar = tfull_bar + 32u;
+  const uint32_t b_bar = tfull_bar + 40u;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_base - base) + L::kBarrierBytes - 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tempty_bar, kEpiThreads);
+    mbar_init(drain_bar, 1);
+    mbar_init(epi_bar, Epi::bar_count(ep, G));
+    mbar_init(x_bar, 1);
+    mbar_init(b_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  grid_dependency_wait();
+  grid_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      const int ntiles = sched.count();
+      bool ok = blockIdx.x < ntiles;
+      bool b_issued = false;
+      if (ok) {
+        // This CTA's hidden chunk: gate rows b_row, up rows b_row2, every k-block.
+        const TileCoord tc0 = sched.coord(blockIdx.x);
+        mbar_arrive_expect_tx(b_bar, static_cast<uint32_t>(kblocks * (BN * 128 + 2 * 512)));
+        for (int kb = 0; kb < kblocks; ++kb) {
+          const uint32_t sb = b_base + static_cast<uint32_t>(kb * BN * 128);
+          tma_load_2d(sb, &tmB, b_bar, kb * 128, tc0.b_row);
+          tma_load_2d(sb + 128 * 128, &tmB, b_bar, kb * 128, tc0.b_row2);
+          bulk_load(sfb_base + static_cast<uint32_t>(kb * 1024),
+                    sf.sfb + (static_cast<size_t>(tc0.b_row / 128) * sf.k_tiles + kb) * 512, 512, b_bar);
+          bulk_load(sfb_base + static_cast<uint32_t>(kb * 1024 + 512),
+                    sf.sfb + (static_cast<size_t>(tc0.b_row2 / 128) * sf.k_tiles + kb) * 512, 512, b_bar);
+        }
+        b_issued = true;
+      }
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const TileCoord tc = sched.coord(t);
+        const int a_tile = tc.a_row / kBM;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
+            record_error(err, kErrTimeoutProducer);
+            ok = false;
+            break;
+          }
+          const uint32_t sa = ring + static_cast<uint32_t>(stage * L::kStageBytes);
+          mbar_arrive_expect_tx(full_bar(stage), L::kABytes + 512);
+          tma_load_2d(sa, &tmA, full_bar(stage), kb * 128, tc.a_row);
+          bulk_load(sa + L::kABytes, sf.sfa + (static_cast<size_t>(a_tile) * sf.k_tiles + kb) * 512, 512,
+                    full_bar(stage));
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < NSTAGE; ++s) {
+          if (issued_mask & (1u << s)) mbar_wait(full_bar(s), (issued_phase >> s) & 1u);
+        }
+      }
+      if (b_issued) mbar_wait(b_bar, 0);  // (normally long complete: the MMA thread waited)
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const int ntiles = sched.count();
+      bool ok = blockIdx.x < ntiles;
+      if (ok && !mbar_wait(b_bar, 0)) {
+        record_error(err, kErrTimeoutMma);
+        ok = false;
+      }
+      if (ok) {
+        tc_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            tmem_cp_32x128b_x4(tmem_base + static_cast<uint32_t>(L::kSfbCol + kb * 8 + 4 * j),
+                               sdesc_sf32x16(sfb_base + static_cast<uint32_t>(kb * 1024 + 512 * j)));
+          }
+        }
+      }
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        if (!mbar_wait(tempty_bar, acc_phase ^ 1u)) {
+          record_error(err, kErrTimeoutMma);
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase)) {
+            record_error(err, kErrTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = ring + static_cast<uint32_t>(stage * L::kStageBytes);
+          const uint32_t sfa_t = tmem_base + static_cast<uint32_t>(L::kSfaCol + stage * 4);
+          tmem_cp_32x128b_x4(sfa_t, sdesc_sf32x16(sa + L::kABytes));
+          const uint64_t adesc = sdesc_k128(sa);
+          const uint64_t bdesc = sdesc_k128(b_base + static_cast<uint32_t>(kb * BN * 128));
+          const uint32_t sfb_t = tmem_base + static_cast<uint32_t>(L::kSfbCol + kb * 8);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            umma_mxf8(tmem_base, adesc + 2u * k, bdesc + 2u * k, idesc_mxf8(kBM, BN, k), sfa_t, sfb_t,
+                      (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == NSTAGE) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar);
+        acc_phase ^= 1u;
+      }
+      umma_commit(drain_bar);
+      if (!mbar_wait(drain_bar, 0)) record_error(err, kErrTimeoutDrain);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    EpiThread et;
+    et.r = quarter * 32 + lane;
+    et.g = (warp - 2) >> 2;
+    et.tid = threadIdx.x - 64;
+    EpiCtx ctx;
+    ctx.smem = epi_base;
+    ctx.smem_ptr = smem + (epi_base - base);
+    ctx.ring = ring;
+    ctx.epi_bar = epi_bar;
+    ctx.x_bar = x_bar;
+    ctx.tmO1 = &tmO1;
+    ctx.tmO2 = &tmO1;
+    ctx.err = err;
+    uint32_t acc_phase = 0;
+    int iter = 0;
+    const int ntiles = sched.count();
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++iter) {
+      const TileCoord tc = sched.coord(t);
+      if (!mbar_wait(tfull_bar, acc_phase)) {
+        record_error(err, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      et.taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      ctx.iter = iter;
+      ctx.tempty_bar = tempty_bar;
+      Epi::template run<G>(ep, tc, et, ctx);
+      acc_phase ^= 1u;
+    }
+    if (et.tid == 0) bulk_wait_all();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
 // ------------------------------------------------------------------ epilogue helpers
 
 // Load 32 consecutive FP32 accumulator columns of this thread's row (one wait).

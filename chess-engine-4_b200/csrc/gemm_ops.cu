@@ -206,14 +206,28 @@ void gemm_mx_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensor
                     const uint8_t* sfa, const uint8_t* sfb, uint8_t* h_scales, int m,
                     int hidden_dim, int k, cudaStream_t s) {
   require(hidden_dim % 128 == 0 && k % 128 == 0, "MXFP8 SwiGLU needs multiples of 128");
-  constexpr int BN = 256, NS = 4, NA = 1;
   using Epi = EpiSwiGLU<128, true>;
+  const int chunks = hidden_dim / 128;
+  DenseSched sched{m, chunks, ceil_div(m, kBM) * chunks, 128, hidden_dim};
+  typename Epi::Params ep{h_scales, chunks};
+  const MxScales sf{sfa, sfb, k / 128};
+  constexpr int kStatKb = 4;
+  if (k / 128 <= kStatKb && chunks <= sm_count() && sched.num_tiles >= sm_count()) {
+    // Short K: each CTA keeps one chunk's gate/up codes resident and streams A only. The
+    // grid is a multiple of the chunk count so that a CTA's chunk is fixed.
+    constexpr int NS = 4;
+    auto kernel = gemm_mx_bstat_kernel<kStatKb, NS, kG, Epi>;
+    constexpr int smem = GemmMxBStatSmem<kStatKb, NS, Epi>::kBytes;
+    ensure_smem(kernel, smem);
+    const int grid = (sm_count() / chunks) * chunks;
+    launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tH, sched, ep, sf, k / 128,
+           device_error_word());
+    return;
+  }
+  constexpr int BN = 256, NS = 4, NA = 1;
   auto kernel = gemm_mx_kernel<BN, NS, NA, 2, kG, false, DenseSched, Epi>;
   constexpr int smem = GemmMxSmem<BN, NS, NA, Epi>::kBytes;
   ensure_smem(kernel, smem);
-  DenseSched sched{m, hidden_dim / 128, ceil_div(m, kBM) * (hidden_dim / 128), 128, hidden_dim};
-  typename Epi::Params ep{h_scales, hidden_dim / 128};
-  const MxScales sf{sfa, sfb, k / 128};
   const int grid = std::min(sched.num_tiles, sm_count());
   launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, tH, null_map(), sched, ep, sf,
          k / 128, device_error_word());
