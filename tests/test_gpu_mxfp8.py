@@ -52,7 +52,7 @@ def test_mxfp8_gemm_matches_dequantised_product(m: int, n: int, k: int) -> None:
     torch.testing.assert_close(c.float().cpu(), ref, atol=1e-3 * float(ref.abs().max()), rtol=8e-3)
 
 
-@pytest.mark.parametrize("d,depth,ratio,batch", [(256, 2, 3.0, 256), (512, 12, 3.0, 1024)])
+@pytest.mark.parametrize("d,depth,ratio,batch", [(256, 2, 3.0, 256), (512, 12, 3.0, 1024), (512, 2, 3.0, 2048)])
 def test_mxfp8_model_matches_oracle(d: int, depth: int, ratio: float, batch: int) -> None:
     from ce4b200 import DenseChessNet, DenseChessNetConfig, synthetic
     from helpers import POLICY_ATOL, WDL_PROB_ATOL, argmax_agreement
@@ -81,3 +81,23 @@ def test_mxfp8_model_matches_oracle(d: int, depth: int, ratio: float, batch: int
     assert argmax_agreement(out.policy_logits, policy) >= 0.995
     wdl_err = (torch.softmax(out.wdl_logits.cpu(), -1) - torch.softmax(wdl, -1)).abs().max(dim=1).values
     assert float((wdl_err <= WDL_PROB_ATOL).float().mean()) >= 0.97
+
+
+def test_mxfp8_weight_stationary_swiglu_matches_streaming() -> None:
+    """At K = d <= 512 and at least one tile per SM the SwiGLU GEMM keeps each CTA's
+    gate/up codes resident; below that it streams A and B. Both issue the same block-scaled
+    MMAs in the same order, so a position's outputs do not depend on which one ran."""
+    from ce4b200 import DenseChessNet, DenseChessNetConfig, synthetic
+
+    d, depth, ratio = 512, 2, 3.0
+    weights = synthetic.make_dense_weights(d_model=d, depth=depth, hidden_dim=int(d * ratio), seed=5)
+    model = DenseChessNet(DenseChessNetConfig(d_model=d, depth=depth, expansion_ratio=ratio, precision="mxfp8"))
+    synthetic.load_into(model, weights)
+    model = model.cuda()
+    planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(2048, 6)).cuda()
+    wide = model(planes.clone())      # 16 row blocks x 12 hidden chunks = 192 tiles: resident path
+    narrow = model(planes[:1024].clone())  # 96 tiles: streaming path
+    torch.cuda.synchronize()
+    assert torch.equal(wide.policy_logits[:1024], narrow.policy_logits)
+    assert torch.equal(wide.wdl_logits[:1024], narrow.wdl_logits)
+    assert torch.equal(wide.moves_left[:1024], narrow.moves_left)
