@@ -13,7 +13,6 @@
 // No TMA multicast is used anywhere.
 #pragma once
 
-#include <type_traits>
 
 #include "mxfp8.cuh"
 #include "ptx.cuh"
@@ -145,26 +144,6 @@ struct GemmSmem {
   static_assert(kBytes <= 232448, "shared memory budget exceeded");
 };
 
-// Row-block gating: an epilogue whose Params name a `ready` counter array starts each tile
-// once ready[tile row block] >= ready_target (acquire) instead of waiting for the whole
-// previous kernel, so a GEMM launched behind a persistent producer kernel works on row
-// blocks as they are finished. Other epilogues wait for the previous kernel (PDL).
-template <class E, class = void>
-struct EpiGate {
-  __device__ static bool gated(const typename E::Params&) { return false; }
-  __device__ static bool wait(const typename E::Params&, const TileCoord&) { return true; }
-};
-template <class E>
-struct EpiGate<E, std::void_t<decltype(E::Params::ready)>> {
-  __device__ static bool gated(const typename E::Params& p) { return p.ready != nullptr; }
-  __device__ static bool wait(const typename E::Params& p, const TileCoord& tc) {
-    if (p.ready == nullptr) return true;
-    const bool ok = wait_counter(p.ready + tc.a_row / kBM, p.ready_target);
-    fence_proxy_async_global();  // the tile's A rows were written by the producer kernel
-    return ok;
-  }
-};
-
 // NBOX = number of TMA boxes that make up the B tile (2 for SwiGLU: gate rows, up rows).
 template <int BN, int NSTAGE, int NACC, int NBOX, int G, bool CLUSTER, class Sched, class Epi>
 __global__ void __launch_bounds__(gemm_threads(G), 1)
@@ -227,9 +206,8 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
   tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   // The prologue above (barriers, TMEM) may overlap the previous kernel of the stream; no
-  // global memory is read or written before that kernel has completed (or, for a gated
-  // epilogue, before the tile's row block is ready).
-  if (!EpiGate<Epi>::gated(ep)) grid_dependency_wait();
+  // global memory is read or written before that kernel has completed.
+  grid_dependency_wait();
   grid_launch_dependents();
 
   if (warp == 0) {
@@ -244,11 +222,6 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
       const int ntiles = sched.count();
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         const TileCoord tc = sched.coord(t);
-        if (!EpiGate<Epi>::wait(ep, tc)) {
-          record_error(err, kErrTimeoutProducer);
-          ok = false;
-          break;
-        }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u)) {
             record_error(err, kErrTimeoutProducer);
@@ -1540,17 +1513,6 @@ struct EpiHeads {
     int policy_storage;         // 1888 (start of the wdl block)
     int n_total;                // policy_storage + 64
     int wdl_probs;
-    // Optional RMSNorm row scale folded out of the A operand (persistent forward): A is the
-    // residual stream x, the weights carry the final norm weight, and each row's logits
-    // are bf16(acc * rsqrt(sum(ss[row, :ss_parts]) / d + eps) + bias).
-    const float* ss = nullptr;
-    int ss_parts = 0;
-    float d = 0.0f;
-    float eps = 0.0f;
-    // Optional row-block gate (persistent forward): the tile of row block rb starts once
-    // ready[rb] >= ready_target instead of after the whole previous kernel.
-    const int* ready = nullptr;
-    int ready_target = 0;
   };
   __device__ static uint32_t bar_count(const Params&, int) { return 1; }
   __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
@@ -1565,31 +1527,14 @@ struct EpiHeads {
     const int row0 = tc.out_row + (et.r & ~31);  // first row of this warp's 32 rows
     float* tbuf = reinterpret_cast<float*>(ctx.smem_ptr) + (et.tid >> 5) * 32 * kPitch;
     const int n0 = tc.n_tile * BN;
-    float scale = 1.0f;
-    // The epilogue threads acquire the row block too before reading its sums of squares
-    // (already met: the producer waited before loading the tile).
-    if (p.ready != nullptr && !wait_counter(p.ready + tc.out_row / kBM, p.ready_target)) {
-      record_error(ctx.err, kErrTimeoutEpilogue);
-    }
-    if (p.ss != nullptr) {
-      const float* ss = p.ss + static_cast<size_t>(tc.out_row + et.r) * p.ss_parts;
-      float total = 0.0f;
-      for (int q = 0; q < p.ss_parts; ++q) total += ss[q];
-      scale = 1.0f / sqrtf(total / p.d + p.eps);
-    }
     for (int c = et.g * 32; c < BN; c += G * 32) {
       const int c0 = n0 + c;
       if (c0 >= p.n_total) break;  // uniform across the warp
       float v[32], b[32];
       load_acc32(et.taddr + c, v);
       load_bf16<32>(p.bias + c0, b);  // bias is padded to a multiple of 32 columns
-      if (p.ss != nullptr) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(__fmul_rn(v[j], scale), b[j]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
-      }
+      for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
       round_bf16_inplace(v);
       const int row = tc.out_row + et.r;
       const bool valid = et.r < tc.rows;

@@ -431,15 +431,6 @@ void dense_forward(const FwdParams& p, cudaStream_t s) {
 void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, float* policy,
                 float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,
                 int wdl_probs, cudaStream_t s) {
-  gemm_heads_scaled(tA, tB, bias, policy, wdl, moves_left, m, d, policy_size, policy_storage,
-                    wdl_probs, nullptr, 0, 0.0f, s);
-}
-
-void gemm_heads_scaled(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias,
-                       float* policy, float* wdl, float* moves_left, int m, int d,
-                       int policy_size, int policy_storage, int wdl_probs, const float* ss,
-                       int ss_parts, float eps, cudaStream_t s, const int* ready,
-                       int ready_target) {
   constexpr int BN = 256, NS = 3, NA = 2;
   using Epi = EpiHeads;
   auto kernel = gemm_tc_kernel<BN, NS, NA, 1, kG, false, DenseSched, Epi>;
@@ -449,12 +440,6 @@ void gemm_heads_scaled(const CUtensorMap& tA, const CUtensorMap& tB, const bf16*
   DenseSched sched{m, ceil_div(n_total, BN), ceil_div(m, kBM) * ceil_div(n_total, BN), BN, 0};
   typename Epi::Params ep{bias, policy, wdl, moves_left, policy_size, policy_storage, n_total,
                           wdl_probs};
-  ep.ss = ss;
-  ep.ss_parts = ss_parts;
-  ep.d = static_cast<float>(d);
-  ep.eps = eps;
-  ep.ready = ready;
-  ep.ready_target = ready_target;
   const int grid = std::min(sched.num_tiles, sm_count());
   launch(kernel, dim3(grid), gemm_threads(kG), smem, 0, s, tA, tB, null_map(), null_map(), sched,
          ep, ceil_div(d, kBK), device_error_word());

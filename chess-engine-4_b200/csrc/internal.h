@@ -79,15 +79,6 @@ void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMa
 void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, float* policy,
                 float* wdl, float* moves_left, int m, int d, int policy_size, int policy_storage,
                 int wdl_probs, cudaStream_t s);
-// gemm_heads with the final RMSNorm folded out of A: A is x, the head weights carry the norm
-// weight, and each row is scaled by rsqrt(sum(ss[row, :ss_parts]) / d + eps) before the bias.
-// `ready` (optional): a tile of row block rb starts once ready[rb] >= ready_target, so the
-// heads overlap the tail of the persistent tower that publishes those counters.
-void gemm_heads_scaled(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias,
-                       float* policy, float* wdl, float* moves_left, int m, int d,
-                       int policy_size, int policy_storage, int wdl_probs, const float* ss,
-                       int ss_parts, float eps, cudaStream_t s, const int* ready = nullptr,
-                       int ready_target = 0);
 // Per position b: probs[i] = softmax over i in [offsets[b], offsets[b+1]) of
 // policy[b, indices[i]] * temperature (legal-move policy of the lc0 backend).
 void policy_softmax(const float* policy, int batch, int policy_size, const int32_t* offsets,

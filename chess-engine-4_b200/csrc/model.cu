@@ -307,7 +307,6 @@ void Model::finalize() {
     bf16* heads = fwd_weights + cfg.depth * gu_elems;
     fold_columns(w("policy.weight"), w("final_norm.weight"), heads, static_cast<int64_t>(heads_rows), d,
                  stream);
-    tm_heads_folded = make_tmap_bf16(heads, heads_rows, d, d, 256);
     maps.heads = make_tmap_bf16(heads, heads_rows, d, d, 128);
     check_cuda(cudaStreamSynchronize(stream), "fold norm weights");
     if (fwd_dev == nullptr) {

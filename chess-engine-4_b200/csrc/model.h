@@ -72,7 +72,6 @@ struct Model {
   bool fused = false;
   uint8_t* fwd_dev = nullptr;      // FwdMaps
   bf16* fwd_weights = nullptr;     // norm-folded gate_up [depth][2h, d], then heads [Ps + 64, d]
-  CUtensorMap tm_heads_folded{};
   size_t fwd_sync_bytes = 0;
   unsigned long long* fwd_trace = nullptr;  // optional per-task timeline (device buffer)
   int fwd_trace_cap = 0;
