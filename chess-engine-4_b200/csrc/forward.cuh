@@ -81,17 +81,37 @@ __device__ __forceinline__ FwdTask fwd_decode(const FwdParams& p, int t) {
     return k;
   }
   t -= k.layer * per_layer;
-  if (t < p.nb * p.nc) {
-    k.type = kTaskGateUp;
-    k.rb = t / p.nc;
-    k.col = t - k.rb * p.nc;
+  // Within a layer: the gate_up tiles of row block i, followed by the down tiles of row block
+  // i - lag (lag = nb: every gate_up tile of the layer first, then every down tile).
+  const int per_dn = p.xt * p.dks;
+  const int lag = p.lag;
+  int i, r;
+  bool gu;
+  if (t < lag * p.nc) {
+    i = t / p.nc;
+    r = t - i * p.nc;
+    gu = true;
+  } else if (t < lag * p.nc + (p.nb - lag) * (p.nc + per_dn)) {
+    const int u = t - lag * p.nc;
+    i = lag + u / (p.nc + per_dn);
+    r = u - (i - lag) * (p.nc + per_dn);
+    gu = r < p.nc;
+    if (!gu) r -= p.nc;
   } else {
-    t -= p.nb * p.nc;
+    const int u = t - lag * p.nc - (p.nb - lag) * (p.nc + per_dn);
+    i = p.nb + u / per_dn;
+    r = u - (i - p.nb) * per_dn;
+    gu = false;
+  }
+  if (gu) {
+    k.type = kTaskGateUp;
+    k.rb = i;
+    k.col = r;
+  } else {
     k.type = kTaskDown;
-    k.rb = t / (p.xt * p.dks);
-    const int rem = t - k.rb * (p.xt * p.dks);
-    k.col = rem / p.dks;
-    k.kh = rem - k.col * p.dks;
+    k.rb = i - lag;
+    k.col = r / p.dks;
+    k.kh = r - k.col * p.dks;
   }
   return k;
 }

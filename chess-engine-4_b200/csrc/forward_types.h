@@ -85,6 +85,7 @@ struct FwdParams {
   int part_rb_chunks;  // 64 KB partial-sum chunks per row block: (d / 128) * max(kis, dks)
   int kb_in;   // k-blocks of the input GEMM (in_dim / 64)
   int d96;     // 1: 128-column down tiles use 96-deep stages (h % 96 == 0)
+  int lag;     // 1..nb: a layer's down tiles of row block i follow its gate_up tiles of i + lag
   int total_tasks;
   float eps;
   // Optional per-task timeline (nullptr: off): kFwdTraceWords u64 per task id < trace_cap,

@@ -419,7 +419,7 @@ void dense_forward(const FwdParams& p, cudaStream_t s) {
               p.batch <= p.nb * 128 && p.policy != nullptr && p.wdl != nullptr &&
               p.moves_left != nullptr && p.head_bias != nullptr && p.policy_size <= p.policy_storage &&
               p.policy_storage % 32 == 0 && p.head_cols == p.policy_storage + 64 &&
-              p.nht == (p.head_cols + 255) / 256,
+              p.nht == (p.head_cols + 255) / 256 && p.lag >= 1 && p.lag <= p.nb,
           "persistent forward: unsupported shape");
   auto kernel = dense_forward_kernel;
   ensure_smem(kernel, FwdSmem::kBytes);
