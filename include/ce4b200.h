@@ -208,11 +208,12 @@ int ce4b_expert_parallel_plan(int world, int rank, const int32_t* meta_send, con
  * last load was issued, its first MMA was issued, its accumulator was committed, its
  * epilogue started and finished, its results were staged in shared memory and published,
  * the store warp took the staged tile; then the CTA index; then the tile's global stores
- * completed. 0 disables. Task ids are numbered
- * input-GEMM tiles first (row block, slice, k split), then per layer the gate_up tiles
- * (row block, hidden chunk) and the down tiles (row block, slice), then the head tiles
- * (row block, 256 head columns). ce4b_model_task_count gives the number of tasks of a
- * forward at `batch` (0 when the model does not use the persistent forward). */
+ * completed. 0 disables. Task ids are numbered input-GEMM tiles first (row block, slice,
+ * k split); then per layer the gate_up tiles of row block i (hidden chunk) each followed by
+ * the down tiles of row block i - lag (slice, k split), lag = ceil(5/8 of the row blocks),
+ * the remaining down tiles last; then the head tiles (row block, 256 head columns).
+ * ce4b_model_task_count gives the number of tasks of a forward at `batch` (0 when the
+ * model does not use the persistent forward). */
 int ce4b_model_set_task_trace(ce4b_model* model, void* device_buffer, int capacity_tasks);
 int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks);
 
