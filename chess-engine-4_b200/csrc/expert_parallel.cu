@@ -2,8 +2,8 @@
 // consecutive experts each); every rank routes its own tokens and the routed rows travel
 // to the rank that owns their expert and back with NCCL send/recv over NVLink.
 //
-// One MoE layer on one rank (the reference's static dispatch path, moe.py:226-287, with the
-// all-to-all of SURVEY's expert-parallel plan):
+// One MoE layer on one rank (the reference's static dispatch path, moe.py:226-287, with an
+// all-to-all of the routed rows between the ranks that own the experts):
 //   1. router GEMM + top-2, routing scan, dispatch into 128-row expert segments (the same
 //      kernels as the single-GPU layer). Segments are ordered by expert, so the rows for
 //      rank r are one contiguous run.

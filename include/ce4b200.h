@@ -183,7 +183,7 @@ int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count);
 /* ------------------------------------------------------------------ expert parallelism
  * moe64a2 across `world` GPUs (one process and one model handle per GPU): each rank
  * computes 64 / world consecutive experts; every MoE layer sends each routed row to the
- * rank of its expert and back with NCCL send/recv (the reference's
+ * rank of its expert and back with NCCL send/recv (expert parallelism over the reference's
  * static dispatch path, src/chess_engine_4/model/moe.py:226-287). Each rank passes its own
  * batch of positions to ce4b_model_forward / ce4b_model_evaluate; results equal the
  * single-GPU forward of those positions. The forward synchronises with the host once per
