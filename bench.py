@@ -2,9 +2,9 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1]
 
-Default workload: the dense d512 x 12 SwiGLU tower (hidden 1536,
-BF16, weights N(0, 0.02)) on a batch of 4096 synthetic positions per GPU (lc0
-InputPlane records, seeded Bernoulli(0.08) planes). Other configurations of BASELINE.json
+Default workload (the headline configuration, c1): the dense d512 x 12 SwiGLU tower
+(hidden 1536, BF16, weights N(0, 0.02)) on a batch of 4096 synthetic positions per GPU (lc0
+InputPlane records, seeded Bernoulli(0.08) planes). The other benchmark configurations
 are selectable with --config (c0 d128x6, c2 MXFP8 d512 batch 16384, c3 moe64a2 d768 batch
 8192 per GPU, c4 / c4-mxfp8 d1024x16 batch 65536 split over the GPUs). One step = one forward of one batch. Each rank of a
 multi-GPU run is an independent replica on its own batch (weak scaling, no collective on
@@ -59,7 +59,7 @@ class Config:
     batch: int  # positions per step: per GPU (weak) or split over the GPUs (strong)
     precision: str  # "bf16" | "mxfp8"
     cpu_sample: int  # positions per CPU-baseline sample
-    strong: bool = False  # BASELINE.json splits this config's batch data-parallel
+    strong: bool = False  # the config's batch is split data-parallel over the GPUs
 
     def per_gpu(self, world: int) -> int:
         if not self.strong:
@@ -77,7 +77,8 @@ class Config:
         return self.hidden if self.arch == "dense" else 4 * self.d
 
     def flop_per_pos(self) -> float:
-        """Algorithmic GEMM FLOPs per position."""
+        """Algorithmic GEMM FLOPs per position: 2 (7168 d + L 3 d h + 1862 d), plus the MoE
+        router and expert terms for moe64a2."""
 
         d = self.d
         f = 2 * (IN_DIM * d + 1862 * d)
