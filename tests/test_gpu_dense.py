@@ -168,6 +168,8 @@ def test_forward_normalizes_rule50_in_place_like_reference() -> None:
         (1024, 2, 3.0, 300),  # four 256-column input tiles per row block
         (256, 4, 3.0, 300),
         (128, 2, 3.0, 7),  # 128-column input tiles, one partial row block
+        (512, 2, 2.0, 300),  # h = 1024: down tiles in 64-deep stages (h % 96 != 0), K split
+        (512, 2, 2.0, 2048),  # same, one K part per down tile
     ],
 )
 def test_persistent_forward_matches_folded_restatement(d: int, depth: int, ratio: float, batch: int) -> None:
