@@ -85,18 +85,22 @@ struct Model {
   // Input tiles: 256 columns where d allows.
   int fused_xwi() const { return cfg.d_model % 256 == 0 ? 256 : 128; }
   // Small batches leave most SMs idle while each row block's chain runs: the input tiles
-  // are then split into 8 K parts and the (128-wide) down tiles into 4, the parts summed
-  // in fixed order by the last finisher. Row blocks up to which this applies:
+  // are then split into 8 K parts, the parts summed in fixed order by the last finisher.
+  // Row blocks up to which this applies:
   int fused_small_nb() const {
-    const int per_rb = std::max((cfg.d_model / fused_xwi()) * 8, (cfg.d_model / 128) * 4);
+    const int per_rb = (cfg.d_model / fused_xwi()) * 8;
     return std::max(0, std::min(rows_cap / 128, sm_count() / per_rb));
   }
   bool fused_small(int batch) const {
     const int nb = (batch + 127) / 128;
-    return nb <= fused_small_nb() && fused_xw(batch) == 128 && (dense_hidden / 64) % 4 == 0;
+    return nb <= fused_small_nb() && fused_xw(batch) == 128;
   }
   int fused_kis(int batch) const { return fused_small(batch) ? 8 : 2; }
-  int fused_dks(int batch) const { return fused_small(batch) ? 4 : 1; }
+  // Down tiles are not split along K: with 96-deep stages a 128-column down tile runs
+  // 6 MMAs per stage, and splitting it in 2 or 4 parts measured equal or slower at every
+  // batch (B = 64 249 vs 249 µs, 256: 253 vs 257, 640: 259 vs 266, 1152: 262 vs 275 with
+  // 4 parts; 2 parts slower still). The kernel keeps the split (dks parts) as a parameter.
+  int fused_dks(int) const { return 1; }
   int fused_head_tasks() const { return (policy_storage + 64 + 255) / 256; }
   int fused_task_count(int batch) const {
     const int nb = (batch + 127) / 128, xt = cfg.d_model / fused_xw(batch), nc = dense_hidden / 128;
