@@ -8,6 +8,8 @@ import subprocess
 import sys
 from pathlib import Path
 
+import pytest
+
 REPO = Path(__file__).resolve().parents[1]
 
 
@@ -34,3 +36,21 @@ def test_reference_arm_prints_contract_line() -> None:
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+@pytest.mark.gpu
+def test_our_arm_prints_roofline_and_launch_count() -> None:
+    out = subprocess.run(
+        [sys.executable, str(REPO / "bench.py"), "--quick", "--config", "c0", "--steps", "3", "--warmup", "3"],
+        cwd=REPO, capture_output=True, text=True, timeout=900, check=True,
+    )
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out.stdout
+    d = json.loads(lines[0])
+    assert "impl" not in d and d["value"] > 0 and d["n_gpus"] == 1
+    roof = d["roofline"]
+    assert roof["bound"] in ("tensor", "hbm") and roof["unit"] in ("TFLOP/s", "GB/s")
+    assert roof["achieved"] > 0 and roof["peak"] > 0
+    assert abs(roof["frac"] - roof["achieved"] / roof["peak"]) < 1e-6
+    assert d["gpu_launches"] > 0 and d["kernels_per_step"] >= 1
+    assert "dense_tower" in d["kernel_ms_per_step"]
