@@ -9,7 +9,10 @@
 // size instead, so the call allocates nothing.
 //
 // The array is part of the library's device image: every GPU on which the library is
-// loaded holds kStaticScratchBytes for the life of the process. All calls on a device
+// loaded holds kStaticScratchBytes for the life of the process. With CUDA's lazy module
+// loading (the default of recent toolkits) the image is loaded, and the 8 MiB reserved,
+// on the first call on each device: a host whose allocator freezes after start-up should
+// make one call per device during start-up. All calls on a device
 // share it and it keeps the previous call's contents; the block writes every scratch
 // element it reads before reading it, so nothing needs clearing. Calls whose GPU work
 // overlaps (different streams, or different host threads on one device) race on the
@@ -36,7 +39,8 @@ std::mutex g_scratch_mu;
 // Device address of g_static_scratch on the current device. The name of a __device__
 // array in host code is a host-side stand-in, so the address is looked up once per
 // device (with that device current) and cached. The first call on a device does this
-// lookup; it should come before any stream capture.
+// lookup, which also loads the library's device image there (reserving the array); it
+// should come during the host's start-up, before any stream capture.
 void* scratch_address() {
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
@@ -106,6 +110,9 @@ extern "C" int ce4b_dense_block_forward_static(const void* x_dev, const void* no
     return e.status;
   } catch (const std::exception& e) {
     set_last_error(e.what());
+    return CE4B_ERR_INVALID_ARGUMENT;
+  } catch (...) {
+    set_last_error("unknown error");
     return CE4B_ERR_INVALID_ARGUMENT;
   }
 }

@@ -304,7 +304,9 @@ int ce4b_mxfp8_gemm(const void* a_codes_dev, const void* a_scales_dev, const voi
  * the library (held on every GPU that loads it), so rows * (d_model + hidden_dim) * 2
  * bytes, each part rounded up to 128 rows and 256 bytes, must fit in 8 MiB; larger calls
  * fail with CE4B_ERR_INVALID_ARGUMENT. The first call on a device looks up the array's
- * device address and should come before any stream capture. All calls on a device share
+ * device address, which (under CUDA's default lazy module loading) loads the library's
+ * device image there and reserves the 8 MiB: make that first call during start-up, before
+ * any stream capture and before the allocator is frozen. All calls on a device share
  * the array: calls whose GPU work overlaps race and must be serialised by the caller.
  * Allocates nothing. This entry point has no counterpart in the reference. */
 int ce4b_dense_block_forward_static(const void* x_dev, const void* norm_weight_dev,
