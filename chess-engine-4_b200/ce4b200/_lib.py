@@ -65,6 +65,16 @@ class ModelInfoStruct(ctypes.Structure):
     ]
 
 
+class Mxfp8TapStruct(ctypes.Structure):
+    _fields_ = [("layer", ctypes.c_int32)] + [
+        (name, ctypes.c_void_p)
+        for name in (
+            "a_codes_dev", "a_scales_dev", "n_bf16_dev", "n_codes_dev", "n_scales_dev",
+            "h_bf16_dev", "h_codes_dev", "h_scales_dev",
+        )
+    ]
+
+
 class Ce4bError(RuntimeError):
     """A libce4b200 call failed on the device or in CUDA."""
 
@@ -112,8 +122,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ce4b_model_enable_expert_parallel": (_i32, [_vp, _i32, _i32, _vp]),
     "ce4b_expert_parallel_plan": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32, ctypes.POINTER(_i32)]),
     "ce4b_model_task_count": (_i32, [_vp, _i32, ctypes.POINTER(_i32)]),
+    "ce4b_model_set_mxfp8_tap": (_i32, [_vp, ctypes.POINTER(Mxfp8TapStruct)]),
     "ce4b_model_trace_label": (_i32, [_vp, _i32, ctypes.c_char_p, _i32]),
     "ce4b_model_destroy": (None, [_vp]),
+    "ce4b_selftest_bounded_wait": (_i32, [_i32, _i64, ctypes.POINTER(_i64), _vp]),
     "ce4b_bf16_gemm": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "ce4b_rmsnorm_forward": (_i32, [_vp, _vp, _vp, _i32, _i32, _f32, _vp]),
     "ce4b_swiglu_forward": (_i32, [_vp, _vp, _i32, _i32, _vp]),
@@ -124,6 +136,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _f32, _i32, _vp],
     ),
     "ce4b_moe_route": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp]),
+    "ce4b_moe_dispatch_capacity": (_i32, [_i32]),
+    "ce4b_moe_route_dispatch_workspace_size": (_i64, [_i32]),
+    "ce4b_moe_route_dispatch": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp],
+    ),
     "ce4b_moe_workspace_size": (_i64, [_i32, _i32, _i32]),
     "ce4b_moe_forward": (
         _i32,

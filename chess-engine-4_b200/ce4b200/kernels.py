@@ -8,6 +8,7 @@ device, dtype, rank and shape problems; src/chess_engine_4/kernels/dense.py:33-4
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import NamedTuple
 
 import torch
 
@@ -309,6 +310,61 @@ def moe_route(
             )
         )
     return experts, probs, counts
+
+
+class MoeDispatch(NamedTuple):
+    """Result of :func:`moe_route_dispatch` (all on the input's device)."""
+
+    logits: torch.Tensor          # BF16 [T, 64]: the router logits the selection used
+    experts: torch.Tensor         # int32 [T, 2]: best expert first
+    probs: torch.Tensor           # float32 [T, 2]: BF16-rounded routing weights
+    positions: torch.Tensor       # int32 [T, 2]: row of each route in the permuted layout
+    expert_offsets: torch.Tensor  # int32 [65]: segment starts (multiples of 128), then the total
+    counts: torch.Tensor          # int32 [64]: routes per expert
+    rows: torch.Tensor            # BF16 [capacity, d]: permuted rows (padding rows unwritten)
+    row_probs: torch.Tensor       # float32 [capacity]: routing weight of each permuted row
+
+
+def moe_route_dispatch(n: torch.Tensor, router_weight: torch.Tensor, qb_beta: torch.Tensor) -> MoeDispatch:
+    """Routing and static dispatch of one MoE layer with the forward's own kernels (router
+    GEMM + top-2 epilogue, histogram scan, dispatch): ``MoeBlock.forward``'s eval-path
+    selection and ``_run_experts_static`` placement (src/chess_engine_4/model/moe.py:36-47,
+    160-177, 232-267). Routes are ordered by ``2 * token + k`` within each expert, and
+    every expert segment starts on a multiple of 128 rows."""
+
+    _check_bf16_matrix("n", n)
+    tokens, d_model = n.shape
+    if tuple(router_weight.shape) != (EXPERT_COUNT, d_model) or router_weight.dtype != torch.bfloat16:
+        raise ValueError(f"router_weight must be BF16 [64, {d_model}]")
+    if not router_weight.is_contiguous() or router_weight.device != n.device:
+        raise ValueError("router_weight must be contiguous and on n's device")
+    beta = qb_beta.to(device=n.device, dtype=torch.float32).contiguous()
+    if tuple(beta.shape) != (EXPERT_COUNT,):
+        raise ValueError("qb_beta must have 64 entries")
+    lib = _lib.library()
+    cap = lib.ce4b_moe_dispatch_capacity(tokens)
+    dev = n.device
+    out = MoeDispatch(
+        logits=torch.empty(tokens, EXPERT_COUNT, dtype=torch.bfloat16, device=dev),
+        experts=torch.empty(tokens, 2, dtype=torch.int32, device=dev),
+        probs=torch.empty(tokens, 2, dtype=torch.float32, device=dev),
+        positions=torch.empty(tokens, 2, dtype=torch.int32, device=dev),
+        expert_offsets=torch.empty(EXPERT_COUNT + 1, dtype=torch.int32, device=dev),
+        counts=torch.empty(EXPERT_COUNT, dtype=torch.int32, device=dev),
+        rows=torch.empty(cap, d_model, dtype=torch.bfloat16, device=dev),
+        row_probs=torch.empty(cap, dtype=torch.float32, device=dev),
+    )
+    ws = torch.empty(lib.ce4b_moe_route_dispatch_workspace_size(tokens), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(
+            lib.ce4b_moe_route_dispatch(
+                n.data_ptr(), router_weight.data_ptr(), beta.data_ptr(), out.logits.data_ptr(),
+                out.experts.data_ptr(), out.probs.data_ptr(), out.positions.data_ptr(),
+                out.expert_offsets.data_ptr(), out.counts.data_ptr(), out.rows.data_ptr(),
+                out.row_probs.data_ptr(), ws.data_ptr(), tokens, d_model, _stream(n),
+            )
+        )
+    return out
 
 
 def policy_softmax(

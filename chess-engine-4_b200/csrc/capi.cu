@@ -276,6 +276,20 @@ int ce4b_model_set_task_trace(ce4b_model* model, void* device_buffer, int capaci
   });
 }
 
+int ce4b_model_set_mxfp8_tap(ce4b_model* model, const ce4b_mxfp8_tap* tap) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    ce4b::Model& m = *model->impl;
+    if (tap == nullptr || tap->layer < 0) {
+      m.mx_tap = ce4b_mxfp8_tap{-1, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+      return;
+    }
+    if (!m.mx) fail(CE4B_ERR_UNSUPPORTED, "the MXFP8 tap needs an MXFP8 model");
+    require(tap->layer <= m.cfg.depth, "tap layer must be in [0, depth]");
+    m.mx_tap = *tap;
+  });
+}
+
 int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks) {
   return guarded([&] {
     require(model != nullptr && model->impl && tasks != nullptr, "null argument");
@@ -400,6 +414,55 @@ int ce4b_moe_route(const void* logits_dev, const float* beta_dev, int32_t* exper
     moe_route_logits(static_cast<const bf16*>(logits_dev), beta_dev,
                      reinterpret_cast<int2*>(experts_dev), reinterpret_cast<float2*>(probs_dev),
                      counts_dev, tokens, as_stream(stream));
+  });
+}
+
+int ce4b_moe_dispatch_capacity(int tokens) {
+  if (tokens < 1) return -1;
+  // Two routes per token; every expert segment padded to a multiple of 128 rows.
+  return (2 * ((tokens + 127) / 128 * 128) + 64 * 127 + 127) / 128 * 128;
+}
+
+int64_t ce4b_moe_route_dispatch_workspace_size(int tokens) {
+  if (tokens < 1) return -1;
+  const int64_t tiles = (static_cast<int64_t>(tokens) + 127) / 128;
+  const int64_t cap_tiles = ce4b_moe_dispatch_capacity(tokens) / 128;
+  auto a = [](int64_t v) { return (v + 255) / 256 * 256; };
+  return 2 * a(tiles * 64 * 4) + a(cap_tiles * 16) + a(4);
+}
+
+int ce4b_moe_route_dispatch(const void* n_dev, const void* router_weight_dev, const float* beta_dev,
+                            void* logits_dev, int32_t* experts_dev, float* probs_dev,
+                            int32_t* positions_dev, int32_t* expert_offsets_dev,
+                            int32_t* counts_dev, void* xperm_dev, float* pprob_dev,
+                            void* workspace_dev, int tokens, int d_model, void* stream) {
+  return guarded([&] {
+    require(n_dev && router_weight_dev && beta_dev && experts_dev && probs_dev && positions_dev &&
+                expert_offsets_dev && xperm_dev && pprob_dev && workspace_dev,
+            "null pointer");
+    require(tokens >= 1, "tokens must be positive");
+    require(d_model >= 64 && d_model % 64 == 0, "d_model must be a multiple of 64");
+    require((reinterpret_cast<uintptr_t>(workspace_dev) & 255u) == 0,
+            "workspace must be 256-byte aligned");
+    cudaStream_t s = as_stream(stream);
+    auto a = [](int64_t v) { return (v + 255) / 256 * 256; };
+    const int tiles = (tokens + 127) / 128;
+    auto* base = static_cast<uint8_t*>(workspace_dev);
+    auto* block_hist = reinterpret_cast<int*>(base);
+    auto* block_off = reinterpret_cast<int*>(base + a(tiles * 64 * 4));
+    auto* m_tiles = reinterpret_cast<int4*>(base + 2 * a(tiles * 64 * 4));
+    const int64_t cap_tiles = ce4b_moe_dispatch_capacity(tokens) / 128;
+    auto* num_m_tiles = reinterpret_cast<int*>(base + 2 * a(tiles * 64 * 4) + a(cap_tiles * 16));
+    const CUtensorMap t_n = make_tmap_bf16(n_dev, tokens, d_model, d_model, 128);
+    const CUtensorMap t_r = make_tmap_bf16(router_weight_dev, 64, d_model, d_model, 64);
+    auto* route_expert = reinterpret_cast<int2*>(experts_dev);
+    auto* route_prob = reinterpret_cast<float2*>(probs_dev);
+    moe_router_gemm(t_n, t_r, beta_dev, route_expert, route_prob, block_hist, tokens, d_model, s,
+                    static_cast<bf16*>(logits_dev));
+    moe_scan(block_hist, tiles, expert_offsets_dev, block_off, m_tiles, num_m_tiles, counts_dev, s);
+    moe_dispatch(static_cast<const bf16*>(n_dev), route_expert, route_prob, expert_offsets_dev,
+                 block_off, static_cast<bf16*>(xperm_dev), pprob_dev, positions_dev, tokens,
+                 d_model, s);
   });
 }
 

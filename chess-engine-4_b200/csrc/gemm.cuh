@@ -1219,6 +1219,17 @@ __device__ __forceinline__ void stage_u8x32(uint32_t tile, int r, int col, const
 }
 
 // TMA-store a staged [128 x cols] code tile (cols / 128 boxes) at (x0, y0).
+// 32 BF16 values of one row to global memory (a test tap of the MXFP8 epilogues: the
+// values a quantising epilogue saw).
+__device__ __forceinline__ void store_bf16x32_global(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    d4[u] = make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
+                       pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
+  }
+}
+
 __device__ __forceinline__ void store_staged_u8(const CUtensorMap* map, uint32_t tile, int cols,
                                                 int x0, int y0) {
   for (int b = 0; b < cols / 128; ++b) {
@@ -1296,6 +1307,7 @@ struct EpiSwiGLU {
   struct Params {
     uint8_t* scales;  // MX: [M/128][h/128][512] scale tiles of the hidden codes
     int col_tiles;    // MX: h / 128
+    __nv_bfloat16* tap;  // MX: [M, h] the BF16 hidden values quantised (nullptr: not stored)
   };
   __device__ static uint32_t bar_count(const Params&, int) { return 1; }
   __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
@@ -1328,6 +1340,10 @@ struct EpiSwiGLU {
         stage_u8x32(ctx.smem, et.r, c, q);
         if (et.r < tc.rows) {
           p.scales[mx_scale_offset(tc.out_row + et.r, (tc.n_tile * HC + c) / 32, p.col_tiles)] = sc;
+          if (p.tap != nullptr) {
+            store_bf16x32_global(
+                p.tap + static_cast<size_t>(tc.out_row + et.r) * (p.col_tiles * 128) + tc.n_tile * HC + c, g);
+          }
         }
       } else {
         stage_bf16x32(ctx.smem, et.r, c, g);
@@ -1376,6 +1392,7 @@ struct EpiResNorm {
     int cluster_n;  // CTAs per row = d / BN
     float eps;
     uint8_t* n_scales;  // MX: [M/128][d/128][512]
+    __nv_bfloat16* tap;  // MX: [M, d] the BF16 values of n quantised (nullptr: not stored)
   };
   __device__ static int groups(int G) { return G < BN / 32 ? G : BN / 32; }
   __device__ static uint32_t bar_count(const Params& p, int G) {
@@ -1476,6 +1493,9 @@ struct EpiResNorm {
           stage_u8x32(ctx.ring, et.r, c, q);
           if (et.r < tc.rows) {
             p.n_scales[mx_scale_offset(tc.out_row + et.r, (n0 + c) / 32, p.d / 128)] = sc;
+            if (p.tap != nullptr) {
+              store_bf16x32_global(p.tap + static_cast<size_t>(tc.out_row + et.r) * p.d + n0 + c, v);
+            }
           }
         } else {
           stage_bf16x32(ctx.ring, et.r, c, v);
@@ -1619,6 +1639,7 @@ struct EpiRouter {
     int2* route_expert;  // [T]
     float2* route_prob;  // [T] (BF16-rounded values)
     int* block_hist;     // [T/128 tiles][64]
+    __nv_bfloat16* logits;  // [T, 64] the BF16 logits the selection used (nullptr: not stored)
   };
   __device__ static uint32_t bar_count(const Params&, int) { return 1; }
   __device__ static bool prefetch(const Params&, const TileCoord&, const CUtensorMap*, uint32_t,
@@ -1644,6 +1665,16 @@ struct EpiRouter {
         const int row = tc.out_row + et.r;
         p.route_expert[row] = make_int2(e0, e1);
         p.route_prob[row] = make_float2(p0, p1);
+        if (p.logits != nullptr) {
+          uint4* dst = reinterpret_cast<uint4*>(p.logits + static_cast<size_t>(row) * 64);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            dst[u] = make_uint4(pack_bf16x2(lo[8 * u], lo[8 * u + 1]), pack_bf16x2(lo[8 * u + 2], lo[8 * u + 3]),
+                                pack_bf16x2(lo[8 * u + 4], lo[8 * u + 5]), pack_bf16x2(lo[8 * u + 6], lo[8 * u + 7]));
+            dst[4 + u] = make_uint4(pack_bf16x2(hi[8 * u], hi[8 * u + 1]), pack_bf16x2(hi[8 * u + 2], hi[8 * u + 3]),
+                                    pack_bf16x2(hi[8 * u + 4], hi[8 * u + 5]), pack_bf16x2(hi[8 * u + 6], hi[8 * u + 7]));
+          }
+        }
         atomicAdd(&hist[e0], 1);
         atomicAdd(&hist[e1], 1);
       }

@@ -204,12 +204,12 @@ void gemm_mx_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUte
 
 void gemm_mx_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH,
                     const uint8_t* sfa, const uint8_t* sfb, uint8_t* h_scales, int m,
-                    int hidden_dim, int k, cudaStream_t s) {
+                    int hidden_dim, int k, cudaStream_t s, bf16* tap) {
   require(hidden_dim % 128 == 0 && k % 128 == 0, "MXFP8 SwiGLU needs multiples of 128");
   using Epi = EpiSwiGLU<128, true>;
   const int chunks = hidden_dim / 128;
   DenseSched sched{m, chunks, ceil_div(m, kBM) * chunks, 128, hidden_dim};
-  typename Epi::Params ep{h_scales, chunks};
+  typename Epi::Params ep{h_scales, chunks, tap};
   const MxScales sf{sfa, sfb, k / 128};
   constexpr int kStatKb = 4;
   if (k / 128 <= kStatKb && chunks <= sm_count() && sched.num_tiles >= sm_count()) {
@@ -236,7 +236,7 @@ void gemm_mx_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensor
 void gemm_mx_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
                      const CUtensorMap& tN, const uint8_t* sfa, const uint8_t* sfb,
                      uint8_t* n_scales, const bf16* bias, const bf16* norm_w, int m, int d, int k,
-                     float eps, cudaStream_t s) {
+                     float eps, cudaStream_t s, bf16* tap) {
   require(d % 128 == 0 && d / 128 <= kMaxClusterN && k % 128 == 0,
           "MXFP8 residual GEMM needs d a multiple of 128 up to 1024 and K a multiple of 128");
   if (d % 256 == 0 && d / 256 <= 4) {
@@ -249,8 +249,8 @@ void gemm_mx_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtenso
     ensure_smem(kernel, smem);
     const int cn = d / BN;
     DenseSched sched{m, cn, ceil_div(m, kBM) * cn, BN, 128};
-    typename Epi::Params ep{bias,     norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
-                            cn,       eps,    n_scales};
+    typename Epi::Params ep{bias, norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
+                            cn,   eps,    n_scales, tap};
     const MxScales sf{sfa, sfb, k / 128};
     launch(kernel, dim3(sched.num_tiles), gemm_threads(kG), smem, cn, s, tA, tB, tX, tN, sched, ep,
            sf, k / 128, device_error_word());
@@ -263,8 +263,8 @@ void gemm_mx_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtenso
   ensure_smem(kernel, smem);
   const int cn = d / BN;
   DenseSched sched{m, cn, ceil_div(m, kBM) * cn, BN, 0};
-  typename Epi::Params ep{bias,     norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
-                          cn,       eps,    n_scales};
+  typename Epi::Params ep{bias, norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
+                          cn,   eps,    n_scales, tap};
   const MxScales sf{sfa, sfb, k / 128};
   launch(kernel, dim3(sched.num_tiles), gemm_threads(kG), smem, cn, s, tA, tB, tX, tN, sched, ep,
          sf, k / 128, device_error_word());
@@ -448,14 +448,14 @@ void gemm_heads(const CUtensorMap& tA, const CUtensorMap& tB, const bf16* bias, 
 // ------------------------------------------------------------------ MoE GEMMs
 void moe_router_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const float* beta,
                      int2* route_expert, float2* route_prob, int* block_hist, int tokens, int d,
-                     cudaStream_t s) {
+                     cudaStream_t s, bf16* logits_out) {
   constexpr int BN = 64, NS = 8, NA = 1;
   using Epi = EpiRouter;
   auto kernel = gemm_tc_kernel<BN, NS, NA, 1, kG, false, DenseSched, Epi>;
   constexpr int smem = GemmSmem<BN, NS, NA, Epi>::kBytes;
   ensure_smem(kernel, smem);
   DenseSched sched{tokens, 1, ceil_div(tokens, kBM), BN, 0};
-  typename Epi::Params ep{beta, route_expert, route_prob, block_hist};
+  typename Epi::Params ep{beta, route_expert, route_prob, block_hist, logits_out};
   // One tile (128 tokens) per CTA: block_hist row = tile index.
   launch(kernel, dim3(sched.num_tiles), gemm_threads(kG), smem, 0, s, tA, tB, null_map(),
          null_map(), sched, ep, ceil_div(d, kBK), device_error_word());

@@ -88,10 +88,13 @@ void fold_columns(const bf16* W, const bf16* w, bf16* out, int64_t rows, int col
 
 // ---------------------------------------------------------------- MoE
 // Router GEMM (A = normalised rows [T, d], B = router weight [64, d] with 64-row boxes)
-// with the top-2 routing epilogue; block_hist receives [ceil(T/128)][64] counts.
+// with the top-2 routing epilogue; block_hist receives [ceil(T/128)][64] counts and, when
+// logits_out is set, the BF16 logits [T, 64] the selection used.
 void moe_router_gemm(const CUtensorMap& tA, const CUtensorMap& tB, const float* beta,
                      int2* route_expert, float2* route_prob, int* block_hist, int tokens, int d,
-                     cudaStream_t s);
+                     cudaStream_t s, bf16* logits_out = nullptr);
+// expert_start receives 65 entries: segment starts (each padded to 128 rows), then the
+// total number of permuted rows.
 void moe_scan(const int* block_hist, int ntiles, int* expert_start, int* block_off,
               int4* m_tiles, int* num_m_tiles, int* counts_out, cudaStream_t s);
 void moe_dispatch(const bf16* n, const int2* route_expert, const float2* route_prob,
@@ -127,13 +130,15 @@ void gemm_mx_store_bf16(const CUtensorMap& tA, const CUtensorMap& tB, const CUte
                         cudaStream_t s);
 // MXFP8 forms of the forward's GEMMs (code maps from make_tmap_u8 with 128-row boxes; the
 // x map of the residual GEMM stays BF16). sfa/sfb are the A/B scale tiles.
+// `tap` (tests): when set, the BF16 values the epilogue quantised are also written there
+// ([m, hidden_dim] / [m, d] row-major).
 void gemm_mx_swiglu(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tH,
                     const uint8_t* sfa, const uint8_t* sfb, uint8_t* h_scales, int m,
-                    int hidden_dim, int k, cudaStream_t s);
+                    int hidden_dim, int k, cudaStream_t s, bf16* tap = nullptr);
 void gemm_mx_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,
                      const CUtensorMap& tN, const uint8_t* sfa, const uint8_t* sfb,
                      uint8_t* n_scales, const bf16* bias, const bf16* norm_w, int m, int d, int k,
-                     float eps, cudaStream_t s);
+                     float eps, cudaStream_t s, bf16* tap = nullptr);
 void gemm_mx_heads(const CUtensorMap& tA, const CUtensorMap& tB, const uint8_t* sfa,
                    const uint8_t* sfb, const bf16* bias, float* policy, float* wdl,
                    float* moves_left, int m, int d, int policy_size, int policy_storage,

@@ -150,7 +150,7 @@ void Model::plan_workspace() {
     ws_off.route_pos = take(r * 8);
     ws_off.block_hist = take(tiles * 64 * 4);
     ws_off.block_off = take(tiles * 64 * 4);
-    ws_off.expert_start = take(64 * 4);
+    ws_off.expert_start = take(65 * 4);
     ws_off.m_tiles = take((p / 128) * 16);
     ws_off.num_m_tiles = take(4);
     ws_off.xperm = take(p * d * 2);
@@ -386,21 +386,48 @@ void Model::forward_mx(int layout, void* input, const void* scalars, int batch, 
   auto* a_scales = workspace + ws_off.a_scales;
   auto* n_scales = workspace + ws_off.n_scales;
   auto* h_scales = workspace + ws_off.h_scales;
+  // Test tap (outside stream capture only): the BF16 operands of one layer's quantisation
+  // points and the codes and scales written for them.
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  check_cuda(cudaStreamIsCapturing(s, &capture), "query stream capture");
+  const ce4b_mxfp8_tap* tap = mx_tap.layer >= 0 && capture == cudaStreamCaptureStatusNone ? &mx_tap : nullptr;
+  const size_t rows_pad = static_cast<size_t>(batch + 127) / 128 * 128;
+  auto copy_out = [&](void* dst, const void* src, size_t bytes) {
+    if (dst != nullptr) check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s), "MXFP8 tap copy");
+  };
+  auto tap_n = [&](int layer) { return tap != nullptr && tap->layer == layer ? static_cast<bf16*>(tap->n_bf16_dev) : nullptr; };
+  auto tap_n_codes = [&](int layer) {
+    if (tap == nullptr || tap->layer != layer) return;
+    copy_out(tap->n_codes_dev, workspace + ws_off.n_codes, rows_pad * d);
+    copy_out(tap->n_scales_dev, n_scales, rows_pad / 128 * (d / 128) * 512);
+  };
   expand_input_mx(layout, input, scalars, batch, cfg.history_length, a_codes, a_scales, write_back,
                   s);
   trace("expand_planes_mxfp8", s);
+  if (tap != nullptr) {
+    copy_out(tap->a_codes_dev, a_codes, rows_pad * in_dim);
+    copy_out(tap->a_scales_dev, a_scales, rows_pad / 128 * (in_dim / 128) * 512);
+  }
   const bf16* first_norm = cfg.depth > 0 ? layers[0].norm : w("final_norm.weight");
   gemm_mx_resnorm(tm_a_u8, tm_w_in, tm_x, tm_n_u8, a_scales, w_in_scales, n_scales,
-                  w("input.bias"), first_norm, batch, d, in_dim, eps, s);
+                  w("input.bias"), first_norm, batch, d, in_dim, eps, s, tap_n(0));
   trace("input_gemm_bias_rmsnorm", s);
+  tap_n_codes(0);
   for (int l = 0; l < cfg.depth; ++l) {
     const Layer& L = layers[l];
     const bf16* next_norm = l + 1 < cfg.depth ? layers[l + 1].norm : w("final_norm.weight");
-    gemm_mx_swiglu(tm_n_u8, L.tm_gate_up, tm_h_u8, n_scales, L.gu_scales, h_scales, batch, h, d, s);
+    const bool tap_h = tap != nullptr && tap->layer == l;
+    gemm_mx_swiglu(tm_n_u8, L.tm_gate_up, tm_h_u8, n_scales, L.gu_scales, h_scales, batch, h, d, s,
+                   tap_h ? static_cast<bf16*>(tap->h_bf16_dev) : nullptr);
     trace("gate_up_swiglu", s);
+    if (tap_h) {
+      copy_out(tap->h_codes_dev, workspace + ws_off.h_codes, rows_pad * h);
+      copy_out(tap->h_scales_dev, h_scales, rows_pad / 128 * (h / 128) * 512);
+    }
     gemm_mx_resnorm(tm_h_u8, L.tm_down, tm_x, tm_n_u8, h_scales, L.down_scales, n_scales, nullptr,
-                    next_norm, batch, d, h, eps, s);
+                    next_norm, batch, d, h, eps, s, tap_n(l + 1));
     trace("down_residual_rmsnorm", s);
+    tap_n_codes(l + 1);
   }
   gemm_mx_heads(tm_n_u8, tm_heads, n_scales, heads_scales, w("policy.bias"), policy, wdl,
                 moves_left, batch, d, policy_size, policy_storage, wdl_probs, s);

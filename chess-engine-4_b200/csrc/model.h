@@ -75,6 +75,8 @@ struct Model {
   size_t fwd_sync_bytes = 0;
   unsigned long long* fwd_trace = nullptr;  // optional per-task timeline (device buffer)
   int fwd_trace_cap = 0;
+  // Optional MXFP8 tap (tests): the operands of one layer's quantisation points.
+  ce4b_mxfp8_tap mx_tap{-1, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   // Column width of the persistent forward's input and down tiles for this batch: 256 once
   // a layer's 256-wide down tiles fill two waves of SMs (throughput-bound), else 128
   // (the per-row-block dependency chain bounds the forward; more, narrower tiles help it).

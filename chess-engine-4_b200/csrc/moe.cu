@@ -65,7 +65,10 @@ __global__ void __launch_bounds__(kScanThreads)
     m_tiles[tstart + i] = make_int4(e, start + kBM * i, min(kBM, run - kBM * i), 0);
   }
   if (counts_out != nullptr) counts_out[e] = run;
-  if (e == kExperts - 1) *num_m_tiles = tstart + nt;
+  if (e == kExperts - 1) {
+    *num_m_tiles = tstart + nt;
+    expert_start[kExperts] = start + nt * kBM;
+  }
 }
 
 // kDispatchParts CTAs per router tile (128 tokens = 256 routes), 256 threads (one per

@@ -100,13 +100,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity. Returns false after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait for the phase with the given parity. Returns false after limit_ns.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - start > kWaitLimitNs) return false;
+    if (global_timer_ns() - start > limit_ns) return false;
   }
 }
 
@@ -480,14 +481,15 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// Waits until *ptr >= target (acquire, bounded). Returns false after kWaitLimitNs.
-__device__ __forceinline__ bool wait_counter(const int* ptr, int target) {
+// Waits until *ptr >= target (acquire, bounded). Returns false after limit_ns.
+__device__ __forceinline__ bool wait_counter(const int* ptr, int target,
+                                             unsigned long long limit_ns = kWaitLimitNs) {
   if (ld_acquire_gpu(ptr) >= target) return true;
   const unsigned long long start = global_timer_ns();
   while (true) {
     __nanosleep(64);
     if (ld_acquire_gpu(ptr) >= target) return true;
-    if (global_timer_ns() - start > kWaitLimitNs) return false;
+    if (global_timer_ns() - start > limit_ns) return false;
   }
 }
 

@@ -219,7 +219,44 @@ int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks);
 
 int ce4b_model_trace_label(const ce4b_model* model, int index, char* buffer, int buffer_len);
 
+/* MXFP8 tap (testing hook) of an MXFP8 model: the operands of the quantisation points of
+ * one layer, as the reference's custom MXFP8 path quantises them (the BF16 activations fed
+ * to quantize_mxfp8 before each mxfp8_gemm, src/chess_engine_4/kernels/dense.py:395,
+ * 403-406). With tap->layer = l in [0, depth], each later ce4b_model_forward outside
+ * stream capture writes, for its batch B (rows_pad = B rounded up to 128):
+ *  - a_codes [rows_pad, 64 * planes] and a_scales [rows_pad/128][planes/2][512]: the input
+ *    planes' codes and scales (planes = selected input planes; NULL: not recorded);
+ *  - n_bf16 [B, d]: the normalised rows (BF16) that the epilogue producing layer l's input
+ *    quantised (l = 0: the input GEMM's; l = depth: the heads' input), with n_codes
+ *    [rows_pad, d] and n_scales [rows_pad/128][d/128][512] written for them;
+ *  - for l < depth, h_bf16 [B, h], h_codes [rows_pad, h], h_scales [rows_pad/128][h/128][512]:
+ *    layer l's SwiGLU hidden rows and their codes and scales.
+ * Scales use the ce4b_quantize_mxfp8 layout. Any pointer may be NULL. tap = NULL or
+ * tap->layer < 0 turns the tap off. No counterpart in the reference's API. */
+typedef struct ce4b_mxfp8_tap {
+  int32_t layer;
+  void* a_codes_dev;
+  void* a_scales_dev;
+  void* n_bf16_dev;
+  void* n_codes_dev;
+  void* n_scales_dev;
+  void* h_bf16_dev;
+  void* h_codes_dev;
+  void* h_scales_dev;
+} ce4b_mxfp8_tap;
+int ce4b_model_set_mxfp8_tap(ce4b_model* model, const ce4b_mxfp8_tap* tap);
+
 void ce4b_model_destroy(ce4b_model* model);
+
+/* Self-test of the bounded in-kernel waits (no counterpart in the reference): launches
+ * one single-thread kernel on `stream` that waits, with the given limit (at most 100 ms),
+ * for something that never happens: kind 0, a global counter nobody publishes (the
+ * persistent forward's cross-CTA dependency wait); kind 1, an mbarrier nobody arrives on
+ * (a pipeline-stage wait). The kernel gives up after the limit, records the timeout code
+ * (kind 0: 7, dependency; kind 1: 1, producer) in the device error word that
+ * ce4b_check_device_error reads and clears, and returns. Blocks until the kernel is done;
+ * waited_ns receives the wait the kernel measured. Nothing faults, traps or hangs. */
+int ce4b_selftest_bounded_wait(int kind, long long limit_ns, long long* waited_ns, void* stream);
 
 /* ------------------------------------------------------------------ kernel-op API
  * Replaces the pybind operators of the reference extension (kernels/src/sm100/dense.cu:760-774)
@@ -265,6 +302,32 @@ int ce4b_dense_block_forward(const void* x_dev, const void* norm_weight_dev,
  * runtime's RouteKernel (kernels/src/inference/moe_bf16_impl.cuh:18-68). */
 int ce4b_moe_route(const void* logits_dev, const float* beta_dev, int32_t* experts_dev,
                    float* probs_dev, int32_t* counts_dev, int tokens, void* stream);
+
+/* Routing and dispatch of one moe64a2 layer, with the kernels the model's forward runs
+ * (router GEMM with the top-2 epilogue and per-tile expert histograms, histogram scan,
+ * dispatch). Replaces the eval-path selection and static dispatch of MoeBlock.forward
+ * (src/chess_engine_4/model/moe.py:160-177, 232-267) with its route order _route_slots
+ * (moe.py:36-47), and the runtime's RouteKernel / PrefixOffsetsKernel / DispatchKernel
+ * (kernels/src/inference/moe_bf16_impl.cuh:18-106).
+ * Inputs: n [tokens, d_model] BF16 normalised rows, router_weight [64, d_model] BF16,
+ * beta [64] FP32 (router_qb_beta). Outputs: logits [tokens, 64] BF16 as the selection
+ * used them (may be NULL), experts [tokens, 2] int32 (best first; the lower index wins
+ * ties of logit - beta), probs [tokens, 2] FP32 (BF16-rounded softmax over all 64 logits),
+ * positions [tokens, 2] int32 (row of each route in the permuted layout), expert_offsets
+ * [65] int32 (segment starts, each a multiple of 128, then the total permuted rows),
+ * counts [64] int32 (routes per expert; may be NULL), xperm [capacity, d_model] BF16
+ * (row positions[t][k] = n[t]; padding rows are not written) and pprob [capacity] FP32.
+ * Within an expert, routes are ordered by 2 * token + k. capacity =
+ * ce4b_moe_dispatch_capacity(tokens); workspace holds
+ * ce4b_moe_route_dispatch_workspace_size(tokens) bytes (256-byte aligned). The outputs feed
+ * ce4b_moe_forward (xperm, pprob as BF16, expert_offsets) directly. */
+int ce4b_moe_dispatch_capacity(int tokens);
+int64_t ce4b_moe_route_dispatch_workspace_size(int tokens);
+int ce4b_moe_route_dispatch(const void* n_dev, const void* router_weight_dev, const float* beta_dev,
+                            void* logits_dev, int32_t* experts_dev, float* probs_dev,
+                            int32_t* positions_dev, int32_t* expert_offsets_dev,
+                            int32_t* counts_dev, void* xperm_dev, float* pprob_dev,
+                            void* workspace_dev, int tokens, int d_model, void* stream);
 
 /* Scratch bytes ce4b_moe_forward needs. */
 int64_t ce4b_moe_workspace_size(int rows, int d_model, int hidden_dim);

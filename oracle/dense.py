@@ -126,6 +126,49 @@ def forward(
     return policy, wdl, moves_left
 
 
+class PortableForward:
+    """``PortableChessNet`` (src/chess_engine_4/model/reference.py:60-101) restated as a
+    function of Safetensors-named weights that are cast to ``dtype`` once, as the module is
+    when it is moved to that dtype; ``forward`` then runs the module's own operations in
+    that dtype: history select and rule-50 / 99 (dense.py:34-51), ``Linear`` with bias,
+    per block ``x + down(silu(gate) * up)`` over ``RMSNorm(x)`` (reference.py:17-43), final
+    ``RMSNorm`` and the three heads (1858 / 3 / 1 columns of the stored 1888 / 32 / 32).
+    With ``dtype=torch.float32`` this is ``forward(mode="fp32")``; with ``torch.bfloat16`` it
+    is the reference module run in BF16 on the CPU (the CPU baseline's BF16 arm), pinned to
+    the reference's own BF16 output in tests/golden/."""
+
+    def __init__(self, weights: dict[str, torch.Tensor], *, depth: int, history_length: int = 8,
+                 eps: float = 1e-6, dtype: torch.dtype = torch.float32) -> None:
+        self.depth, self.history_length, self.eps, self.dtype = depth, history_length, eps, dtype
+        c = {k: v.detach().to(dtype).contiguous() for k, v in weights.items()}
+        self.w = c
+        self.heads = {
+            "policy": (c["policy.weight"][:POLICY_SIZE].contiguous(), c["policy.bias"][:POLICY_SIZE].contiguous()),
+            "wdl": (c["wdl.weight"][:3].contiguous(), c["wdl.bias"][:3].contiguous()),
+            "moves_left": (c["moves_left.weight"][:1].contiguous(), c["moves_left.bias"][:1].contiguous()),
+        }
+
+    def __call__(self, planes: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        from torch.nn import functional as F
+
+        w, d = self.w, self.w["input.weight"].shape[0]
+        x = planes.to(self.dtype)
+        hp = self.history_length * PLANES_PER_HISTORY
+        x = torch.cat((x[:, :hp], x[:, HISTORY_PLANES:]), dim=1) if hp != HISTORY_PLANES else x.clone()
+        x[:, hp + 5] = x[:, hp + 5] / 99.0
+        x = F.linear(x.flatten(start_dim=1), w["input.weight"], w["input.bias"])
+        for layer in range(self.depth):
+            p = f"blocks.{layer}"
+            n = F.rms_norm(x, (d,), w[f"{p}.norm.weight"], self.eps)
+            gate, up = F.linear(n, w[f"{p}.gate_up.weight"]).chunk(2, dim=-1)
+            x = x + F.linear(F.silu(gate) * up, w[f"{p}.down.weight"])
+        x = F.rms_norm(x, (d,), w["final_norm.weight"], self.eps)
+        policy = F.linear(x, *self.heads["policy"])
+        wdl = F.linear(x, *self.heads["wdl"])
+        moves_left = F.linear(x, *self.heads["moves_left"]).squeeze(-1)
+        return policy, wdl, moves_left
+
+
 def wdl_probabilities(wdl_logits: torch.Tensor) -> torch.Tensor:
     """FP32 softmax of the three logits (kernels/src/inference/runtime.cu:309-328)."""
 

@@ -78,3 +78,16 @@ def test_safetensors_loader_reports_missing_file() -> None:
     status = _lib.library().ce4b_model_load_safetensors(b"/nonexistent/model.safetensors", 0, 8, 0, ctypes.byref(handle))
     assert status == _lib.CE4B_ERR_IO
     assert "cannot open" in _lib.last_error()
+
+
+def test_bounded_wait_selftest_checks_arguments_on_the_host() -> None:
+    import ctypes
+
+    from ce4b200 import _lib
+
+    waited = ctypes.c_int64(0)
+    lib = _lib.library()
+    assert lib.ce4b_selftest_bounded_wait(2, 1000, ctypes.byref(waited), None) == _lib.CE4B_ERR_INVALID_ARGUMENT
+    assert "kind" in _lib.last_error()
+    assert lib.ce4b_selftest_bounded_wait(0, 10**9, ctypes.byref(waited), None) == _lib.CE4B_ERR_INVALID_ARGUMENT
+    assert "limit" in _lib.last_error()

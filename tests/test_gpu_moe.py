@@ -90,3 +90,81 @@ def test_moe_model_matches_oracle(d: int, depth: int, ratio: float, batch: int) 
     assert argmax_agreement(out.policy_logits, policy) >= 0.99
     wdl_err = (torch.softmax(out.wdl_logits.cpu(), -1) - torch.softmax(wdl, -1)).abs().max(dim=1).values
     assert float((wdl_err <= WDL_PROB_ATOL).float().mean()) >= 0.99
+
+
+@pytest.mark.parametrize("tokens,d", [(300, 128), (8192, 768)])
+def test_dispatch_places_routes_like_route_slots(tokens: int, d: int) -> None:
+    """The forward's routing kernels (router GEMM with the top-2 epilogue, scan, dispatch)
+    against the reference's selection and ``_route_slots`` placement, given the BF16
+    logits the GPU's selection used: expert indices, weights, each route's row in the
+    128-row-padded permuted layout, segment offsets and the copied rows, bit for bit."""
+    from ce4b200 import kernels, synthetic
+    from oracle import moe as oracle_moe
+
+    g = torch.Generator().manual_seed(tokens + d)
+    n = torch.randn(tokens, d, generator=g).bfloat16()
+    w_r = (0.02 * torch.randn(64, d, generator=g)).bfloat16()
+    beta = synthetic.zipf_router_bias(11)  # skewed load: several experts span many tiles
+    got = kernels.moe_route_dispatch(n.cuda(), w_r.cuda(), beta.cuda())
+    torch.cuda.synchronize()
+    logits = got.logits.cpu().float()
+    # The logits are the GEMM's own BF16 outputs: they match a CPU product to BF16 rounding.
+    torch.testing.assert_close(logits, (n.float() @ w_r.float().T).bfloat16().float(), atol=2e-2, rtol=1e-2)
+    ref_e, ref_p = oracle_moe.route_top2(logits, beta)
+    assert torch.equal(got.experts.cpu().long(), ref_e)
+    # Weights: a softmax over 64 logits (device expf vs the CPU's) rounded to BF16 agree to
+    # one BF16 step; the indices and positions below are exact.
+    torch.testing.assert_close(got.probs.cpu(), ref_p.bfloat16().float(), atol=0, rtol=2**-8)
+    flat = ref_e.reshape(-1)  # route r = 2 * token + k
+    counts = torch.bincount(flat, minlength=64)
+    padded = (counts + 127) // 128 * 128
+    starts = torch.cumsum(padded, 0) - padded
+    expected_pos = starts[flat] + oracle_moe.route_slots(flat)
+    assert torch.equal(got.counts.cpu().long(), counts)
+    assert torch.equal(got.expert_offsets.cpu().long(), torch.cat([starts, padded.sum().reshape(1)]))
+    assert torch.equal(got.positions.cpu().reshape(-1).long(), expected_pos)
+    rows = got.rows.cpu()
+    assert torch.equal(rows[expected_pos], n.repeat_interleave(2, dim=0))
+    assert torch.equal(got.row_probs.cpu()[expected_pos], got.probs.cpu().reshape(-1))
+
+
+def test_moe_model_matches_oracle_at_c3() -> None:
+    """moe64a2 at the c3 configuration: d768, 12 layers (6 MoE with 64 experts of hidden
+    768, 6 dense with hidden 3072), Zipf-skewed router_qb_beta, against the CPU oracle on
+    2048 positions. Routing follows BF16 logits that the GPU and the CPU accumulate in
+    different orders, so a token whose 2nd and 3rd expert scores lie within one BF16 step
+    can take the other expert (the dispatch itself is pinned bit for bit by
+    test_dispatch_places_routes_like_route_slots)."""
+    from ce4b200 import Moe64A2ChessNet, Moe64A2ChessNetConfig, synthetic
+    from helpers import POLICY_ATOL, WDL_PROB_ATOL, argmax_agreement
+    from oracle import moe as oracle_moe
+
+    d, depth, ratio, batch = 768, 12, 1.0, 2048
+    weights = synthetic.make_moe_weights(d_model=d, depth=depth, expert_hidden=int(d * ratio), seed=8)
+    planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(batch, 12))
+    model = Moe64A2ChessNet(
+        Moe64A2ChessNetConfig(d_model=d, depth=depth, expansion_ratio=ratio, precision="bf16")
+    )
+    synthetic.load_into(model, weights)
+    model = model.cuda()
+    out = model(planes.clone().cuda())
+    torch.cuda.synchronize()
+    policy, wdl, ml, counts = oracle_moe.forward(weights, planes, depth=depth, mode="bf16")
+    got = out.router_tokens_per_expert.cpu()
+    assert got.shape == (depth // 2, 64)
+    assert torch.all(got.sum(dim=1) == 2 * batch)
+    moved = int((got - counts).abs().sum()) // 2
+    err = (out.policy_logits.cpu() - policy).abs().max(dim=1).values
+    within = float((err <= POLICY_ATOL).float().mean())
+    raw = argmax_agreement(out.policy_logits, policy, tol=0.0)
+    tol_aware = argmax_agreement(out.policy_logits, policy)
+    wdl_err = (torch.softmax(out.wdl_logits.cpu(), -1) - torch.softmax(wdl, -1)).abs().max(dim=1).values
+    print(f"c3 B={batch}: routes moved {moved} of {2 * batch * depth // 2}, policy rows within "
+          f"{POLICY_ATOL}: {within:.4f} (max {float(err.max()):.4f}), argmax raw {raw:.4f}, "
+          f"tolerance-aware {tol_aware:.4f}, wdl rows within {WDL_PROB_ATOL}: "
+          f"{float((wdl_err <= WDL_PROB_ATOL).float().mean()):.4f}")
+    assert moved <= 0.01 * 2 * batch * (depth // 2)
+    assert int(out.router_dead_experts) == int(counts.eq(0).sum(dim=1).max())
+    assert within >= 0.99
+    assert tol_aware >= 0.99
+    assert float((wdl_err <= WDL_PROB_ATOL).float().mean()) >= 0.99

@@ -101,3 +101,97 @@ def test_mxfp8_weight_stationary_swiglu_matches_streaming() -> None:
     assert torch.equal(wide.policy_logits[:1024], narrow.policy_logits)
     assert torch.equal(wide.wdl_logits[:1024], narrow.wdl_logits)
     assert torch.equal(wide.moves_left[:1024], narrow.moves_left)
+
+
+def _c2_model(batch: int, seed: int = 3):
+    from ce4b200 import DenseChessNet, DenseChessNetConfig, synthetic
+
+    d, depth, ratio = 512, 12, 3.0
+    weights = synthetic.make_dense_weights(d_model=d, depth=depth, hidden_dim=int(d * ratio), seed=seed)
+    model = DenseChessNet(DenseChessNetConfig(d_model=d, depth=depth, expansion_ratio=ratio, precision="mxfp8"))
+    synthetic.load_into(model, weights)
+    return weights, model.cuda()
+
+
+def test_mxfp8_epilogue_codes_bit_exact_at_c2() -> None:
+    """Teacher-forced MXFP8 parity at the c2 configuration (d512 x 12, B = 16384): at each
+    tapped layer, the E4M3 codes and E8M0 scales that the quantising epilogues wrote (the
+    normalised rows feeding the layer, its SwiGLU hidden rows) and the input planes' codes
+    must equal the reference recipe's quantisation (oracle/mxfp8.c) of the very BF16 values
+    the epilogue saw, bit for bit."""
+    import ctypes
+
+    from ce4b200 import _lib, synthetic
+    from oracle import dense as oracle
+    from oracle import mxfp8
+
+    batch, d, h, depth = 16384, 512, 1536, 12
+    _, model = _c2_model(batch)
+    planes_cpu = synthetic.lc0_to_dense(synthetic.make_lc0_planes(batch, 9))
+    planes = planes_cpu.cuda()
+    engine = model._engine(batch, planes.device)
+    in_dim = 7168
+    for layer in (0, 5, 11, depth):
+        bufs = {
+            "n_bf16_dev": torch.empty(batch, d, dtype=torch.bfloat16, device="cuda"),
+            "n_codes_dev": torch.empty(batch, d, dtype=torch.uint8, device="cuda"),
+            "n_scales_dev": torch.empty(batch // 128, d // 128, 512, dtype=torch.uint8, device="cuda"),
+        }
+        if layer < depth:
+            bufs |= {
+                "h_bf16_dev": torch.empty(batch, h, dtype=torch.bfloat16, device="cuda"),
+                "h_codes_dev": torch.empty(batch, h, dtype=torch.uint8, device="cuda"),
+                "h_scales_dev": torch.empty(batch // 128, h // 128, 512, dtype=torch.uint8, device="cuda"),
+            }
+        if layer == 0:
+            bufs |= {
+                "a_codes_dev": torch.empty(batch, in_dim, dtype=torch.uint8, device="cuda"),
+                "a_scales_dev": torch.empty(batch // 128, in_dim // 128, 512, dtype=torch.uint8, device="cuda"),
+            }
+        tap = _lib.Mxfp8TapStruct(layer=layer, **{k: v.data_ptr() for k, v in bufs.items()})
+        _lib.check(engine.lib.ce4b_model_set_mxfp8_tap(engine.handle, ctypes.byref(tap)))
+        try:
+            model(planes.clone())
+            torch.cuda.synchronize()
+        finally:
+            _lib.check(engine.lib.ce4b_model_set_mxfp8_tap(engine.handle, None))
+        for part in ("n", "h") if layer < depth else ("n",):
+            values = bufs[f"{part}_bf16_dev"].cpu()
+            codes, scales = mxfp8.quantize(values)
+            assert torch.equal(bufs[f"{part}_codes_dev"].cpu(), codes), (layer, part)
+            assert torch.equal(bufs[f"{part}_scales_dev"].cpu().reshape(scales.shape), scales), (layer, part)
+        if layer == 0:
+            a = oracle.select_and_normalize(planes_cpu, 8).bfloat16()
+            codes, scales = mxfp8.quantize(a)
+            assert torch.equal(bufs["a_codes_dev"].cpu(), codes)
+            assert torch.equal(bufs["a_scales_dev"].cpu().reshape(scales.shape), scales)
+
+
+def test_mxfp8_model_matches_oracle_at_c2_batch() -> None:
+    """The MXFP8 forward at c2's batch (16384 positions, the weight-stationary SwiGLU path
+    and multi-wave schedules) against the reference-recipe MXFP8 oracle on a strided sample
+    of 1024 positions (positions are independent, so a sample checks the full-batch run)."""
+    from ce4b200 import synthetic
+    from helpers import POLICY_ATOL, WDL_PROB_ATOL, argmax_agreement
+    from oracle import dense as oracle
+
+    batch = 16384
+    weights, model = _c2_model(batch, seed=4)
+    planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(batch, 10))
+    out = model(planes.clone().cuda())
+    torch.cuda.synchronize()
+    sample = torch.arange(0, batch, 16)
+    policy, wdl, _ = oracle.forward(weights, planes[sample], depth=12, mode="mxfp8")
+    policy_bf16 = oracle.forward(weights, planes[sample], depth=12, mode="bf16")[0]
+    got = out.policy_logits.cpu()[sample]
+    err = (got - policy).abs().max(dim=1).values
+    fmt = (policy - policy_bf16).abs().max(dim=1).values
+    raw = argmax_agreement(got, policy, tol=0.0)
+    tol_aware = argmax_agreement(got, policy)
+    print(f"c2 MXFP8 B={batch}: rows within {POLICY_ATOL}: {float((err <= POLICY_ATOL).float().mean()):.4f}, "
+          f"max {float(err.max()):.4f}, argmax raw {raw:.4f}, tolerance-aware {tol_aware:.4f}")
+    assert float((err <= POLICY_ATOL).float().mean()) >= 0.97, float(err.max())
+    assert float(err.max()) <= float(fmt.quantile(0.99)) + POLICY_ATOL
+    assert tol_aware >= 0.995
+    wdl_err = (torch.softmax(out.wdl_logits.cpu()[sample], -1) - torch.softmax(wdl, -1)).abs().max(dim=1).values
+    assert float((wdl_err <= WDL_PROB_ATOL).float().mean()) >= 0.97

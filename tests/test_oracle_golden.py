@@ -6,6 +6,8 @@ inputs. The weights are regenerated here from the recorded seeds (checked by SHA
 
 from __future__ import annotations
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -93,3 +95,51 @@ def test_route_slots_known_answer_and_routing_fixture() -> None:
     scores = logits - beta
     order = torch.sort(scores, dim=1, descending=True, stable=True).indices[:, :2]
     np.testing.assert_array_equal(order.numpy(), data["indices"])
+
+
+def test_portable_forward_reproduces_reference_module_in_fp32_and_bf16() -> None:
+    """oracle.dense.PortableForward (the CPU baseline's implementation) reproduces the
+    reference's PortableChessNet bit for bit: in FP32, and moved to BF16."""
+    from ce4b200 import synthetic
+    from oracle import dense as oracle
+
+    for name, dtype in (("dense_d128_l6_r3", torch.float32), ("dense_d128_l6_r3_bf16module", torch.bfloat16)):
+        meta, data = load_golden(name)
+        weights = synthetic.make_dense_weights(
+            d_model=meta["d_model"], depth=meta["depth"],
+            hidden_dim=int(meta["d_model"] * meta["expansion_ratio"]), seed=meta["weight_seed"],
+        )
+        planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(meta["batch"], meta["plane_seed"])).to(dtype)
+        with torch.no_grad():
+            policy, wdl, ml = oracle.PortableForward(weights, depth=meta["depth"], dtype=dtype)(planes)
+        assert torch.equal(policy.float(), torch.from_numpy(data["policy"])), name
+        assert torch.equal(wdl.float(), torch.from_numpy(data["wdl"])), name
+        assert torch.equal(ml.float(), torch.from_numpy(data["moves_left"])), name
+
+
+def test_mxfp8_oracle_matches_reference_quantizer() -> None:
+    """oracle/mxfp8.c against codes and scales that the reference's own torch quantiser
+    produced (tests/golden/make_golden.py runs torch_mxfp8_quantize and scale_swizzle from
+    the reference's test_quantize.py). Every E4M3 code and every scale of a non-zero block
+    is identical. An all-zero block is the one documented difference: the reference's
+    kernel clamps the scale at 1e-12 (E8M0 code 88), which oracle/mxfp8.c and the GPU
+    quantiser follow, while the torch restatement clamps the exponent at -127 (code 0)."""
+    import hashlib
+    import sys
+
+    from oracle import mxfp8
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    from make_golden import mxfp8_sample
+
+    meta, data = load_golden("mxfp8_reference_quantizer")
+    x = mxfp8_sample()
+    assert hashlib.sha256(x.view(torch.int16).numpy().tobytes()).hexdigest() == meta["input_sha256"]
+    codes, scales = mxfp8.quantize(x)
+    assert torch.equal(codes, torch.from_numpy(data["codes"]))
+    ours = mxfp8.unswizzle_scales(scales)
+    ref = mxfp8.unswizzle_scales(torch.from_numpy(data["scales"]))
+    zero_block = x.float().abs().view(x.shape[0], -1, 32).amax(-1) == 0
+    assert int(zero_block.sum()) == 1
+    assert torch.equal(ours[~zero_block], ref[~zero_block])
+    assert torch.all(ours[zero_block] == 88) and torch.all(ref[zero_block] == 0)
