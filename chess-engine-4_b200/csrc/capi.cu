@@ -276,6 +276,21 @@ int ce4b_model_set_task_trace(ce4b_model* model, void* device_buffer, int capaci
   });
 }
 
+int ce4b_model_set_routing_tap(ce4b_model* model, int32_t* experts_dev, int capacity_tokens) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    ce4b::Model& m = *model->impl;
+    if (experts_dev == nullptr || capacity_tokens <= 0) {
+      m.moe_tap = nullptr;
+      m.moe_tap_tokens = 0;
+      return;
+    }
+    if (m.cfg.arch != CE4B_ARCH_MOE64A2) fail(CE4B_ERR_UNSUPPORTED, "the routing tap needs a moe64a2 model");
+    m.moe_tap = experts_dev;
+    m.moe_tap_tokens = capacity_tokens;
+  });
+}
+
 int ce4b_model_set_mxfp8_tap(ce4b_model* model, const ce4b_mxfp8_tap* tap) {
   return guarded([&] {
     require(model != nullptr && model->impl, "null model");

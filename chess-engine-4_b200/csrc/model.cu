@@ -575,6 +575,15 @@ void Model::moe_layer(const Layer& L, int moe_index, const bf16* next_norm, int 
   auto* n = reinterpret_cast<bf16*>(at(ws_off.n));
   moe_router_gemm(tm_n, L.tm_router, L.beta, route_expert, route_prob, block_hist, batch, d, s);
   trace("moe_router", s);
+  if (moe_tap != nullptr && batch <= moe_tap_tokens) {
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    check_cuda(cudaStreamIsCapturing(s, &capture), "query stream capture");
+    if (capture == cudaStreamCaptureStatusNone) {
+      check_cuda(cudaMemcpyAsync(moe_tap + static_cast<size_t>(moe_index) * batch * 2, route_expert,
+                                 static_cast<size_t>(batch) * 8, cudaMemcpyDeviceToDevice, s),
+                 "routing tap copy");
+    }
+  }
   moe_scan(block_hist, (batch + 127) / 128, expert_start, block_off, m_tiles, num_m_tiles,
            tokens_per_expert != nullptr ? tokens_per_expert + 64 * moe_index : nullptr, s);
   trace("moe_scan", s);

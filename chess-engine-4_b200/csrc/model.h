@@ -75,6 +75,10 @@ struct Model {
   size_t fwd_sync_bytes = 0;
   unsigned long long* fwd_trace = nullptr;  // optional per-task timeline (device buffer)
   int fwd_trace_cap = 0;
+  // Optional routing tap (tests): each MoE layer's expert pair per token,
+  // [depth/2][batch][2] int32, written by forwards outside stream capture.
+  int32_t* moe_tap = nullptr;
+  int moe_tap_tokens = 0;
   // Optional MXFP8 tap (tests): the operands of one layer's quantisation points.
   ce4b_mxfp8_tap mx_tap{-1, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   // Column width of the persistent forward's input and down tiles for this batch: 256 once

@@ -219,6 +219,13 @@ int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks);
 
 int ce4b_model_trace_label(const ce4b_model* model, int index, char* buffer, int buffer_len);
 
+/* Routing tap (testing hook) of a moe64a2 model: with experts_dev set, each later
+ * single-GPU ce4b_model_forward outside stream capture whose batch B <= capacity_tokens
+ * writes every MoE layer's expert pair per token, [depth/2][B][2] int32 (best first), as
+ * MoeBlock.forward selects them (src/chess_engine_4/model/moe.py:160-177). NULL turns the
+ * tap off. No counterpart in the reference's API. */
+int ce4b_model_set_routing_tap(ce4b_model* model, int32_t* experts_dev, int capacity_tokens);
+
 /* MXFP8 tap (testing hook) of an MXFP8 model: the operands of the quantisation points of
  * one layer, as the reference's custom MXFP8 path quantises them (the BF16 activations fed
  * to quantize_mxfp8 before each mxfp8_gemm, src/chess_engine_4/kernels/dense.py:395,

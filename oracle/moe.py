@@ -69,15 +69,27 @@ def moe_block(
     *,
     eps: float = 1e-6,
     mode: str = "bf16",
+    forced_experts: torch.Tensor | None = None,
+    record: list | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """One MoE block. Returns (x_out [T,d], experts [T,2], tokens_per_expert [64])."""
+    """One MoE block. Returns (x_out [T,d], experts [T,2], tokens_per_expert [64]).
+
+    ``forced_experts`` [T,2] replaces the top-2 choice (a teacher-forced check: the weights
+    are still the softmax of this block's own logits at those experts). ``record``, if
+    given, receives (own top-2 choice, scores = logits - beta) of this block."""
 
     rnd = _bf16 if mode == "bf16" else (lambda t: t)
     p = f"blocks.{layer}"
     f = {k: v.to(torch.float32) for k, v in weights.items() if k.startswith(p + ".")}
     n = rnd(dense._rmsnorm(x, f[f"{p}.norm.weight"], eps))
     logits = _bf16(n @ f[f"{p}.router.weight"].T)
-    experts, probs = route_top2(logits, weights[f"{p}.router_qb_beta"])
+    beta = weights[f"{p}.router_qb_beta"]
+    experts, probs = route_top2(logits, beta)
+    if record is not None:
+        record.append((experts, logits - beta.to(torch.float32)))
+    if forced_experts is not None:
+        experts = forced_experts.to(torch.int64)
+        probs = torch.softmax(logits, dim=-1).gather(1, experts)
     probs = rnd(probs)
     gate_up = f[f"{p}.experts.gate_up.weight"]
     down = f[f"{p}.experts.down.weight"]
@@ -106,15 +118,20 @@ def forward(
     history_length: int = 8,
     eps: float = 1e-6,
     mode: str = "bf16",
+    forced_experts: torch.Tensor | None = None,
+    record: list | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """moe64a2 tower: even layers MoE, odd layers dense (moe.py:354-366).
 
+    ``forced_experts`` [depth/2, B, 2] teacher-forces every MoE layer's expert choice;
+    ``record`` collects each MoE layer's own (top-2 choice, scores) (see moe_block).
     Returns (policy [B,1858], wdl [B,3], moves_left [B], tokens_per_expert [depth/2, 64])."""
 
     counts: list[torch.Tensor] = []
 
     def moe_forward(x: torch.Tensor, layer: int, m: str) -> torch.Tensor:
-        out, _, c = moe_block(x, weights, layer, eps=eps, mode=m)
+        forced = forced_experts[layer // 2] if forced_experts is not None else None
+        out, _, c = moe_block(x, weights, layer, eps=eps, mode=m, forced_experts=forced, record=record)
         counts.append(c)
         return out
 

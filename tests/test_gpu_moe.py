@@ -113,8 +113,9 @@ def test_dispatch_places_routes_like_route_slots(tokens: int, d: int) -> None:
     ref_e, ref_p = oracle_moe.route_top2(logits, beta)
     assert torch.equal(got.experts.cpu().long(), ref_e)
     # Weights: a softmax over 64 logits (device expf vs the CPU's) rounded to BF16 agree to
-    # one BF16 step; the indices and positions below are exact.
-    torch.testing.assert_close(got.probs.cpu(), ref_p.bfloat16().float(), atol=0, rtol=2**-8)
+    # one BF16 step (a relative 2^-8 .. 2^-7 depending on the place in the binade); the
+    # indices and positions below are exact.
+    torch.testing.assert_close(got.probs.cpu(), ref_p.bfloat16().float(), atol=0, rtol=2**-7)
     flat = ref_e.reshape(-1)  # route r = 2 * token + k
     counts = torch.bincount(flat, minlength=64)
     padded = (counts + 127) // 128 * 128
@@ -128,15 +129,27 @@ def test_dispatch_places_routes_like_route_slots(tokens: int, d: int) -> None:
     assert torch.equal(got.row_probs.cpu()[expected_pos], got.probs.cpu().reshape(-1))
 
 
+def _bf16_ulp(v: torch.Tensor) -> torch.Tensor:
+    """Spacing of BF16 values at |v| (8 significant bits)."""
+    return torch.exp2(torch.floor(torch.log2(v.abs().clamp_min(2.0**-126))) - 7)
+
+
 def test_moe_model_matches_oracle_at_c3() -> None:
     """moe64a2 at the c3 configuration: d768, 12 layers (6 MoE with 64 experts of hidden
-    768, 6 dense with hidden 3072), Zipf-skewed router_qb_beta, against the CPU oracle on
-    2048 positions. Routing follows BF16 logits that the GPU and the CPU accumulate in
-    different orders, so a token whose 2nd and 3rd expert scores lie within one BF16 step
-    can take the other expert (the dispatch itself is pinned bit for bit by
-    test_dispatch_places_routes_like_route_slots)."""
-    from ce4b200 import Moe64A2ChessNet, Moe64A2ChessNetConfig, synthetic
-    from helpers import POLICY_ATOL, WDL_PROB_ATOL, argmax_agreement
+    768, 6 dense with hidden 3072), Zipf-skewed router_qb_beta, 2048 positions.
+
+    Routing decides on BF16 logits that the GPU and the CPU accumulate in different
+    orders, so a token whose 2nd and 3rd expert scores lie within a BF16 step can take the
+    other expert, after which its row legitimately differs. The test therefore
+    (1) reads the GPU's expert choice of every token and MoE layer (routing tap), runs the
+    oracle teacher-forced on those choices and requires the BF16 bars on the outputs;
+    (2) requires every choice where the oracle would have picked differently to be a near
+    tie: the score gap at most a few BF16 steps of the two logits; and
+    (3) reports the free-running comparison (the oracle routing on its own) beside it."""
+    import ctypes
+
+    from ce4b200 import Moe64A2ChessNet, Moe64A2ChessNetConfig, _lib, synthetic
+    from helpers import POLICY_ATOL, POLICY_RTOL, WDL_PROB_ATOL, argmax_agreement
     from oracle import moe as oracle_moe
 
     d, depth, ratio, batch = 768, 12, 1.0, 2048
@@ -147,24 +160,56 @@ def test_moe_model_matches_oracle_at_c3() -> None:
     )
     synthetic.load_into(model, weights)
     model = model.cuda()
-    out = model(planes.clone().cuda())
-    torch.cuda.synchronize()
-    policy, wdl, ml, counts = oracle_moe.forward(weights, planes, depth=depth, mode="bf16")
-    got = out.router_tokens_per_expert.cpu()
-    assert got.shape == (depth // 2, 64)
-    assert torch.all(got.sum(dim=1) == 2 * batch)
-    moved = int((got - counts).abs().sum()) // 2
-    err = (out.policy_logits.cpu() - policy).abs().max(dim=1).values
-    within = float((err <= POLICY_ATOL).float().mean())
+    gpu_planes = planes.clone().cuda()
+    engine = model._engine(batch, gpu_planes.device)
+    taps = torch.full((depth // 2, batch, 2), -1, dtype=torch.int32, device="cuda")
+    _lib.check(engine.lib.ce4b_model_set_routing_tap(engine.handle, ctypes.c_void_p(taps.data_ptr()), batch))
+    try:
+        out = model(gpu_planes)
+        torch.cuda.synchronize()
+    finally:
+        _lib.check(engine.lib.ce4b_model_set_routing_tap(engine.handle, None, 0))
+    gpu_experts = taps.cpu().long()
+    assert int(gpu_experts.min()) >= 0 and int(gpu_experts.max()) < 64
+    got_counts = out.router_tokens_per_expert.cpu()
+    for layer in range(depth // 2):
+        assert torch.equal(got_counts[layer], torch.bincount(gpu_experts[layer].reshape(-1), minlength=64))
+
+    record: list = []
+    policy, wdl, ml, counts = oracle_moe.forward(
+        weights, planes, depth=depth, mode="bf16", forced_experts=gpu_experts, record=record
+    )
+    # (2) Every routing difference is a near tie of the oracle's own scores.
+    worst = 0.0
+    differ = 0
+    for layer, (own, scores) in enumerate(record):
+        forced = gpu_experts[layer]
+        for k in range(2):
+            bad = own[:, k] != forced[:, k]
+            differ += int(bad.sum())
+            if bad.any():
+                s_own = scores[bad].gather(1, own[bad][:, k : k + 1])[:, 0]
+                s_gpu = scores[bad].gather(1, forced[bad][:, k : k + 1])[:, 0]
+                gap = (s_own - s_gpu) / (_bf16_ulp(s_own) + _bf16_ulp(s_gpu))
+                worst = max(worst, float(gap.max()))
+    # (1) Teacher-forced outputs against the BF16 bars.
+    err = (out.policy_logits.cpu() - policy).abs()
+    row_ok = (err <= POLICY_ATOL + POLICY_RTOL * policy.abs()).all(dim=1)
     raw = argmax_agreement(out.policy_logits, policy, tol=0.0)
     tol_aware = argmax_agreement(out.policy_logits, policy)
     wdl_err = (torch.softmax(out.wdl_logits.cpu(), -1) - torch.softmax(wdl, -1)).abs().max(dim=1).values
-    print(f"c3 B={batch}: routes moved {moved} of {2 * batch * depth // 2}, policy rows within "
-          f"{POLICY_ATOL}: {within:.4f} (max {float(err.max()):.4f}), argmax raw {raw:.4f}, "
-          f"tolerance-aware {tol_aware:.4f}, wdl rows within {WDL_PROB_ATOL}: "
-          f"{float((wdl_err <= WDL_PROB_ATOL).float().mean()):.4f}")
-    assert moved <= 0.01 * 2 * batch * (depth // 2)
-    assert int(out.router_dead_experts) == int(counts.eq(0).sum(dim=1).max())
-    assert within >= 0.99
-    assert tol_aware >= 0.99
-    assert float((wdl_err <= WDL_PROB_ATOL).float().mean()) >= 0.99
+    # (3) Free-running oracle for scale.
+    free = oracle_moe.forward(weights, planes, depth=depth, mode="bf16")
+    free_rows = float(((out.policy_logits.cpu() - free[0]).abs() <= POLICY_ATOL + POLICY_RTOL * free[0].abs())
+                      .all(dim=1).float().mean())
+    print(f"c3 B={batch}: teacher-forced policy rows within the bar {float(row_ok.float().mean()):.4f} "
+          f"(max {float(err.max()):.4f}), argmax raw {raw:.4f}, tolerance-aware {tol_aware:.4f}, wdl max "
+          f"{float(wdl_err.max()):.4f}; routes the oracle would pick differently {differ} of "
+          f"{2 * batch * depth // 2}, largest score gap {worst:.2f} BF16 steps; free-running rows within "
+          f"the bar {free_rows:.4f}")
+    assert worst <= 4.0
+    assert differ <= 0.01 * 2 * batch * (depth // 2)
+    assert float(row_ok.float().mean()) >= 0.995
+    assert tol_aware >= 0.995
+    assert float((wdl_err <= WDL_PROB_ATOL).float().mean()) >= 0.995
+    assert int(out.router_dead_experts) == int(got_counts.eq(0).sum(dim=1).max())
