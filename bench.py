@@ -61,6 +61,7 @@ class Config:
     precision: str  # "bf16" | "mxfp8"
     cpu_sample: int  # positions per CPU-baseline sample
     strong: bool = False  # the config's batch is split data-parallel over the GPUs
+    published: float | None = None  # the reference's own published number for this metric
 
     def per_gpu(self, world: int) -> int:
         if not self.strong:
@@ -118,6 +119,12 @@ CONFIGS = {
     "c3": Config("c3", "moe64a2", 768, 12, 1.0, 8192, "bf16", 128),
     "c4": Config("c4", "dense", 1024, 16, 3.0, 65536, "bf16", 256, strong=True),
     "c4-mxfp8": Config("c4-mxfp8", "dense", 1024, 16, 3.0, 65536, "mxfp8", 256, strong=True),
+    # The reference's one published B200 forward measurement: Transformer Engine MXFP8,
+    # dense d2048 x 8, SwiGLU ratio 4, batch 4096, 1,538,739 and (rerun) 1,758,459
+    # positions/s (experiments/2026-08-11.03-nvfp4-inference-crossover/README.md:49-52);
+    # vs_baseline divides by the faster rerun.
+    "d2048-mxfp8": Config("d2048-mxfp8", "dense", 2048, 8, 4.0, 4096, "mxfp8", 256, published=1758459.0),
+    "d2048": Config("d2048", "dense", 2048, 8, 4.0, 4096, "bf16", 256),
 }
 
 
@@ -295,7 +302,10 @@ class CpuForward:
 def cpu_sample_size(cfg: Config) -> int:
     """Positions per CPU step: the whole batch up to 4096 (c0, c1), a bounded sample beyond."""
 
-    return min(cfg.batch, 4096) if cfg.arch == "dense" else cfg.cpu_sample
+    if cfg.arch != "dense":
+        return cfg.cpu_sample
+    # At most ~300 GFLOP of CPU work per step (c0, c1: the whole batch).
+    return max(1, min(cfg.batch, 4096, int(300e9 / cfg.flop_per_pos())))
 
 
 def cpu_rate(cfg: Config, dtype: torch.dtype, sample: int, steps: int, warmup: int) -> tuple[float, int]:
@@ -636,7 +646,7 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
             "ms_per_step": total_ms / args.steps,
             "higher_is_better": True,
             "scaling": "strong" if cfg.strong else "weak",
-            "vs_baseline": None,
+            "vs_baseline": value / cfg.published if cfg.published else None,
             "dtype": "e4m3/e8m0 (mxfp8), bf16 residual" if cfg.precision == "mxfp8" else "bf16",
             "data": "synthetic",
             "config": {
@@ -687,7 +697,7 @@ def main() -> None:
     cfg = CONFIGS[args.config]
     if args.batch:
         cfg = Config(cfg.name, cfg.arch, cfg.d, cfg.depth, cfg.ratio, args.batch, cfg.precision, cfg.cpu_sample,
-                     cfg.strong)
+                     cfg.strong, cfg.published if args.batch == cfg.batch else None)
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -1375,7 +1375,11 @@ struct EpiSwiGLU {
 // With MX, n is written as MXFP8 (BF16-rounded, then E4M3 codes through tmO2 as a byte
 // map with 128-code boxes, one E8M0 scale per row and 32 columns into n_scales).
 // MAXC bounds the CTAs per row (cluster_n), which sizes the partial-sum receive buffer.
-template <int BN, bool MX = false, int MAXC = kMaxClusterN>
+// LATE: the x tile lives in the stage ring, which is idle once the CTA's only tile has been
+// accumulated; the residual is then loaded after the main loop instead of prefetched during
+// it. This frees the tile's shared memory for another operand stage (wide models, where the
+// cluster's receive buffer and a 256-column x tile would otherwise leave three stages).
+template <int BN, bool MX = false, int MAXC = kMaxClusterN, bool LATE = false>
 struct EpiResNorm {
   static_assert(BN % 64 == 0, "64-column boxes");
   static_assert(!MX || BN % 128 == 0, "MXFP8 output needs 128-column slices");
@@ -1383,7 +1387,7 @@ struct EpiResNorm {
   enum Mode : int { kBias = 0, kResidual = 1 };
   static constexpr int kXBytes = kBM * BN * 2;
   static constexpr int kRecvFloats = MAXC * kMaxG * kBM;
-  static constexpr int kSmemBytes = kXBytes + kRecvFloats * 4;
+  static constexpr int kSmemBytes = (LATE ? 0 : kXBytes) + kRecvFloats * 4;
   struct Params {
     const __nv_bfloat16* bias;
     const __nv_bfloat16* norm_w;  // nullptr: no norm output
@@ -1398,14 +1402,17 @@ struct EpiResNorm {
   __device__ static uint32_t bar_count(const Params& p, int G) {
     return static_cast<uint32_t>(p.cluster_n * groups(G) * kBM);
   }
-  __device__ static bool prefetch(const Params& p, const TileCoord& tc, const CUtensorMap* tm_x,
-                                  uint32_t dst, uint32_t bar) {
-    if (p.mode != kResidual) return false;
+  __device__ static void load_x(const TileCoord& tc, const CUtensorMap* tm_x, uint32_t dst, uint32_t bar) {
     mbar_arrive_expect_tx(bar, kXBytes);
     for (int b = 0; b < BN / 64; ++b) {
       tma_load_2d(dst + static_cast<uint32_t>(b) * (kBM * 128), tm_x, bar, tc.n_tile * BN + 64 * b,
                   tc.out_row);
     }
+  }
+  __device__ static bool prefetch(const Params& p, const TileCoord& tc, const CUtensorMap* tm_x,
+                                  uint32_t dst, uint32_t bar) {
+    if (LATE || p.mode != kResidual) return false;
+    load_x(tc, tm_x, dst, bar);
     return true;
   }
 
@@ -1418,8 +1425,12 @@ struct EpiResNorm {
     static_assert(kPer % kGroups == 0, "chunks must split evenly");
     const bool active = et.g < kGroups;
     const int n0 = tc.n_tile * BN;
-    const uint32_t xs = ctx.smem;  // x tile (prefetched residual, then updated x)
-    float* recv = reinterpret_cast<float*>(ctx.smem_ptr + kXBytes);
+    // x tile (residual, then updated x) and n staging: the tile's own shared memory and the
+    // idle ring, or both in the ring (LATE).
+    const uint32_t xs = LATE ? ctx.ring : ctx.smem;
+    const uint32_t n_stage = LATE ? ctx.ring + kXBytes : ctx.ring;
+    float* recv = reinterpret_cast<float*>(ctx.smem_ptr + (LATE ? 0 : kXBytes));
+    if (LATE && p.mode == kResidual && et.tid == 0) load_x(tc, ctx.tmO1, xs, ctx.x_bar);
     bool ok = true;
     if (p.mode == kResidual && !mbar_wait(ctx.x_bar, 0)) {
       record_error(ctx.err, kErrTimeoutEpilogue);
@@ -1490,7 +1501,7 @@ struct EpiResNorm {
           round_bf16_inplace(v);
           uint32_t q[8];
           const uint8_t sc = mx_quantize32(v, q);
-          stage_u8x32(ctx.ring, et.r, c, q);
+          stage_u8x32(n_stage, et.r, c, q);
           if (et.r < tc.rows) {
             p.n_scales[mx_scale_offset(tc.out_row + et.r, (n0 + c) / 32, p.d / 128)] = sc;
             if (p.tap != nullptr) {
@@ -1498,7 +1509,7 @@ struct EpiResNorm {
             }
           }
         } else {
-          stage_bf16x32(ctx.ring, et.r, c, v);
+          stage_bf16x32(n_stage, et.r, c, v);
         }
       }
     }
@@ -1506,9 +1517,9 @@ struct EpiResNorm {
     epi_bar_sync<G>();
     if (et.tid == 0 && tc.rows > 0) {
       if constexpr (MX) {
-        store_staged_u8(ctx.tmO2, ctx.ring, BN, n0, tc.out_row);
+        store_staged_u8(ctx.tmO2, n_stage, BN, n0, tc.out_row);
       } else {
-        store_staged(ctx.tmO2, ctx.ring, BN, n0, tc.out_row);
+        store_staged(ctx.tmO2, n_stage, BN, n0, tc.out_row);
       }
     }
   }

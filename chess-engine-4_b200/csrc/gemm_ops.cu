@@ -237,8 +237,27 @@ void gemm_mx_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtenso
                      const CUtensorMap& tN, const uint8_t* sfa, const uint8_t* sfb,
                      uint8_t* n_scales, const bf16* bias, const bf16* norm_w, int m, int d, int k,
                      float eps, cudaStream_t s, bf16* tap) {
-  require(d % 128 == 0 && d / 128 <= kMaxClusterN && k % 128 == 0,
-          "MXFP8 residual GEMM needs d a multiple of 128 up to 1024 and K a multiple of 128");
+  require(d % 128 == 0 && k % 128 == 0 && (d / 128 <= kMaxClusterN || (d % 256 == 0 && d / 256 <= kMaxClusterN)),
+          "MXFP8 residual GEMM needs d a multiple of 128 up to 1024 (of 256 up to 2048) and K a multiple of 128");
+  if (d > 1024) {
+    // d / 256 CTAs per row (up to 8): the x tile moves into the stage ring after the main
+    // loop, which leaves room for four operand stages beside the cluster's receive buffer.
+    constexpr int BN = 256, NS = 4, NA = 1;
+    using Epi = EpiResNorm<BN, true, kMaxClusterN, true>;
+    auto kernel = gemm_mx_kernel<BN, NS, NA, 2, kG, true, DenseSched, Epi>;
+    constexpr int smem = GemmMxSmem<BN, NS, NA, Epi>::kBytes;
+    static_assert(GemmMxSmem<BN, NS, NA, Epi>::kRingBytes >= Epi::kXBytes + kBM * BN,
+                  "the ring must hold the x tile and the n codes");
+    ensure_smem(kernel, smem);
+    const int cn = d / BN;
+    DenseSched sched{m, cn, ceil_div(m, kBM) * cn, BN, 128};
+    typename Epi::Params ep{bias, norm_w, d, bias != nullptr ? Epi::kBias : Epi::kResidual,
+                            cn,   eps,    n_scales, tap};
+    const MxScales sf{sfa, sfb, k / 128};
+    launch(kernel, dim3(sched.num_tiles), gemm_threads(kG), smem, cn, s, tA, tB, tX, tN, sched, ep,
+           sf, k / 128, device_error_word());
+    return;
+  }
   if (d % 256 == 0 && d / 256 <= 4) {
     // 128 x 256 tiles (B as two 128-row boxes): a 256-column MMA keeps the tensor core busy
     // per ring stage where a 128-column one runs at half rate, and half as many CTAs.

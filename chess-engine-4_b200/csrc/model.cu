@@ -195,8 +195,8 @@ void Model::create(const ce4b_model_config& c, int dev, int maxb) {
   sel = selected_planes(c.history_length);
   in_dim = sel * 64;
   if (mx) {
-    require(c.d_model % 128 == 0 && c.d_model <= 1024,
-            "MXFP8 needs d_model a multiple of 128, at most 1024");
+    require(c.d_model % 128 == 0 && (c.d_model <= 1024 || (c.d_model % 256 == 0 && c.d_model <= 2048)),
+            "MXFP8 needs d_model a multiple of 128 up to 1024, or of 256 up to 2048");
     require(dense_hidden % 128 == 0, "MXFP8 needs a hidden width that is a multiple of 128");
     require(in_dim % 128 == 0, "MXFP8 needs an even history_length (input width multiple of 128)");
   }
