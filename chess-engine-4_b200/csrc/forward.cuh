@@ -856,7 +856,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) dense_forward_kernel(const Fwd
             ok = false;
             break;
           }
-          tc_fence_after();
+          // Operands landed by TMA: the stage barrier orders the MMAs after them (no
+          // tcgen05 fence; it is needed only where TMEM changes hands between threads).
           if (kb == 0) fwd_stamp(p, t, 3);
           const uint32_t sa = base + stage * L::kStageBytes;
           if (d96) {

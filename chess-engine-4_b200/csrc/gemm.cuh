@@ -278,7 +278,8 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
             ok = false;
             break;
           }
-          tc_fence_after();
+          // Operands landed by TMA: the stage barrier orders the MMAs after them (no
+          // tcgen05 fence; it is needed only where TMEM changes hands between threads).
           const uint32_t sa = base + stage * L::kStageBytes;
           const uint64_t adesc = sdesc_k128(sa);
           const uint64_t bdesc = sdesc_k128(sa + L::kABytes);
@@ -548,7 +549,8 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
             ok = false;
             break;
           }
-          tc_fence_after();
+          // Operands landed by TMA: the stage barrier orders the MMAs after them (no
+          // tcgen05 fence; it is needed only where TMEM changes hands between threads).
           const uint32_t sa = base + stage * L::kStageBytes;
           const uint64_t adesc = sdesc_k128(sa);
           const uint64_t bdesc = sdesc_k128(sa + L::kABytes);
@@ -803,7 +805,8 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
             ok = false;
             break;
           }
-          tc_fence_after();
+          // Operands landed by TMA: the stage barrier orders the MMAs after them (no
+          // tcgen05 fence; it is needed only where TMEM changes hands between threads).
           const uint32_t sa = base + stage * L::kStageBytes;
           const uint32_t sb = sa + L::kABytes;
           const uint32_t ssf = sb + L::kBBytes;
@@ -1058,7 +1061,8 @@ __global__ void __launch_bounds__(gemm_threads(G), 1)
             ok = false;
             break;
           }
-          tc_fence_after();
+          // Operands landed by TMA: the stage barrier orders the MMAs after them (no
+          // tcgen05 fence; it is needed only where TMEM changes hands between threads).
           const uint32_t sa = ring + static_cast<uint32_t>(stage * L::kStageBytes);
           const uint32_t sfa_t = tmem_base + static_cast<uint32_t>(L::kSfaCol + stage * 4);
           tmem_cp_32x128b_x4(sfa_t, sdesc_sf32x16(sa + L::kABytes));
