@@ -138,8 +138,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--batch", type=int, default=0, help="override the per-GPU batch")
     p.add_argument("--quick", action="store_true", help="skip e2e, latency, clocks and CPU baseline (profiling)")
     p.add_argument("--ep", action="store_true",
-                   help="moe64a2 under torchrun: split the 64 experts over the ranks (NCCL all-to-all of routed "
-                        "rows) instead of replicating them")
+                   help="moe64a2 under torchrun: split the 64 experts over the ranks (routed rows exchanged over "
+                        "NVLink peer memory) instead of replicating them")
     return p.parse_args()
 
 
@@ -653,8 +653,9 @@ def run_ours(args: argparse.Namespace, cfg: Config) -> None:
                 "workload": cfg.workload,
                 "global_batch": batch * world,
                 "per_gpu_batch": batch,
-                "parallelism": (f"expert parallel x{world} ({64 // world} experts per GPU, NCCL send/recv of "
-                                "routed rows; dense layers data-parallel)") if expert_parallel else
+                "parallelism": (f"expert parallel x{world} ({64 // world} experts held per GPU; routed rows and "
+                                "results over NVLink peer memory, planned on the device; dense layers "
+                                "data-parallel)") if expert_parallel else
                                f"replicas x{world} (no collective)",
                 "l2": "flushed between timed steps (256 MiB write, untimed)",
                 "input_layout": "lc0 InputPlane records resident in HBM",

@@ -675,12 +675,14 @@ class Moe64A2ChessNet(_NativeForwardMixin):
         world: int | None = None,
         unique_id: bytes | None = None,
     ) -> None:
-        """Splits the 64 experts over the ranks (64 / world consecutive experts each): every
-        MoE layer sends each routed row to its expert's rank and back with NCCL. Collective:
-        every rank calls it, each with its own GPU. rank / world default to the
-        torch.distributed default group, which also carries rank 0's NCCL unique id to the
-        others. Later forwards take this rank's positions (at most ``max_batch``) and return
-        their outputs, equal to the single-GPU forward's."""
+        """Splits the 64 experts over the ranks (64 / world consecutive experts each, the
+        only ones this rank keeps): every MoE layer sends each routed row to its expert's
+        rank and the result back over NVLink peer memory, with no host synchronisation.
+        Collective: every rank calls it, each with its own GPU. rank / world default to the
+        torch.distributed default group, which also carries rank 0's NCCL unique id (used
+        once, to exchange the buffer handles) to the others. Later forwards take this
+        rank's positions (at most ``max_batch``) and return their outputs, equal to the
+        single-GPU forward's; the weights are fixed from then on."""
 
         if rank is None or world is None:
             import torch.distributed as dist

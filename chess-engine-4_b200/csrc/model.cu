@@ -47,7 +47,6 @@ Model::~Model() {
   disable_expert_parallel();
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   if (fwd_dev) cudaFree(fwd_dev);
-  if (fwd_weights) cudaFree(fwd_weights);
   for (auto& slot : io)
     if (slot.free) cudaEventDestroy(slot.free);
   if (forward_done) cudaEventDestroy(forward_done);
@@ -69,7 +68,7 @@ void Model::add_slot(const std::string& name, std::vector<int64_t> shape, int dt
   slots.emplace(name, s);
 }
 
-void Model::plan_weights() {
+void Model::plan_weights(int experts) {
   const int d = cfg.d_model;
   size_t cur = 0;
   add_slot("input.weight", {d, in_dim}, CE4B_DTYPE_BF16, cur);
@@ -89,8 +88,8 @@ void Model::plan_weights() {
     if (is_moe_layer(l)) {
       add_slot(p + ".router.weight", {64, d}, CE4B_DTYPE_BF16, cur);
       add_slot(p + ".router_qb_beta", {64}, CE4B_DTYPE_F32, cur);
-      add_slot(p + ".experts.gate_up.weight", {64, 2 * expert_hidden, d}, CE4B_DTYPE_BF16, cur);
-      add_slot(p + ".experts.down.weight", {64, d, expert_hidden}, CE4B_DTYPE_BF16, cur);
+      add_slot(p + ".experts.gate_up.weight", {experts, 2 * expert_hidden, d}, CE4B_DTYPE_BF16, cur);
+      add_slot(p + ".experts.down.weight", {experts, d, expert_hidden}, CE4B_DTYPE_BF16, cur);
     } else {
       add_slot(p + ".gate_up.weight", {2 * dense_hidden, d}, CE4B_DTYPE_BF16, cur);
       add_slot(p + ".down.weight", {d, dense_hidden}, CE4B_DTYPE_BF16, cur);
@@ -231,6 +230,9 @@ void Model::set_tensor(const std::string& name, const void* data, int dtype,
          "tensor " + name + " has shape " + shape_str(shape) + ", expected " + shape_str(s.shape));
   }
   if (dtype != s.dtype) fail(CE4B_ERR_INVALID_ARGUMENT, "tensor " + name + " has the wrong dtype");
+  if (experts_held != 64) {
+    fail(CE4B_ERR_UNSUPPORTED, "an expert-parallel model holds only its own experts; its weights are fixed");
+  }
   require(data != nullptr, "tensor data is null");
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
   check_cuda(cudaMemcpy(arena + s.offset, data, s.bytes,
@@ -269,9 +271,10 @@ void Model::finalize() {
       const int he = expert_hidden;
       L.tm_router = make_tmap_bf16(w(p + ".router.weight"), 64, d, d, 64);
       L.beta = reinterpret_cast<const float*>(w(p + ".router_qb_beta"));
-      L.tm_gate_up = make_tmap_bf16(w(p + ".experts.gate_up.weight"), 64ull * 2 * he, d, d,
+      const uint64_t held = static_cast<uint64_t>(experts_held);
+      L.tm_gate_up = make_tmap_bf16(w(p + ".experts.gate_up.weight"), held * 2 * he, d, d,
                                     static_cast<uint32_t>(swiglu_chunk(he)));
-      L.tm_down = make_tmap_bf16(w(p + ".experts.down.weight"), 64ull * d, he, he,
+      L.tm_down = make_tmap_bf16(w(p + ".experts.down.weight"), held * d, he, he,
                                  static_cast<uint32_t>(grouped_bn(d)));
     }
     layers.push_back(L);
@@ -618,9 +621,6 @@ void Model::trace(const char* label, cudaStream_t s) {
 }
 
 cudaGraphExec_t Model::evaluate_graph(int batch, int slot) {
-  // Expert-parallel models synchronise with the host inside the forward (NCCL segment
-  // sizes), so they run without a graph.
-  if (ep_world > 1) return nullptr;
   IoSlot& io_slot = io[slot];
   auto* planes = reinterpret_cast<ce4b_input_plane*>(workspace + io_slot.planes);
   float* pol = reinterpret_cast<float*>(workspace + io_slot.policy);

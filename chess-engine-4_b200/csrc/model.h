@@ -175,8 +175,7 @@ struct Model {
                               const int32_t* host_offsets, const int32_t* host_indices,
                               float temperature, float* host_probs, float* host_wdl,
                               float* host_moves_left, cudaStream_t s);
-  // Graph of the host-buffer forward for (batch, slot), built on first use (nullptr for
-  // expert-parallel models, which run without a graph).
+  // Graph of the host-buffer forward for (batch, slot), built on first use.
   cudaGraphExec_t evaluate_graph(int batch, int slot);
   void trace(const char* label, cudaStream_t s);
   void quantize_weights();
@@ -184,23 +183,25 @@ struct Model {
                   float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s);
   void forward_fused(int layout, void* input, const void* scalars, int batch, float* policy,
                      float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s);
-  // Expert parallelism (moe64a2): each of ep_world ranks computes 64 / ep_world experts;
-  // routed rows travel with NCCL (ep_comm is an ncclComm_t).
+  // Expert parallelism (moe64a2): each of ep_world ranks holds and computes 64 / ep_world
+  // consecutive experts (the weight arena is repacked to them). Routed rows, their weights
+  // and the results travel through every rank's shared EP buffer over NVLink peer memory
+  // (CUDA IPC), ordered by per-layer epoch flags; NCCL only carries the IPC handles once.
   int ep_world = 1;
   int ep_rank = 0;
-  void* ep_comm = nullptr;
-  size_t ep_cap_rows = 0;
-  uint8_t* ep_buf = nullptr;
-  void* ep_host = nullptr;  // pinned: segment metadata and the m-tile table
-  bf16* ep_x = nullptr;
-  bf16* ep_h = nullptr;
-  bf16* ep_y = nullptr;
-  float* ep_p = nullptr;
-  int* ep_counts = nullptr;
-  int2* ep_meta = nullptr;
-  int4* ep_tiles = nullptr;
-  int* ep_num_tiles = nullptr;
+  void* ep_comm = nullptr;        // ncclComm_t used at set-up
+  size_t ep_cap_rows = 0;         // received-row capacity
+  uint8_t* ep_buf = nullptr;      // this rank's buffer: shared part, then local part
+  size_t ep_buf_bytes = 0;
+  std::vector<uint8_t*> ep_peer;  // every rank's buffer (own included), IPC-mapped
+  struct EpOffsets {
+    size_t x = 0, p = 0, meta = 0, flags = 0, ret = 0;  // shared: peers write these
+    size_t h = 0, y = 0, counts = 0, epoch = 0, done = 0, send_off = 0, recv_off = 0, recv_rows = 0,
+           ret_off = 0, tiles = 0, num_tiles = 0;       // local
+  } ep_off;
   CUtensorMap tm_ep_x{}, tm_ep_h{}, tm_ep_y{};
+  // Experts held per MoE layer (64, or 64 / ep_world once the arena is repacked).
+  int experts_held = 64;
   void enable_expert_parallel(int rank, int world, const void* unique_id);
   void disable_expert_parallel();
   void moe_layer_ep(const Layer& L, int moe_index, const bf16* next_norm, int batch,
@@ -215,7 +216,9 @@ struct Model {
  private:
   void add_slot(const std::string& name, std::vector<int64_t> shape, int dtype, size_t& cursor,
                 bool pack = false);
-  void plan_weights();
+  void plan_weights(int experts = 64);
+  // Keeps this rank's experts only (expert parallelism): new arena, tensors copied.
+  void repack_experts(int rank, int world);
   void plan_workspace();
   bf16* w(const std::string& name) const;
 };

@@ -181,19 +181,26 @@ int ce4b_model_evaluate_legal(ce4b_model* model, const ce4b_input_plane* host_pl
  * ce4b_model_trace_label names kernel i of the last traced forward. */
 int ce4b_model_set_trace(ce4b_model* model, void* const* events, int count);
 /* ------------------------------------------------------------------ expert parallelism
- * moe64a2 across `world` GPUs (one process and one model handle per GPU): each rank
- * computes 64 / world consecutive experts; every MoE layer sends each routed row to the
- * rank of its expert and back with NCCL send/recv (expert parallelism over the reference's
- * static dispatch path, src/chess_engine_4/model/moe.py:226-287). Each rank passes its own
- * batch of positions to ce4b_model_forward / ce4b_model_evaluate; results equal the
- * single-GPU forward of those positions. The forward synchronises with the host once per
- * MoE layer (segment sizes), so expert-parallel forwards are not graph-captured.
- * ce4b_nccl_unique_id fills the 128-byte NCCL unique id (rank 0 makes it, every rank passes
- * the same bytes); ce4b_model_enable_expert_parallel is collective over the ranks. */
+ * moe64a2 across `world` GPUs of one node (one process and one model handle per GPU, world
+ * in {2, 4, 8}): each rank holds and computes only 64 / world consecutive experts (its
+ * weight arena is repacked to them when this is enabled, so weights are fixed from then on).
+ * Every MoE layer sends each routed row to the rank of its expert and the result back
+ * (expert parallelism over the reference's static dispatch path,
+ * src/chess_engine_4/model/moe.py:226-287) through the ranks' shared buffers over NVLink
+ * peer memory (CUDA IPC), with the receive layout and the grouped GEMMs' tile table built
+ * on the device: no host synchronisation, so forwards may be captured in CUDA graphs. Each
+ * rank passes its own batch of positions to ce4b_model_forward / ce4b_model_evaluate, and
+ * every rank must run the same sequence of forwards; results equal the single-GPU forward
+ * of those positions. A peer that stops answering turns into a device error
+ * (ce4b_check_device_error) after 2 s instead of a hang. ce4b_nccl_unique_id fills the
+ * 128-byte NCCL unique id used once to exchange the buffer handles (rank 0 makes it, every
+ * rank passes the same bytes); ce4b_model_enable_expert_parallel is collective over the
+ * ranks and needs a finalized model. */
 int ce4b_nccl_unique_id(void* out, int out_len);
 int ce4b_model_enable_expert_parallel(ce4b_model* model, int rank, int world, const void* unique_id);
 
-/* Host planning of one exchange, as the forward does it (no GPU): meta_send[64][2] holds
+/* Host restatement of the exchange plan that the forward builds on the device (no GPU;
+ * the forward's tile table uses local expert indices): meta_send[64][2] holds
  * this rank's {segment rows padded to 128, valid rows} per expert, meta_recv[world][64 /
  * world][2] the same from every rank for this rank's experts. Outputs rows sent to / received
  * from each rank and the m-tile table over the received rows (int32 x4 per tile: global

@@ -53,24 +53,40 @@ def ep_plan_worker(rank: int, world: int, port: int, seed: int, queue) -> None:
     dist.destroy_process_group()
 
 
-def ep_forward_worker(rank: int, world: int, port: int, unique_id: bytes, batch: int, queue) -> None:
-    """One expert-parallel rank on GPU `rank`: forwards its half of the batch."""
+def ep_forward_worker(rank: int, world: int, port: int, unique_id: bytes, batch: int, queue,
+                      d: int = 256, depth: int = 2, repeats: int = 1) -> None:
+    """One expert-parallel rank on GPU `rank`: forwards its share of the batch `repeats`
+    times (every result must be the same) and reports the weight bytes it holds before and
+    after enabling expert parallelism."""
+
+    import ctypes
 
     import torch
 
     torch.cuda.set_device(rank)
-    from ce4b200 import Moe64A2ChessNet, Moe64A2ChessNetConfig, replicas, synthetic
+    from ce4b200 import Moe64A2ChessNet, Moe64A2ChessNetConfig, _lib, replicas, synthetic
 
-    model = Moe64A2ChessNet(Moe64A2ChessNetConfig(d_model=256, depth=2, expansion_ratio=1.0, precision="bf16"))
-    synthetic.load_into(model, synthetic.make_moe_weights(d_model=256, depth=2, expert_hidden=256, seed=5))
+    model = Moe64A2ChessNet(Moe64A2ChessNetConfig(d_model=d, depth=depth, expansion_ratio=1.0, precision="bf16"))
+    synthetic.load_into(model, synthetic.make_moe_weights(d_model=d, depth=depth, expert_hidden=d, seed=5))
     model = model.cuda()
     planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(batch, 9))
     start, count = replicas.shard_rows(batch, world, rank)
+    engine = model._engine(batch, torch.device("cuda", rank))
+    info = _lib.ModelInfoStruct()
+    _lib.check(engine.lib.ce4b_model_info_get(engine.handle, ctypes.byref(info)))
+    full_bytes = info.weight_bytes
     model.enable_expert_parallel(max_batch=batch, rank=rank, world=world, unique_id=unique_id)
-    out = model(planes[start:start + count].cuda())
-    torch.cuda.synchronize()
-    queue.put((rank, out.policy_logits.cpu(), out.wdl_logits.cpu(), out.moves_left.cpu(),
-               out.router_tokens_per_expert.cpu() if out.router_tokens_per_expert is not None else None))
+    _lib.check(engine.lib.ce4b_model_info_get(engine.handle, ctypes.byref(info)))
+    outs = []
+    for _ in range(repeats):
+        out = model(planes[start:start + count].cuda())
+        torch.cuda.synchronize()
+        outs.append((out.policy_logits.cpu(), out.wdl_logits.cpu(), out.moves_left.cpu()))
+    code = _lib.check_device_error(rank)
+    same = all(torch.equal(a, b) for o in outs[1:] for a, b in zip(o, outs[0]))
+    queue.put((rank, *outs[0],
+               out.router_tokens_per_expert.cpu() if out.router_tokens_per_expert is not None else None,
+               full_bytes, info.weight_bytes, code, same))
 
 
 def collect(procs, queue, timeout_s: float):

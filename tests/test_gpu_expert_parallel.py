@@ -1,5 +1,6 @@
-"""GPU, two or more devices: moe64a2 with experts split over two ranks (NCCL send/recv of
-routed rows) gives, on each rank's positions, exactly the single-GPU forward's outputs."""
+"""GPU, two or more devices: moe64a2 with experts split over the ranks (each rank holds
+only its 64 / world experts; routed rows and results travel over NVLink peer memory) gives,
+on each rank's positions, exactly the single-GPU forward's outputs."""
 
 from __future__ import annotations
 
@@ -19,20 +20,22 @@ def _free_port() -> int:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_expert_parallel_forward_equals_single_gpu() -> None:
+@pytest.mark.parametrize("d,depth,batch,repeats", [(256, 2, 700, 1), (768, 4, 4096, 3)])
+def test_expert_parallel_forward_equals_single_gpu(d: int, depth: int, batch: int, repeats: int) -> None:
     from ce4b200 import Moe64A2ChessNet, Moe64A2ChessNetConfig, _lib, replicas, synthetic
     from dist_worker import collect, ep_forward_worker
 
-    batch = 700
+    world = 2
     unique_id = _lib.nccl_unique_id()
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=ep_forward_worker, args=(r, 2, port, unique_id, batch, queue)) for r in range(2)]
+    procs = [ctx.Process(target=ep_forward_worker, args=(r, world, port, unique_id, batch, queue, d, depth, repeats))
+             for r in range(world)]
     try:
         for p in procs:
             p.start()
-        results = sorted(collect(procs, queue, 300), key=lambda x: x[0])
+        results = sorted(collect(procs, queue, 600), key=lambda x: x[0])
         for p in procs:
             p.join(timeout=120)
             assert p.exitcode == 0
@@ -41,18 +44,23 @@ def test_expert_parallel_forward_equals_single_gpu() -> None:
             if p.is_alive():
                 p.kill()
 
-    model = Moe64A2ChessNet(Moe64A2ChessNetConfig(d_model=256, depth=2, expansion_ratio=1.0, precision="bf16"))
-    synthetic.load_into(model, synthetic.make_moe_weights(d_model=256, depth=2, expert_hidden=256, seed=5))
+    model = Moe64A2ChessNet(Moe64A2ChessNetConfig(d_model=d, depth=depth, expansion_ratio=1.0, precision="bf16"))
+    weights = synthetic.make_moe_weights(d_model=d, depth=depth, expert_hidden=d, seed=5)
+    synthetic.load_into(model, weights)
     model = model.cuda()
     planes = synthetic.lc0_to_dense(synthetic.make_lc0_planes(batch, 9))
     ref = model(planes.cuda())
     torch.cuda.synchronize()
-    for rank, policy, wdl, ml, tokens in results:
-        start, count = replicas.shard_rows(batch, 2, rank)
+    expert_bytes = sum(t.numel() * t.element_size() for k, t in weights.items() if ".experts." in k)
+    for rank, policy, wdl, ml, tokens, full_bytes, held_bytes, code, same in results:
+        assert code == 0, f"rank {rank}: device error word {code}"
+        assert same, f"rank {rank}: repeated forwards differ"
+        start, count = replicas.shard_rows(batch, world, rank)
         assert torch.equal(policy, ref.policy_logits.cpu()[start:start + count])
         assert torch.equal(wdl, ref.wdl_logits.cpu()[start:start + count])
         assert torch.equal(ml, ref.moves_left.cpu()[start:start + count])
-    # Tokens per expert count this rank's own tokens; the two ranks add up to the total.
-    if results[0][4] is not None and ref.router_tokens_per_expert is not None:
-        total = results[0][4] + results[1][4]
-        assert torch.equal(total, ref.router_tokens_per_expert.cpu())
+        # Only this rank's experts stay resident.
+        assert full_bytes - held_bytes >= expert_bytes * (world - 1) // world - 4096 * depth
+    # Tokens per expert count this rank's own tokens; the ranks add up to the total.
+    total = sum(r[4] for r in results)
+    assert torch.equal(total, ref.router_tokens_per_expert.cpu())
