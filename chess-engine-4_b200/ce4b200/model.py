@@ -373,6 +373,14 @@ class _NativeModel:
         _lib.check(self.lib.ce4b_model_create(ctypes.byref(cfg), device, max_batch, ctypes.byref(handle)))
         self.handle = handle
 
+    def set_latency_path(self, enabled: bool) -> None:
+        _lib.check(self.lib.ce4b_model_set_latency_path(self.handle, 1 if enabled else 0))
+
+    def uses_latency_path(self, batch: int) -> bool:
+        uses = ctypes.c_int32()
+        _lib.check(self.lib.ce4b_model_uses_latency_path(self.handle, batch, ctypes.byref(uses)))
+        return bool(uses.value)
+
     def upload(self, tensors: dict[str, torch.Tensor]) -> None:
         target = torch.device("cuda", self.device)
         staged: dict[str, torch.Tensor] = {}
@@ -484,6 +492,7 @@ class _NativeForwardMixin(nn.Module):
             capacity = (capacity + 255) // 256 * 256
             self.__dict__["_native"] = None
             engine = _NativeModel(self._native_config(), index, capacity)
+            engine.set_latency_path(self.__dict__.get("_latency_path", True))
             self.__dict__["_native"] = engine
             self.__dict__["_native_signature"] = None
         signature = self._weights_signature()
@@ -582,6 +591,17 @@ class _NativeForwardMixin(nn.Module):
 
     def enable_custom_kernels(self) -> None:
         """Always on the sm_100a kernels; kept for API compatibility."""
+
+    def set_latency_path(self, enabled: bool) -> None:
+        """Dense BF16 models with d_model <= 512 run batches of at most 64 positions on the
+        small-batch forward (one cooperative launch of transposed tiles spread over the SMs,
+        RMSNorm at the reference's rounding point). ``False`` sends them to the persistent
+        forward instead; the default is ``True``."""
+
+        self.__dict__["_latency_path"] = bool(enabled)
+        engine = self.__dict__.get("_native")
+        if engine is not None:
+            engine.set_latency_path(enabled)
 
 
 def _bf16(t: torch.Tensor) -> torch.Tensor:

@@ -310,7 +310,31 @@ int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks) {
     require(model != nullptr && model->impl && tasks != nullptr, "null argument");
     const ce4b::Model& m = *model->impl;
     require(batch >= 1 && batch <= m.max_batch, "batch size exceeds model capacity");
-    *tasks = m.fused ? m.fused_task_count(batch) : 0;
+    if (m.fused && m.latency_path(batch)) {
+      *tasks = m.lat_grid * m.lat_max_tasks;
+    } else {
+      *tasks = m.fused ? m.fused_task_count(batch) : 0;
+    }
+  });
+}
+
+int ce4b_model_set_latency_path(ce4b_model* model, int enable) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    ce4b::Model& m = *model->impl;
+    if (m.lat_enabled != (enable != 0)) {
+      m.lat_enabled = enable != 0;
+      m.graphs_clear();  // captured forwards of small batches used the other path
+    }
+  });
+}
+
+int ce4b_model_uses_latency_path(const ce4b_model* model, int batch, int* uses) {
+  return guarded([&] {
+    require(model != nullptr && model->impl && uses != nullptr, "null argument");
+    const ce4b::Model& m = *model->impl;
+    require(batch >= 1 && batch <= m.max_batch, "batch size exceeds model capacity");
+    *uses = m.fused && m.latency_path(batch) ? 1 : 0;
   });
 }
 

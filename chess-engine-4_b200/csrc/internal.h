@@ -70,6 +70,9 @@ int resnorm_bn(int d);
 // Persistent dense forward (input GEMM, all layers, RMSNorm passes) in one launch.
 struct FwdParams;
 void dense_forward(const FwdParams& p, cudaStream_t s);
+// Small-batch dense forward (latency.cu) in one cooperative launch of `grid` CTAs.
+struct LatParams;
+void latency_forward(const LatParams& p, int grid, cudaStream_t s);
 // Rows of the tB box that gemm_resnorm expects for width d (BN, or BN/2 on CTA pairs).
 int resnorm_b_box(int d);
 void gemm_resnorm(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tX,

@@ -47,6 +47,8 @@ Model::~Model() {
   disable_expert_parallel();
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   if (fwd_dev) cudaFree(fwd_dev);
+  if (fwd_weights) cudaFree(fwd_weights);
+  if (lat_dev) cudaFree(lat_dev);
   for (auto& slot : io)
     if (slot.free) cudaEventDestroy(slot.free);
   if (forward_done) cudaEventDestroy(forward_done);
@@ -139,6 +141,15 @@ void Model::plan_workspace() {
     fwd_sync_bytes = (2 * nb + 2 * nb * sj + 1) * 4;
     ws_off.fwd_sync = take(fwd_sync_bytes);
   }
+  if (lat) {
+    // FP32 partial tiles [d / 128][K parts][64 positions][128] of the input and down GEMMs,
+    // and the counters (x ready, hidden ready, one per 128-row block for each GEMM).
+    const size_t mt = static_cast<size_t>(d / 128);
+    ws_off.lat_part_in = take(mt * lat_kp_in * kLatMaxRows * 128 * 4);
+    ws_off.lat_part_dn = take(mt * lat_kp_dn * kLatMaxRows * 128 * 4);
+    lat_sync_bytes = (2 + 2 * mt) * 4;
+    ws_off.lat_sync = take(lat_sync_bytes);
+  }
   if (cfg.arch == CE4B_ARCH_MOE64A2) {
     // Expert rows: 2 routes per token, each expert segment padded to 128 rows.
     perm_rows = static_cast<int>((2 * r + 64 * 127 + 127) / 128 * 128);
@@ -208,6 +219,7 @@ void Model::create(const ce4b_model_config& c, int dev, int maxb) {
   (void)resnorm_bn(c.d_model);  // validates width against the cluster limit
 
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  plan_latency();
   plan_weights();
   plan_workspace();
   check_cuda(cudaMalloc(&arena, arena_bytes), "cudaMalloc weights");
@@ -318,6 +330,7 @@ void Model::finalize() {
     check_cuda(cudaMemcpy(fwd_dev, &maps, sizeof(FwdMaps), cudaMemcpyHostToDevice),
                "copy forward tensor maps");
   }
+  if (lat) build_latency();
   if (mx) quantize_weights();
   for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
   graphs.clear();
@@ -504,6 +517,125 @@ void Model::forward_fused(int layout, void* input, const void* scalars, int batc
   trace("dense_tower", s);
 }
 
+// Shapes of the small-batch forward (latency.cu). Input GEMM: the most K parts of at most 4
+// k-blocks that fit the SMs with d / 128 row blocks each. Down GEMMs: K parts of 2 k-blocks
+// (1 when h / 64 is odd). gate_up tiles of even and odd layers, down tiles and head tiles
+// each get their own CTAs, so a CTA's next weights load while it waits for its inputs.
+void Model::plan_latency() {
+  lat = false;
+  const int d = cfg.d_model, h = dense_hidden;
+  if (!fused || d > kLatMaxD || d % 128 != 0 || h % 64 != 0 || cfg.depth > kFwdMaxDepth) return;
+  const int sms = sm_count();
+  const int mt = d / 128, kb_in = in_dim / 64, hb = h / 64;
+  int kp_in = 0;
+  for (int kp = 1; kp <= kb_in; ++kp) {
+    if (kb_in % kp == 0 && kb_in / kp <= kLatMaxKbSlot && mt * kp <= sms) kp_in = kp;
+  }
+  const int kc_dn = hb % 2 == 0 ? 2 : 1;
+  const int kp_dn = hb / kc_dn;
+  const int ht = (policy_storage + 64 + 127) / 128;
+  const int layer_ctas = (cfg.depth > 1 ? 2 : 1) * hb + mt * kp_dn + ht;
+  const int grid = std::max(layer_ctas, mt * kp_in);
+  if (kp_in == 0 || grid > sms) return;
+  lat = true;
+  lat_kp_in = kp_in;
+  lat_kp_dn = kp_dn;
+  lat_grid = grid;
+}
+
+// Tensor maps and the per-CTA task lists of the small-batch forward (one device buffer).
+void Model::build_latency() {
+  const int d = cfg.d_model, h = dense_hidden, depth = cfg.depth;
+  const int mt = d / 128, gt = h / 64, ht = (policy_storage + 64 + 127) / 128;
+  LatMaps maps{};
+  maps.a_in = make_tmap_bf16(workspace + ws_off.a_in, rows_cap, in_dim, in_dim, 64);
+  maps.x = make_tmap_bf16(workspace + ws_off.x, rows_cap, d, d, 64);
+  maps.hidden = make_tmap_bf16(workspace + ws_off.hidden, rows_cap, h, h, 64);
+  maps.w_in = make_tmap_bf16(w("input.weight"), d, in_dim, in_dim, 128);
+  for (int l = 0; l < depth; ++l) {
+    const std::string p = "blocks." + std::to_string(l);
+    maps.gate_up[l] = make_tmap_bf16(w(p + ".gate_up.weight"), 2 * h, d, d, 64);
+    maps.down[l] = make_tmap_bf16(w(p + ".down.weight"), d, h, h, 128);
+  }
+  maps.heads = make_tmap_bf16(w("policy.weight"), policy_storage + 64, d, d, 128);
+  // Task lists, each in dependency order (input, layers, heads), so that with every CTA
+  // resident no wait can form a cycle.
+  std::vector<std::vector<int4>> lists(lat_grid);
+  const int n_in = mt * lat_kp_in;
+  for (int m = 0; m < mt; ++m) {
+    for (int k = 0; k < lat_kp_in; ++k) lists[lat_grid - n_in + m * lat_kp_in + k].push_back({kLatInput, 0, m, k});
+  }
+  const int down0 = (depth > 1 ? 2 : 1) * gt;
+  const int heads0 = down0 + mt * lat_kp_dn;
+  for (int l = 0; l < depth; ++l) {
+    for (int j = 0; j < gt; ++j) lists[(l % 2) * gt + j].push_back({kLatGateUp, l, j, 0});
+    for (int m = 0; m < mt; ++m) {
+      for (int k = 0; k < lat_kp_dn; ++k) lists[down0 + m * lat_kp_dn + k].push_back({kLatDown, l, m, k});
+    }
+  }
+  for (int t = 0; t < ht; ++t) lists[heads0 + t].push_back({kLatHeads, depth, t, 0});
+  lat_max_tasks = 1;
+  for (const auto& v : lists) lat_max_tasks = std::max(lat_max_tasks, static_cast<int>(v.size()) + 1);
+  std::vector<int4> table(static_cast<size_t>(lat_grid) * lat_max_tasks, int4{kLatEnd, 0, 0, 0});
+  for (int c = 0; c < lat_grid; ++c) {
+    for (size_t i = 0; i < lists[c].size(); ++i) table[static_cast<size_t>(c) * lat_max_tasks + i] = lists[c][i];
+  }
+  const size_t maps_bytes = align256(sizeof(LatMaps));
+  if (lat_dev != nullptr) cudaFree(lat_dev);
+  lat_dev = nullptr;
+  check_cuda(cudaMalloc(&lat_dev, maps_bytes + table.size() * sizeof(int4)), "cudaMalloc small-batch plan");
+  check_cuda(cudaMemcpy(lat_dev, &maps, sizeof(LatMaps), cudaMemcpyHostToDevice), "copy small-batch maps");
+  check_cuda(cudaMemcpy(lat_dev + maps_bytes, table.data(), table.size() * sizeof(int4), cudaMemcpyHostToDevice),
+             "copy small-batch tasks");
+}
+
+void Model::forward_latency(int layout, void* input, const void* scalars, int batch, float* policy,
+                            float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s) {
+  const int d = cfg.d_model;
+  auto* sync = reinterpret_cast<int*>(workspace + ws_off.lat_sync);
+  check_cuda(cudaMemsetAsync(sync, 0, lat_sync_bytes, s), "reset small-batch counters");
+  expand_input(layout, input, scalars, batch, cfg.history_length,
+               reinterpret_cast<bf16*>(workspace + ws_off.a_in), write_back, s);
+  trace("expand_planes", s);
+  LatParams p{};
+  p.maps = reinterpret_cast<const LatMaps*>(lat_dev);
+  p.tasks = reinterpret_cast<const int4*>(lat_dev + align256(sizeof(LatMaps)));
+  p.max_tasks = lat_max_tasks;
+  p.in_bias = w("input.bias");
+  for (int l = 0; l < cfg.depth; ++l) p.norm[l] = layers[l].norm;
+  p.final_norm = w("final_norm.weight");
+  p.head_bias = w("policy.bias");
+  p.x = reinterpret_cast<bf16*>(workspace + ws_off.x);
+  p.hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);
+  p.part_in = reinterpret_cast<float*>(workspace + ws_off.lat_part_in);
+  p.part_dn = reinterpret_cast<float*>(workspace + ws_off.lat_part_dn);
+  p.cnt = sync;
+  p.err = device_error_word();
+  p.policy = policy;
+  p.wdl = wdl;
+  p.moves_left = moves_left;
+  p.batch = batch;
+  p.n = (batch + 15) / 16 * 16;
+  p.d = d;
+  p.h = dense_hidden;
+  p.depth = cfg.depth;
+  p.mt = d / 128;
+  p.kb_in = in_dim / 64;
+  p.kp_in = lat_kp_in;
+  p.kp_dn = lat_kp_dn;
+  p.gt = dense_hidden / 64;
+  p.ht = (policy_storage + 64 + 127) / 128;
+  p.policy_size = policy_size;
+  p.policy_storage = policy_storage;
+  p.head_cols = policy_storage + 64;
+  p.wdl_probs = wdl_probs;
+  p.eps = cfg.rms_norm_eps;
+  p.trace = fwd_trace;
+  p.trace_cap = fwd_trace_cap;
+  latency_forward(p, lat_grid, s);
+  trace("dense_latency", s);
+}
+
 void Model::forward(int layout, void* input, const void* scalars, int batch, float* policy,
                     float* wdl, float* moves_left, int wdl_probs, int normalize_in_place,
                     int32_t* tokens_per_expert, cudaStream_t s) {
@@ -521,7 +653,11 @@ void Model::forward(int layout, void* input, const void* scalars, int batch, flo
   trace_next = 0;
   trace_labels.clear();
   if (fused) {
-    forward_fused(layout, input, scalars, batch, policy, wdl, moves_left, wdl_probs, write_back, s);
+    if (latency_path(batch)) {
+      forward_latency(layout, input, scalars, batch, policy, wdl, moves_left, wdl_probs, write_back, s);
+    } else {
+      forward_fused(layout, input, scalars, batch, policy, wdl, moves_left, wdl_probs, write_back, s);
+    }
     return;
   }
   if (mx) {

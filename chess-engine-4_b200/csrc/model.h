@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "internal.h"
+#include "latency_types.h"
 
 namespace ce4b {
 
@@ -48,6 +49,7 @@ struct Model {
     size_t yperm = 0;
     size_t a_codes = 0, a_scales = 0, n_codes = 0, n_scales = 0, h_codes = 0, h_scales = 0;
     size_t fwd_ss = 0, fwd_part = 0, fwd_sync = 0;  // persistent dense forward
+    size_t lat_part_in = 0, lat_part_dn = 0, lat_sync = 0;  // small-batch forward
   };
 
   ce4b_model_config cfg{};
@@ -113,6 +115,20 @@ struct Model {
     return nb * (cfg.d_model / fused_xwi()) * fused_kis(batch) +
            cfg.depth * nb * (nc + xt * fused_dks(batch)) + nb * fused_head_tasks();
   }
+  // Small-batch forward (latency.cu): dense BF16 models with d <= 512 run batches of at
+  // most kLatMaxRows positions as one cooperative launch of short transposed tiles spread
+  // over the SMs. Planned at create (lat = the shape allows it); lat_enabled can turn it
+  // off (ce4b_model_set_latency_path), which sends small batches to the persistent forward.
+  bool lat = false;
+  bool lat_enabled = true;
+  int lat_grid = 0, lat_max_tasks = 0, lat_kp_in = 0, lat_kp_dn = 0;
+  uint8_t* lat_dev = nullptr;  // LatMaps, then the [grid][max_tasks] task table
+  size_t lat_sync_bytes = 0;
+  bool latency_path(int batch) const { return lat && lat_enabled && batch <= kLatMaxRows; }
+  void plan_latency();
+  void build_latency();
+  void forward_latency(int layout, void* input, const void* scalars, int batch, float* policy,
+                       float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s);
   uint8_t* mx_arena = nullptr;    // quantised weights (codes + scales)
   size_t mx_arena_bytes = 0;
   const uint8_t* w_in_scales = nullptr;

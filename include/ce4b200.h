@@ -224,6 +224,23 @@ int ce4b_expert_parallel_plan(int world, int rank, const int32_t* meta_send, con
 int ce4b_model_set_task_trace(ce4b_model* model, void* device_buffer, int capacity_tasks);
 int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks);
 
+/* Small-batch forward of dense BF16 models with d_model <= 512: batches of at most 64
+ * positions run as one cooperative launch in which every GEMM is computed transposed
+ * (weights on the MMA's 128-row side, positions on its N side) and split over most SMs,
+ * with RMSNorm at the reference's rounding point (n = bf16(x * rsqrt(mean(x^2)+eps) * w),
+ * kernels/src/inference/runtime.cu:182-336). It is the latency path of the lc0 backend's
+ * per-search-batch evaluation (third_party/lc0/src/neural/backends/ce4/backend.cc:163-168,
+ * Model::Evaluate in kernels/src/inference/runtime.cu:532-564). Enabled by default;
+ * enable = 0 sends small batches to the persistent forward instead (for comparisons).
+ * With the task trace on, task index = CTA * max_tasks + position in the CTA's list
+ * (ce4b_model_task_count gives grid * max_tasks), words 0..7 = task start, inputs ready,
+ * activations landed, MMAs issued, MMAs done, results stored and published, all K parts
+ * in, this CTA's share of the sum published; word 10 = CTA, word 11 = type << 48 |
+ * layer << 32 | tile << 16 | part. ce4b_model_uses_latency_path reports the choice for a
+ * batch size. */
+int ce4b_model_set_latency_path(ce4b_model* model, int enable);
+int ce4b_model_uses_latency_path(const ce4b_model* model, int batch, int* uses);
+
 int ce4b_model_trace_label(const ce4b_model* model, int index, char* buffer, int buffer_len);
 
 /* Routing tap (testing hook) of a moe64a2 model: with experts_dev set, each later
