@@ -47,7 +47,8 @@ constexpr uint32_t kOffW = 0;
 constexpr uint32_t kOffAct = 2 * kLatWSlotBytes;
 constexpr uint32_t kOffXch = kOffAct + kLatMaxRows * kLatMaxD * 2;
 constexpr uint32_t kOffBar = kOffXch + kLatMaxRows * 64 * 4;
-constexpr int kLatSmemBytes = 1024 + kOffBar + 64;
+constexpr uint32_t kOffNorm = kOffBar + 64;  // norm weights of the current task [d] BF16
+constexpr int kLatSmemBytes = 1024 + kOffNorm + kLatMaxD * 2;
 static_assert(kLatSmemBytes <= 232448, "shared memory budget exceeded");
 
 __device__ __forceinline__ void lat_stamp(const LatParams& p, int idx, int slot) {
@@ -108,35 +109,36 @@ __device__ __forceinline__ void lat_issue_weights(const LatParams& p, const int4
 // In place: the 64 x d BF16 tile at `act` (d / 64 boxes of [64 rows][128 B] with the 128-byte
 // swizzle) becomes n = bf16((x * rsqrt(mean(x^2) + eps)) * w), row by row (four threads a
 // row, eight columns a chunk).
-__device__ __forceinline__ void lat_normalize(uint32_t act, const bf16* __restrict__ w, int d, float eps) {
+__device__ __forceinline__ void lat_normalize(uint8_t* act, const uint4* __restrict__ wq, int d, float eps) {
   const int r = threadIdx.x >> 2, q = threadIdx.x & 3;
   const int nch = d / 32;
   uint4 v[kLatMaxD / 32];
-  float ss = 0.0f;
+  float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int k = 0; k < kLatMaxD / 32; ++k) {
     if (k < nch) {
       const int c = q + 4 * k;
-      v[k] = ld_shared_v4(act + static_cast<uint32_t>((c >> 3) * kLatActKb) + swz128(r, c & 7));
+      v[k] = *reinterpret_cast<const uint4*>(act + (c >> 3) * kLatActKb + swz128(r, c & 7));
       const uint32_t wd[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = unpack_bf16x2(wd[j]);
-        ss = fmaf(f.x, f.x, ss);
-        ss = fmaf(f.y, f.y, ss);
+        ss[j] = fmaf(f.x, f.x, ss[j]);
+        ss[j] = fmaf(f.y, f.y, ss[j]);
       }
     }
   }
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-  const float rs = rsqrtf(__fdiv_rn(ss, static_cast<float>(d)) + eps);
+  float sum = (ss[0] + ss[1]) + (ss[2] + ss[3]);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  const float rs = rsqrtf(__fdiv_rn(sum, static_cast<float>(d)) + eps);
 #pragma unroll
   for (int k = 0; k < kLatMaxD / 32; ++k) {
     if (k < nch) {
       const int c = q + 4 * k;
-      const uint4 wq = __ldg(reinterpret_cast<const uint4*>(w) + c);
       const uint32_t xs[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-      const uint32_t ws[4] = {wq.x, wq.y, wq.z, wq.w};
+      const uint4 wc = wq[c];
+      const uint32_t ws[4] = {wc.x, wc.y, wc.z, wc.w};
       uint32_t o[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -144,8 +146,7 @@ __device__ __forceinline__ void lat_normalize(uint32_t act, const bf16* __restri
         const float2 wf = unpack_bf16x2(ws[j]);
         o[j] = pack_bf16x2(__fmul_rn(__fmul_rn(xf.x, rs), wf.x), __fmul_rn(__fmul_rn(xf.y, rs), wf.y));
       }
-      st_shared_v4(act + static_cast<uint32_t>((c >> 3) * kLatActKb) + swz128(r, c & 7),
-                   make_uint4(o[0], o[1], o[2], o[3]));
+      *reinterpret_cast<uint4*>(act + (c >> 3) * kLatActKb + swz128(r, c & 7)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
@@ -157,8 +158,9 @@ __device__ __forceinline__ void lat_red_add(int* ptr, int v) {
 }
 
 // All threads' global stores of this task, then one increment of `counter` (release).
-__device__ __forceinline__ void lat_publish(int* counter) {
-  fence_proxy_async_global();  // the stores may be read by TMA
+// `tma_readers`: the stores are read by TMA (async proxy) in other CTAs.
+__device__ __forceinline__ void lat_publish(int* counter, bool tma_readers) {
+  if (tma_readers) fence_proxy_async_global();
   __syncthreads();
   if (threadIdx.x == 0) {
     lat_fence_gpu();
@@ -175,28 +177,38 @@ __device__ __forceinline__ void lat_reduce(const LatParams& p, const float* part
   const int hi = static_cast<int>(static_cast<long long>(kp + 1) * e4 / kpn);
   const float4* src = reinterpret_cast<const float4*>(part) + static_cast<size_t>(m) * kpn * e4;
   for (int e = lo + static_cast<int>(threadIdx.x); e < hi; e += kLatThreads) {
-    float4 s = __ldcg(src + e);
-#pragma unroll 4
-    for (int q = 1; q < kpn; ++q) {
-      const float4 t = __ldcg(src + static_cast<size_t>(q) * e4 + e);
-      s.x += t.x;
-      s.y += t.y;
-      s.z += t.z;
-      s.w += t.w;
-    }
     const int b = e >> 5, col = m * 128 + (e & 31) * 4;
     bf16* xp = p.x + static_cast<size_t>(b) * p.d + col;
+    // Bias or residual, loaded together with the parts.
+    const uint2 addq =
+        input ? *reinterpret_cast<const uint2*>(p.in_bias + col) : __ldcg(reinterpret_cast<const uint2*>(xp));
+    float4 s = __ldcg(src + e);
+    // Up to 12 parts' loads in flight at once, then added in part order.
+    for (int q0 = 1; q0 < kpn; q0 += 12) {
+      float4 t[12];
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        if (q0 + j < kpn) t[j] = __ldcg(src + static_cast<size_t>(q0 + j) * e4 + e);
+      }
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        if (q0 + j < kpn) {
+          s.x += t[j].x;
+          s.y += t[j].y;
+          s.z += t[j].z;
+          s.w += t[j].w;
+        }
+      }
+    }
     float o[4];
     if (input) {
-      const uint2 bq = *reinterpret_cast<const uint2*>(p.in_bias + col);
-      const float2 b01 = unpack_bf16x2(bq.x), b23 = unpack_bf16x2(bq.y);
+      const float2 b01 = unpack_bf16x2(addq.x), b23 = unpack_bf16x2(addq.y);
       o[0] = __fadd_rn(s.x, b01.x);
       o[1] = __fadd_rn(s.y, b01.y);
       o[2] = __fadd_rn(s.z, b23.x);
       o[3] = __fadd_rn(s.w, b23.y);
     } else {
-      const uint2 xq = __ldcg(reinterpret_cast<const uint2*>(xp));
-      const float2 x01 = unpack_bf16x2(xq.x), x23 = unpack_bf16x2(xq.y);
+      const float2 x01 = unpack_bf16x2(addq.x), x23 = unpack_bf16x2(addq.y);
       o[0] = __fadd_rn(x01.x, bf16_round(s.x));
       o[1] = __fadd_rn(x01.y, bf16_round(s.y));
       o[2] = __fadd_rn(x23.x, bf16_round(s.z));
@@ -327,6 +339,11 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     // 2. gate_up and heads normalise their x rows in shared memory.
     const bool norm = type == kLatGateUp || type == kLatHeads;
     if (norm) {
+      // The norm weights go to shared memory while the x tile lands.
+      const bf16* nw = type == kLatHeads ? p.final_norm : p.norm[layer];
+      if (tid < p.d / 2) {
+        reinterpret_cast<uint32_t*>(smem + kOffNorm)[tid] = __ldg(reinterpret_cast<const uint32_t*>(nw) + tid);
+      }
       if (!mbar_wait(abar, act_phase)) failed = true;
       if (__syncthreads_or(failed)) {
         if (tid == 0) record_error(p.err, kErrTimeoutProducer);
@@ -336,9 +353,10 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
         act_pending = false;
         lat_stamp(p, tr, 2);
       }
-      lat_normalize(act, type == kLatHeads ? p.final_norm : p.norm[layer], p.d, p.eps);
+      lat_normalize(smem + kOffAct, reinterpret_cast<const uint4*>(smem + kOffNorm), p.d, p.eps);
       fence_proxy_async_smem();
       __syncthreads();
+      if (tid == 0) lat_stamp(p, tr, 8);
     }
     // 3. MMAs (one thread): D^T[128 x n] over the task's K range.
     if (tid == 0) {
@@ -363,6 +381,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
         if (ok) ++landed1;
       }
       if (ok) {
+        lat_stamp(p, tr, 9);
         tc_fence_after();
         const uint32_t idesc = idesc_bf16(128, p.n);
         const uint32_t wa = w_base + static_cast<uint32_t>(first) * kLatWSlotBytes;
@@ -393,9 +412,8 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     act_phase ^= 1u;
     if (tid == 0) {
       mma_pending = false;
-      busy &= ~cur_mask;
+      busy &= ~cur_mask;  // the slots this task read are free again (refilled after the epilogue)
       lat_stamp(p, tr, 4);
-      prefetch();  // the slots this task read are free again
     }
     // 4. Epilogue. Warp w reads TMEM lanes 32 * (w % 4).. (output features) and accumulator
     // columns 32 * (w / 4).. (positions).
@@ -415,10 +433,11 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       }
       tc_fence_before();
       int* pc = p.cnt + 2 + (input ? 0 : p.mt) + tile;
-      lat_publish(pc);
+      lat_publish(pc, false);
       // 5. Once every K part of this 128-row block is in, this CTA's share of the sum.
       if (tid == 0) {
         lat_stamp(p, tr, 5);
+        prefetch();
         if (!wait_counter(pc, input ? kpn : (layer + 1) * kpn)) {
           record_error(p.err, kErrTimeoutDependency);
           failed = true;
@@ -428,34 +447,41 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       }
       if (__syncthreads_or(failed)) break;
       lat_reduce(p, part_base, tile, part, kpn, input);
-      lat_publish(p.cnt);
+      lat_publish(p.cnt, true);
       if (tid == 0) lat_stamp(p, tr, 7);
     } else if (type == kLatGateUp) {
       // Lanes 0..63: gate units 64 * tile + lane; lanes 64..127: the matching up units.
-      if (q4 >= 2 && has_cols) {
-        float v[32];
+      // Every warp reads its accumulator columns first; the up warps then hand theirs over.
+      float v[32];
+      if (has_cols) {
         load_acc32(tmem + (static_cast<uint32_t>(32 * q4) << 16) + static_cast<uint32_t>(32 * half), v);
         round_bf16_inplace(v);
+      }
+      if (q4 >= 2 && has_cols) {
         const int u = 32 * (q4 - 2) + lane;
 #pragma unroll
         for (int c = 0; c < 32; ++c) xch[(32 * half + c) * 64 + u] = v[c];
       }
       __syncthreads();
       if (q4 < 2 && has_cols) {
-        float v[32];
-        load_acc32(tmem + (static_cast<uint32_t>(32 * q4) << 16) + static_cast<uint32_t>(32 * half), v);
-        round_bf16_inplace(v);
         const int u = 32 * q4 + lane;
+        float up[32];  // read every up value before the first global store
+#pragma unroll
+        for (int c = 0; c < 32; ++c) up[c] = xch[(32 * half + c) * 64 + u];
         bf16* dst = p.hidden + tile * 64 + u;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const int b = 32 * half + c;
-          if (b < p.n) dst[static_cast<size_t>(b) * p.h] = __float2bfloat16(swiglu_f32(v[c], xch[b * 64 + u]));
+          if (b < p.n) dst[static_cast<size_t>(b) * p.h] = __float2bfloat16(swiglu_f32(v[c], up[c]));
         }
       }
+      if (tid == 0) lat_stamp(p, tr, 6);
       tc_fence_before();
-      lat_publish(p.cnt + 1);
-      if (tid == 0) lat_stamp(p, tr, 5);
+      lat_publish(p.cnt + 1, true);
+      if (tid == 0) {
+        lat_stamp(p, tr, 5);
+        prefetch();
+      }
     } else {
       // Heads: lane = head column tile * 128 + 32 * (w % 4) + lane.
       if (has_cols) {
@@ -468,36 +494,39 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
         for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bias);
         round_bf16_inplace(v);
         if (c0 == p.policy_storage) {
+          // Lanes 0..2 hold the three WDL logits of 32 positions: transpose them through the
+          // exchange area so that lane j takes position 32 * half + j.
+          float* tw = xch + half * 96;
+          if (lane < 3) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int b = 32 * half + j;
-            const float a0 = __shfl_sync(0xffffffffu, v[j], 0);
-            const float a1 = __shfl_sync(0xffffffffu, v[j], 1);
-            const float a2 = __shfl_sync(0xffffffffu, v[j], 2);
-            if (lane == 0 && b < p.batch) {
-              float* w = p.wdl + static_cast<size_t>(b) * 3;
-              if (p.wdl_probs) {
-                const float mx = fmaxf(fmaxf(a0, a1), a2);
-                const float e0 = expf(a0 - mx), e1 = expf(a1 - mx), e2 = expf(a2 - mx);
-                const float total = e0 + e1 + e2;
-                w[0] = e0 / total;
-                w[1] = e1 / total;
-                w[2] = e2 / total;
-              } else {
-                w[0] = a0;
-                w[1] = a1;
-                w[2] = a2;
-              }
+            for (int j = 0; j < 32; ++j) tw[lane * 32 + j] = v[j];
+          }
+          __syncwarp();
+          const int b = 32 * half + lane;
+          const float a0 = tw[lane], a1 = tw[32 + lane], a2 = tw[64 + lane];
+          if (b < p.batch) {
+            float* w = p.wdl + static_cast<size_t>(b) * 3;
+            if (p.wdl_probs) {
+              const float mx = fmaxf(fmaxf(a0, a1), a2);
+              const float e0 = expf(a0 - mx), e1 = expf(a1 - mx), e2 = expf(a2 - mx);
+              const float total = e0 + e1 + e2;
+              w[0] = e0 / total;
+              w[1] = e1 / total;
+              w[2] = e2 / total;
+            } else {
+              w[0] = a0;
+              w[1] = a1;
+              w[2] = a2;
             }
           }
         } else if (c0 == p.policy_storage + 32) {
+          float* tm = xch + 192 + half * 32;
           if (lane == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int b = 32 * half + j;
-              if (b < p.batch) p.moves_left[b] = v[j];
-            }
+            for (int j = 0; j < 32; ++j) tm[j] = v[j];
           }
+          __syncwarp();
+          if (32 * half + lane < p.batch) p.moves_left[32 * half + lane] = tm[lane];
         } else if (c < p.policy_size) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {

@@ -110,7 +110,7 @@ def test_small_batch_evaluate_through_the_c_abi(tmp_path) -> None:
 
     d, depth, batch = 512, 3, 64
     weights = synthetic.make_dense_weights(d_model=d, depth=depth, hidden_dim=3 * d, seed=6)
-    model = DenseChessNet(DenseChessNetConfig(d_model=d, depth=depth, expansion_ratio=3.0))
+    model = DenseChessNet(DenseChessNetConfig(d_model=d, depth=depth, expansion_ratio=3.0, precision="bf16"))
     synthetic.load_into(model, weights)
     path = tmp_path / "m.safetensors"
     export_model(model, path)
