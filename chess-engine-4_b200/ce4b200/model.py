@@ -595,7 +595,7 @@ class _NativeForwardMixin(nn.Module):
     def set_latency_path(self, enabled: bool) -> None:
         """Dense BF16 models with d_model <= 512 run batches of at most 64 positions on the
         small-batch forward (one cooperative launch of transposed tiles spread over the SMs,
-        RMSNorm at the reference's rounding point). ``False`` sends them to the persistent
+        the same folded-RMSNorm arithmetic as the persistent forward). ``False`` sends them to the persistent
         forward instead; the default is ``True``."""
 
         self.__dict__["_latency_path"] = bool(enabled)

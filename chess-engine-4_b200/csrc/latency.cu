@@ -11,11 +11,12 @@
 // layer is spread over ~100 SMs as short tiles:
 //
 //   input   (m, k): partial x^T[m*128.., :] over K part k of the 7168 input columns
-//   gate_up (l, j): hidden[:, 64j..64j+63] = bf16(silu(bf16(n W_g^T)) * bf16(n W_u^T)) with
-//                   n = bf16((x * rsqrt(mean(x^2) + eps)) * w_norm) computed by the CTA
-//                   itself from x (the reference's RMSNorm rounding point)
+//   gate_up (l, j): hidden[:, 64j..64j+63] = bf16(silu(bf16(r * x W'_g^T)) * bf16(r * x W'_u^T))
+//                   with the RMSNorm folded as in the persistent forward: W' = bf16(W * diag(w)),
+//                   r = rsqrt(mean(x^2) + eps) per position, computed by four warps of the CTA
+//                   from its x tile while the MMAs run (so no normalisation pass precedes them)
 //   down    (l, m, k): partial of (hidden . W_d^T)[:, m*128..] over K part k
-//   heads   (t): head columns t*128.. of bf16(n_final . H^T + b), FP32 policy, WDL, moves-left
+//   heads   (t): head columns t*128.. of bf16(r * x H'^T + b), FP32 policy, WDL, moves-left
 //
 // K-split partial sums go to global memory; once all parts of a 128-row block are in
 // (a counter), every part's CTA sums its share of the block in part order (the result does
@@ -47,8 +48,8 @@ constexpr uint32_t kOffW = 0;
 constexpr uint32_t kOffAct = 2 * kLatWSlotBytes;
 constexpr uint32_t kOffXch = kOffAct + kLatMaxRows * kLatMaxD * 2;
 constexpr uint32_t kOffBar = kOffXch + kLatMaxRows * 64 * 4;
-constexpr uint32_t kOffNorm = kOffBar + 64;  // norm weights of the current task [d] BF16
-constexpr int kLatSmemBytes = 1024 + kOffNorm + kLatMaxD * 2;
+constexpr uint32_t kOffRow = kOffBar + 128;  // row scales of the current gate_up / heads task [64]
+constexpr int kLatSmemBytes = 1024 + kOffRow + kLatMaxRows * 4;
 static_assert(kLatSmemBytes <= 232448, "shared memory budget exceeded");
 
 __device__ __forceinline__ void lat_stamp(const LatParams& p, int idx, int slot) {
@@ -106,49 +107,26 @@ __device__ __forceinline__ void lat_issue_weights(const LatParams& p, const int4
   }
 }
 
-// In place: the 64 x d BF16 tile at `act` (d / 64 boxes of [64 rows][128 B] with the 128-byte
-// swizzle) becomes n = bf16((x * rsqrt(mean(x^2) + eps)) * w), row by row (four threads a
-// row, eight columns a chunk).
-__device__ __forceinline__ void lat_normalize(uint8_t* act, const uint4* __restrict__ wq, int d, float eps) {
-  const int r = threadIdx.x >> 2, q = threadIdx.x & 3;
-  const int nch = d / 32;
-  uint4 v[kLatMaxD / 32];
+// r[row] = rsqrt(mean(x^2) + eps) for the 64 rows of the x tile at `act` (d / 64 boxes of
+// [64 rows][128 B] with the 128-byte swizzle), by threads 0..127, two a row.
+__device__ __forceinline__ void lat_row_scale(const uint8_t* act, float* rsm, int d, float eps) {
+  const int r = threadIdx.x >> 1, q = threadIdx.x & 1;
   float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+  for (int k = 0; k < d / 16; ++k) {
+    const int c = q + 2 * k;
+    const uint4 v = *reinterpret_cast<const uint4*>(act + (c >> 3) * kLatActKb + swz128(r, c & 7));
+    const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int k = 0; k < kLatMaxD / 32; ++k) {
-    if (k < nch) {
-      const int c = q + 4 * k;
-      v[k] = *reinterpret_cast<const uint4*>(act + (c >> 3) * kLatActKb + swz128(r, c & 7));
-      const uint32_t wd[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack_bf16x2(wd[j]);
-        ss[j] = fmaf(f.x, f.x, ss[j]);
-        ss[j] = fmaf(f.y, f.y, ss[j]);
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(wd[j]);
+      ss[j] = fmaf(f.x, f.x, ss[j]);
+      ss[j] = fmaf(f.y, f.y, ss[j]);
     }
   }
   float sum = (ss[0] + ss[1]) + (ss[2] + ss[3]);
   sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-  const float rs = rsqrtf(__fdiv_rn(sum, static_cast<float>(d)) + eps);
-#pragma unroll
-  for (int k = 0; k < kLatMaxD / 32; ++k) {
-    if (k < nch) {
-      const int c = q + 4 * k;
-      const uint32_t xs[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-      const uint4 wc = wq[c];
-      const uint32_t ws[4] = {wc.x, wc.y, wc.z, wc.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 xf = unpack_bf16x2(xs[j]);
-        const float2 wf = unpack_bf16x2(ws[j]);
-        o[j] = pack_bf16x2(__fmul_rn(__fmul_rn(xf.x, rs), wf.x), __fmul_rn(__fmul_rn(xf.y, rs), wf.y));
-      }
-      *reinterpret_cast<uint4*>(act + (c >> 3) * kLatActKb + swz128(r, c & 7)) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-  }
+  if (q == 0) rsm[r] = rsqrtf(__fdiv_rn(sum, static_cast<float>(d)) + eps);
 }
 
 __device__ __forceinline__ void lat_fence_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
@@ -157,10 +135,10 @@ __device__ __forceinline__ void lat_red_add(int* ptr, int v) {
   asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 
-// All threads' global stores of this task, then one increment of `counter` (release).
-// `tma_readers`: the stores are read by TMA (async proxy) in other CTAs.
-__device__ __forceinline__ void lat_publish(int* counter, bool tma_readers) {
-  if (tma_readers) fence_proxy_async_global();
+// All threads' global stores of this task, then one increment of `counter` (release). The
+// stores are generic; a reader that loads them with TMA issues fence.proxy.async.global
+// after acquiring the counter, which orders them before its async-proxy reads.
+__device__ __forceinline__ void lat_publish(int* counter) {
   __syncthreads();
   if (threadIdx.x == 0) {
     lat_fence_gpu();
@@ -227,14 +205,22 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
   const uint32_t w_base = base + kOffW;
   const uint32_t act = base + kOffAct;
   float* xch = reinterpret_cast<float*>(smem + kOffXch);  // [row][64 up units]
-  const uint32_t wbar0 = base + kOffBar, wbar1 = wbar0 + 8, abar = wbar0 + 16, mbar = wbar0 + 24;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 32);
+  // Barriers: two weight slots, MMA completion, then one per group of 4 activation k-blocks
+  // (MMAs start on the first group while the second lands; a wait costs ~250 ns, so finer
+  // groups lose).
+  const uint32_t wbar0 = base + kOffBar, wbar1 = wbar0 + 8, mbar = wbar0 + 16, abar0 = wbar0 + 32;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 24);
+  auto abar = [&](int kb) { return abar0 + 8u * static_cast<uint32_t>(kb >> 2); };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // The leader (lane 0 of the last warp) issues every TMA load and MMA and polls the
+  // counters; warps 0..3 compute row scales while it issues a task's MMAs.
+  constexpr int kLead = kLatThreads - 32;
+  float* rsm = reinterpret_cast<float*>(smem + kOffRow);
   if (tid == 0) {
     mbar_init(wbar0, 1);
     mbar_init(wbar1, 1);
-    mbar_init(abar, 1);
+    for (int g = 0; g < kLatMaxD / 256; ++g) mbar_init(abar0 + 8u * g, 1);
     mbar_init(mbar, 1);
     fence_mbar_init();
   }
@@ -260,7 +246,8 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
   uint32_t busy = 0, cur_mask = 0;
   uint32_t issued0 = 0, issued1 = 0, landed0 = 0, landed1 = 0;
   bool act_pending = false, mma_pending = false;
-  uint32_t act_phase = 0, mma_phase = 0;
+  uint32_t act_par = 0, mma_phase = 0;  // act_par bit kb: parity of k-block kb's next phase
+  int act_nkb = 0;
 
   auto prefetch = [&]() {
     while (next_w < ntask) {
@@ -279,7 +266,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     }
   };
 
-  if (tid == 0) {
+  if (tid == kLead) {
     const LatMaps* maps = p.maps;
     tma_prefetch_desc(&maps->a_in);
     tma_prefetch_desc(&maps->x);
@@ -300,7 +287,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     const int kb0 = lat_kb0(p, t);
     const int tr = static_cast<int>(blockIdx.x) * p.max_tasks + i;
     // 1. Inputs ready, then their activation boxes.
-    if (tid == 0) {
+    if (tid == kLead) {
       lat_stamp(p, tr, 0);
       if (p.trace != nullptr && tr < p.trace_cap) {
         p.trace[static_cast<size_t>(tr) * kLatTraceWords + 10] = blockIdx.x;
@@ -328,46 +315,31 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
         lat_stamp(p, tr, 1);
         const LatMaps* maps = p.maps;
         const CUtensorMap* ma = type == kLatInput ? &maps->a_in : (type == kLatDown ? &maps->hidden : &maps->x);
-        mbar_arrive_expect_tx(abar, static_cast<uint32_t>(nkb) * kLatActKb);
         act_pending = true;
+        act_nkb = nkb;
         for (int kb = 0; kb < nkb; ++kb) {
-          tma_load_2d(act + static_cast<uint32_t>(kb) * kLatActKb, ma, abar, (kb0 + kb) * 64, 0);
+          if ((kb & 3) == 0) mbar_arrive_expect_tx(abar(kb), static_cast<uint32_t>(min(4, nkb - kb)) * kLatActKb);
+          tma_load_2d(act + static_cast<uint32_t>(kb) * kLatActKb, ma, abar(kb), (kb0 + kb) * 64, 0);
         }
       }
     }
     if (__syncthreads_or(failed)) break;
     // 2. gate_up and heads normalise their x rows in shared memory.
     const bool norm = type == kLatGateUp || type == kLatHeads;
-    if (norm) {
-      // The norm weights go to shared memory while the x tile lands.
-      const bf16* nw = type == kLatHeads ? p.final_norm : p.norm[layer];
-      if (tid < p.d / 2) {
-        reinterpret_cast<uint32_t*>(smem + kOffNorm)[tid] = __ldg(reinterpret_cast<const uint32_t*>(nw) + tid);
+    if (norm && warp < 4) {
+      // Row scales of the folded RMSNorm (warps 0..3) while the leader issues the MMAs.
+      for (int kb = 0; kb < nkb && !failed; kb += 4) {
+        if (!mbar_wait(abar(kb), (act_par >> (kb >> 2)) & 1u)) {
+          record_error(p.err, kErrTimeoutProducer);
+          failed = true;
+        }
       }
-      if (!mbar_wait(abar, act_phase)) failed = true;
-      if (__syncthreads_or(failed)) {
-        if (tid == 0) record_error(p.err, kErrTimeoutProducer);
-        break;
-      }
-      if (tid == 0) {
-        act_pending = false;
-        lat_stamp(p, tr, 2);
-      }
-      lat_normalize(smem + kOffAct, reinterpret_cast<const uint4*>(smem + kOffNorm), p.d, p.eps);
-      fence_proxy_async_smem();
-      __syncthreads();
+      if (!failed) lat_row_scale(smem + kOffAct, rsm, p.d, p.eps);
       if (tid == 0) lat_stamp(p, tr, 8);
     }
     // 3. MMAs (one thread): D^T[128 x n] over the task's K range.
-    if (tid == 0) {
-      bool ok = true;
-      if (!norm) {
-        ok = mbar_wait(abar, act_phase);
-        if (ok) {
-          act_pending = false;
-          lat_stamp(p, tr, 2);
-        }
-      }
+    if (tid == kLead) {
+      bool ok = true, issued = false;
       const bool both = nkb > kLatMaxKbSlot;
       const int first = both ? 0 : alt_use;
       if (!both) alt_use ^= 1;
@@ -384,19 +356,33 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
         lat_stamp(p, tr, 9);
         tc_fence_after();
         const uint32_t idesc = idesc_bf16(128, p.n);
-        const uint32_t wa = w_base + static_cast<uint32_t>(first) * kLatWSlotBytes;
-        for (int kb = 0; kb < nkb; ++kb) {
-          const uint32_t a = wa + static_cast<uint32_t>(kb) * kLatKbBytes;
-          const uint32_t b = act + static_cast<uint32_t>(kb) * kLatActKb;
+        // Descriptors advance by address / 16 in their low field (every operand lies in the
+        // first 256 KB of shared memory, so the field does not carry).
+        const uint64_t da = sdesc_k128(w_base + static_cast<uint32_t>(first) * kLatWSlotBytes);
+        const uint64_t db = sdesc_k128(act);
+        for (int kb = 0; kb < nkb && ok; ++kb) {
+          if ((kb & 3) == 0) {
+            ok = mbar_wait(abar(kb), (act_par >> (kb >> 2)) & 1u);
+            if (!ok) break;
+            if (kb == 0) lat_stamp(p, tr, 2);
+          }
+          issued = true;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            umma_bf16(tmem, sdesc_k128(a + 32u * k), sdesc_k128(b + 32u * k), idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16(tmem, da + ((kb * kLatKbBytes + 32u * k) >> 4), db + ((kb * kLatActKb + 32u * k) >> 4), idesc,
+                      (kb | k) != 0 ? 1u : 0u);
           }
         }
+      }
+      if (ok) act_pending = false;
+      if (issued) {
+        // Committed also when a later k-block timed out, so that teardown can wait for the
+        // MMAs already issued.
         umma_commit(mbar);
         mma_pending = true;
         lat_stamp(p, tr, 3);
-      } else {
+      }
+      if (!ok) {
         record_error(p.err, kErrTimeoutMma);
         failed = true;
       }
@@ -404,13 +390,13 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     if (__syncthreads_or(failed)) break;
     if (!mbar_wait(mbar, mma_phase)) failed = true;
     if (__syncthreads_or(failed)) {
-      if (tid == 0) record_error(p.err, kErrTimeoutEpilogue);
+      if (tid == kLead) record_error(p.err, kErrTimeoutEpilogue);
       break;
     }
     tc_fence_after();
     mma_phase ^= 1u;
-    act_phase ^= 1u;
-    if (tid == 0) {
+    act_par ^= (1u << ((nkb + 3) >> 2)) - 1u;
+    if (tid == kLead) {
       mma_pending = false;
       busy &= ~cur_mask;  // the slots this task read are free again (refilled after the epilogue)
       lat_stamp(p, tr, 4);
@@ -433,9 +419,9 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       }
       tc_fence_before();
       int* pc = p.cnt + 2 + (input ? 0 : p.mt) + tile;
-      lat_publish(pc, false);
+      lat_publish(pc);
       // 5. Once every K part of this 128-row block is in, this CTA's share of the sum.
-      if (tid == 0) {
+      if (tid == kLead) {
         lat_stamp(p, tr, 5);
         prefetch();
         if (!wait_counter(pc, input ? kpn : (layer + 1) * kpn)) {
@@ -447,38 +433,49 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       }
       if (__syncthreads_or(failed)) break;
       lat_reduce(p, part_base, tile, part, kpn, input);
-      lat_publish(p.cnt, true);
-      if (tid == 0) lat_stamp(p, tr, 7);
+      lat_publish(p.cnt);
+      if (tid == kLead) lat_stamp(p, tr, 7);
     } else if (type == kLatGateUp) {
-      // Lanes 0..63: gate units 64 * tile + lane; lanes 64..127: the matching up units.
-      // Every warp reads its accumulator columns first; the up warps then hand theirs over.
-      float v[32];
+      // Lanes 0..63: gate units 64 * tile + lane; lanes 64..127: the matching up units. Every
+      // warp stages its scaled, rounded accumulator columns in the (consumed) activation area
+      // as G[position][unit] and U[position][unit]; then all 256 threads take 16 units of one
+      // position each, so the SiLU runs on every SM sub-partition and a thread stores 32 B.
+      constexpr int kStride = 68;  // floats a staged row (16-byte aligned, fewer bank conflicts)
+      float* gsm = reinterpret_cast<float*>(smem + kOffAct);
+      float* usm = gsm + kLatMaxRows * kStride;
       if (has_cols) {
+        float v[32];
         load_acc32(tmem + (static_cast<uint32_t>(32 * q4) << 16) + static_cast<uint32_t>(32 * half), v);
-        round_bf16_inplace(v);
-      }
-      if (q4 >= 2 && has_cols) {
-        const int u = 32 * (q4 - 2) + lane;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) xch[(32 * half + c) * 64 + u] = v[c];
+        for (int c = 0; c < 32; ++c) v[c] = __fmul_rn(rsm[32 * half + c], v[c]);  // folded RMSNorm
+        round_bf16_inplace(v);
+        float* dst = (q4 < 2 ? gsm : usm) + 32 * (q4 & 1) + lane;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) dst[(32 * half + c) * kStride] = v[c];
       }
       __syncthreads();
-      if (q4 < 2 && has_cols) {
-        const int u = 32 * q4 + lane;
-        float up[32];  // read every up value before the first global store
+      {
+        const int b = tid >> 2, u0 = (tid & 3) * 16;
+        if (b < p.n) {
+          const float4* g4 = reinterpret_cast<const float4*>(gsm + b * kStride + u0);
+          const float4* u4 = reinterpret_cast<const float4*>(usm + b * kStride + u0);
+          uint32_t o[8];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) up[c] = xch[(32 * half + c) * 64 + u];
-        bf16* dst = p.hidden + tile * 64 + u;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int b = 32 * half + c;
-          if (b < p.n) dst[static_cast<size_t>(b) * p.h] = __float2bfloat16(swiglu_f32(v[c], up[c]));
+          for (int k = 0; k < 4; ++k) {
+            const float4 g = g4[k], u = u4[k];
+            o[2 * k] = pack_bf16x2(swiglu_f32(g.x, u.x), swiglu_f32(g.y, u.y));
+            o[2 * k + 1] = pack_bf16x2(swiglu_f32(g.z, u.z), swiglu_f32(g.w, u.w));
+          }
+          uint4* dst = reinterpret_cast<uint4*>(p.hidden + static_cast<size_t>(b) * p.h + tile * 64 + u0);
+          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
         }
       }
-      if (tid == 0) lat_stamp(p, tr, 6);
+      fence_proxy_async_smem();  // these generic accesses precede the next TMA into the area
+      if (tid == kLead) lat_stamp(p, tr, 6);
       tc_fence_before();
-      lat_publish(p.cnt + 1, true);
-      if (tid == 0) {
+      lat_publish(p.cnt + 1);
+      if (tid == kLead) {
         lat_stamp(p, tr, 5);
         prefetch();
       }
@@ -491,7 +488,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
         const int c = c0 + lane;
         const float bias = c < p.head_cols ? __bfloat162float(p.head_bias[c]) : 0.0f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bias);
+        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(__fmul_rn(v[j], rsm[32 * half + j]), bias);
         round_bf16_inplace(v);
         if (c0 == p.policy_storage) {
           // Lanes 0..2 hold the three WDL logits of 32 positions: transpose them through the
@@ -537,16 +534,16 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       }
       tc_fence_before();
       __syncthreads();
-      if (tid == 0) lat_stamp(p, tr, 5);
+      if (tid == kLead) lat_stamp(p, tr, 5);
     }
   }
 
   // Teardown: let this CTA's own loads and MMAs land (bounded) before its shared and
   // tensor memory are released.
-  if (tid == 0) {
+  if (tid == kLead) {
     while (landed0 < issued0 && mbar_wait(wbar0, landed0 & 1u)) ++landed0;
     while (landed1 < issued1 && mbar_wait(wbar1, landed1 & 1u)) ++landed1;
-    if (act_pending) mbar_wait(abar, act_phase);
+    for (int kb = 0; act_pending && kb < act_nkb; kb += 4) mbar_wait(abar(kb), (act_par >> (kb >> 2)) & 1u);
     if (mma_pending) mbar_wait(mbar, mma_phase);
   }
   tc_fence_before();

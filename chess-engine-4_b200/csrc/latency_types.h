@@ -26,9 +26,10 @@ struct LatMaps {
   CUtensorMap x;       // residual stream [rows, d]
   CUtensorMap hidden;  // [rows, h]
   CUtensorMap w_in;    // input.weight [d, in_dim], box 64 x 128
-  CUtensorMap gate_up[kFwdMaxDepth];  // gate_up.weight [2h, d], box 64 x 64 (gate, up rows)
+  CUtensorMap gate_up[kFwdMaxDepth];  // bf16(gate_up.weight * norm.weight) [2h, d], box 64 x 64
   CUtensorMap down[kFwdMaxDepth];     // down.weight [d, h], box 64 x 128
-  CUtensorMap heads;  // [policy | wdl | moves-left].weight [head_cols, d], box 64 x 128
+  // bf16(final_norm.weight * [policy | wdl | moves-left].weight) [head_cols, d], box 64 x 128
+  CUtensorMap heads;
 };
 
 struct LatParams {
@@ -36,8 +37,6 @@ struct LatParams {
   const int4* tasks;  // [grid][max_tasks] {type, layer, tile, part}; type -1 ends a list
   int max_tasks;
   const __nv_bfloat16* in_bias;              // input.bias [d]
-  const __nv_bfloat16* norm[kFwdMaxDepth];   // blocks.l.norm.weight [d]
-  const __nv_bfloat16* final_norm;           // final_norm.weight [d]
   const __nv_bfloat16* head_bias;            // [head_cols]
   __nv_bfloat16* x;       // [rows_cap, d]
   __nv_bfloat16* hidden;  // [rows_cap, h]

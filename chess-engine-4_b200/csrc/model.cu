@@ -554,10 +554,11 @@ void Model::build_latency() {
   maps.w_in = make_tmap_bf16(w("input.weight"), d, in_dim, in_dim, 128);
   for (int l = 0; l < depth; ++l) {
     const std::string p = "blocks." + std::to_string(l);
-    maps.gate_up[l] = make_tmap_bf16(w(p + ".gate_up.weight"), 2 * h, d, d, 64);
+    // RMSNorm folded into the weight, as in the persistent forward (built just before).
+    maps.gate_up[l] = make_tmap_bf16(fwd_weights + static_cast<size_t>(l) * 2 * h * d, 2 * h, d, d, 64);
     maps.down[l] = make_tmap_bf16(w(p + ".down.weight"), d, h, h, 128);
   }
-  maps.heads = make_tmap_bf16(w("policy.weight"), policy_storage + 64, d, d, 128);
+  maps.heads = make_tmap_bf16(fwd_weights + static_cast<size_t>(depth) * 2 * h * d, policy_storage + 64, d, d, 128);
   // Task lists, each in dependency order (input, layers, heads), so that with every CTA
   // resident no wait can form a cycle.
   std::vector<std::vector<int4>> lists(lat_grid);
@@ -602,8 +603,6 @@ void Model::forward_latency(int layout, void* input, const void* scalars, int ba
   p.tasks = reinterpret_cast<const int4*>(lat_dev + align256(sizeof(LatMaps)));
   p.max_tasks = lat_max_tasks;
   p.in_bias = w("input.bias");
-  for (int l = 0; l < cfg.depth; ++l) p.norm[l] = layers[l].norm;
-  p.final_norm = w("final_norm.weight");
   p.head_bias = w("policy.bias");
   p.x = reinterpret_cast<bf16*>(workspace + ws_off.x);
   p.hidden = reinterpret_cast<bf16*>(workspace + ws_off.hidden);

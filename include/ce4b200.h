@@ -227,8 +227,10 @@ int ce4b_model_task_count(const ce4b_model* model, int batch, int* tasks);
 /* Small-batch forward of dense BF16 models with d_model <= 512: batches of at most 64
  * positions run as one cooperative launch in which every GEMM is computed transposed
  * (weights on the MMA's 128-row side, positions on its N side) and split over most SMs,
- * with RMSNorm at the reference's rounding point (n = bf16(x * rsqrt(mean(x^2)+eps) * w),
- * kernels/src/inference/runtime.cu:182-336). It is the latency path of the lc0 backend's
+ * with the same folded-RMSNorm arithmetic as the persistent forward (the norm weight in
+ * the next linear's weight, the row's rsqrt(mean(x^2)+eps) on the FP32 accumulator;
+ * the reference rounds n = bf16(x * r * w) first, kernels/src/inference/runtime.cu:182-336).
+ * It is the latency path of the lc0 backend's
  * per-search-batch evaluation (third_party/lc0/src/neural/backends/ce4/backend.cc:163-168,
  * Model::Evaluate in kernels/src/inference/runtime.cu:532-564). Enabled by default;
  * enable = 0 sends small batches to the persistent forward instead (for comparisons).

@@ -1,9 +1,9 @@
 """GPU parity of the small-batch dense forward (batches of at most 64 positions, d_model <=
-512): one cooperative launch of transposed tcgen05 tiles spread over the SMs, with RMSNorm
-at the reference's rounding point (n = bf16(x * rsqrt(mean(x^2) + eps) * w) before each
-GEMM, kernels/src/inference/runtime.cu:182-336). Checked against the CPU restatement of
-the reference's BF16 forward (oracle/dense.py, mode="bf16"), against the persistent
-forward of the same model, and for determinism."""
+512): one cooperative launch of transposed tcgen05 tiles spread over the SMs, with the
+persistent forward's folded RMSNorm (W' = bf16(W * diag(w)), the row's rsqrt(mean(x^2) +
+eps) on the FP32 accumulator). Checked against the CPU restatement of the reference's BF16
+forward (oracle/dense.py, mode="bf16": the full contract), against the restatement of the
+folded arithmetic, against the persistent forward of the same model, and for determinism."""
 
 from __future__ import annotations
 
@@ -64,9 +64,10 @@ def test_small_batch_forward_matches_oracle(d: int, depth: int, ratio: float, ba
     mean_folded = float((ours - folded[0]).abs().mean())
     print(f"d{d}x{depth} B={batch}: max {float((ours - ref16[0]).abs().max()):.4g}, mean {mean_ref:.3g} "
           f"(folded restatement {mean_folded:.3g}), argmax raw {raw:.4f}, tolerance-aware {tol_aware:.4f}")
-    # The small-batch path keeps the reference's rounding points: it sits closer to the
-    # reference restatement than to the persistent kernel's folded-norm arithmetic.
-    assert mean_ref <= mean_folded
+    # The kernel computes the folded arithmetic: it sits closer to that restatement than to
+    # the reference's rounding points, and within the logit bar of it.
+    assert mean_folded <= mean_ref
+    assert float((ours - folded[0]).abs().max()) <= POLICY_ATOL
     assert tol_aware >= ARGMAX_AGREEMENT
     torch.testing.assert_close(
         torch.softmax(out.wdl_logits.cpu(), -1), oracle.wdl_probabilities(ref16[1]), atol=WDL_PROB_ATOL, rtol=0
@@ -96,7 +97,9 @@ def test_small_batch_forward_is_deterministic_and_agrees_with_persistent() -> No
     assert not model._native.uses_latency_path(64)
     persistent = model(x.clone())
     torch.cuda.synchronize()
+    # Same arithmetic, different FP32 accumulation order.
     torch.testing.assert_close(persistent.policy_logits, ref[0], atol=POLICY_ATOL, rtol=POLICY_RTOL)
+    print("small-batch vs persistent: max", float((persistent.policy_logits - ref[0]).abs().max()))
     torch.testing.assert_close(
         torch.softmax(persistent.wdl_logits, -1), torch.softmax(ref[1], -1), atol=WDL_PROB_ATOL, rtol=0
     )
