@@ -43,6 +43,9 @@ namespace ce4b {
 namespace {
 
 constexpr uint32_t kLatKbBytes = 128 * 64 * 2;  // one 128-row x 64-column weight k-block
+// gate_up tiles are M = 64 (32 gate + 32 up rows): an N = 64 MMA reads its operands from
+// shared memory, so a 64-row weight tile makes each of its 32 MMAs a third cheaper.
+constexpr int kLatGuRows = 2 * kLatGuUnits;
 constexpr uint32_t kLatActKb = 64 * 64 * 2;     // one 64-row x 64-column activation k-block
 constexpr uint32_t kOffW = 0;
 constexpr uint32_t kOffAct = 2 * kLatWSlotBytes;
@@ -76,26 +79,34 @@ __device__ __forceinline__ int lat_kb0(const LatParams& p, const int4& t) {
   }
 }
 
-// Weights of task t into the slots from `first` on (k-block kb at slot byte kb * 16 KB).
+// Bytes of one weight k-block of a task (M rows x 64 columns).
+__device__ __forceinline__ uint32_t lat_kb_bytes(int type) {
+  return type == kLatGateUp ? kLatGuRows * 64 * 2 : kLatKbBytes;
+}
+
+// Weights of task t into the slots from `first` on (k-block kb at byte kb * lat_kb_bytes).
 __device__ __forceinline__ void lat_issue_weights(const LatParams& p, const int4& t, uint32_t w_base,
                                                   uint32_t wbar0, uint32_t wbar1, int first, int nkb) {
   const LatMaps* maps = p.maps;
-  const int lo = first * kLatMaxKbSlot, hi = lo + nkb;
-  const int in0 = max(0, min(hi, kLatMaxKbSlot) - lo), in1 = max(0, hi - max(lo, kLatMaxKbSlot));
-  if (in0 > 0) mbar_arrive_expect_tx(wbar0, static_cast<uint32_t>(in0) * kLatKbBytes);
-  if (in1 > 0) mbar_arrive_expect_tx(wbar1, static_cast<uint32_t>(in1) * kLatKbBytes);
+  const uint32_t kbb = lat_kb_bytes(t.x);
+  const uint32_t lo = static_cast<uint32_t>(first) * kLatWSlotBytes, hi = lo + static_cast<uint32_t>(nkb) * kbb;
+  const uint32_t slot = kLatWSlotBytes;
+  const uint32_t in0 = hi > lo && lo < slot ? min(hi, slot) - lo : 0u;
+  const uint32_t in1 = hi > slot ? hi - max(lo, slot) : 0u;
+  if (in0 > 0) mbar_arrive_expect_tx(wbar0, in0);
+  if (in1 > 0) mbar_arrive_expect_tx(wbar1, in1);
   const int kb0 = lat_kb0(p, t);
   for (int kb = 0; kb < nkb; ++kb) {
-    const int pos = lo + kb;
-    const uint32_t dst = w_base + static_cast<uint32_t>(kb) * kLatKbBytes;
-    const uint32_t bar = pos < kLatMaxKbSlot ? wbar0 : wbar1;
+    const uint32_t pos = lo + static_cast<uint32_t>(kb) * kbb;
+    const uint32_t dst = w_base + static_cast<uint32_t>(kb) * kbb;
+    const uint32_t bar = pos < slot ? wbar0 : wbar1;
     switch (t.x) {
       case kLatInput:
         tma_load_2d(dst, &maps->w_in, bar, (kb0 + kb) * 64, t.z * 128);
         break;
       case kLatGateUp:
-        tma_load_2d(dst, &maps->gate_up[t.y], bar, kb * 64, t.z * 64);
-        tma_load_2d(dst + kLatKbBytes / 2, &maps->gate_up[t.y], bar, kb * 64, p.h + t.z * 64);
+        tma_load_2d(dst, &maps->gate_up[t.y], bar, kb * 64, t.z * kLatGuUnits);
+        tma_load_2d(dst + kbb / 2, &maps->gate_up[t.y], bar, kb * 64, p.h + t.z * kLatGuUnits);
         break;
       case kLatDown:
         tma_load_2d(dst, &maps->down[t.y], bar, (kb0 + kb) * 64, t.z * 128);
@@ -253,7 +264,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     while (next_w < ntask) {
       const int4 t = list[next_w];
       const int nkb = lat_kb(p, t);
-      const bool both = nkb > kLatMaxKbSlot;
+      const bool both = static_cast<uint32_t>(nkb) * lat_kb_bytes(t.x) > kLatWSlotBytes;
       const int first = both ? 0 : alt_issue;
       const uint32_t mask = both ? 3u : (1u << first);
       if (busy & mask) break;
@@ -340,7 +351,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     // 3. MMAs (one thread): D^T[128 x n] over the task's K range.
     if (tid == kLead) {
       bool ok = true, issued = false;
-      const bool both = nkb > kLatMaxKbSlot;
+      const bool both = static_cast<uint32_t>(nkb) * lat_kb_bytes(type) > kLatWSlotBytes;
       const int first = both ? 0 : alt_use;
       if (!both) alt_use ^= 1;
       cur_mask = both ? 3u : (1u << first);
@@ -355,7 +366,8 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       if (ok) {
         lat_stamp(p, tr, 9);
         tc_fence_after();
-        const uint32_t idesc = idesc_bf16(128, p.n);
+        const uint32_t idesc = idesc_bf16(type == kLatGateUp ? kLatGuRows : 128, p.n);
+        const uint32_t kbb = lat_kb_bytes(type);
         // Descriptors advance by address / 16 in their low field (every operand lies in the
         // first 256 KB of shared memory, so the field does not carry).
         const uint64_t da = sdesc_k128(w_base + static_cast<uint32_t>(first) * kLatWSlotBytes);
@@ -365,11 +377,12 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
             ok = mbar_wait(abar(kb), (act_par >> (kb >> 2)) & 1u);
             if (!ok) break;
             if (kb == 0) lat_stamp(p, tr, 2);
+            if (kb == 4) lat_stamp(p, tr, 7);  // second activation group landed
           }
           issued = true;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            umma_bf16(tmem, da + ((kb * kLatKbBytes + 32u * k) >> 4), db + ((kb * kLatActKb + 32u * k) >> 4), idesc,
+            umma_bf16(tmem, da + ((kb * kbb + 32u * k) >> 4), db + ((kb * kLatActKb + 32u * k) >> 4), idesc,
                       (kb | k) != 0 ? 1u : 0u);
           }
         }
@@ -436,11 +449,12 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       lat_publish(p.cnt);
       if (tid == kLead) lat_stamp(p, tr, 7);
     } else if (type == kLatGateUp) {
-      // Lanes 0..63: gate units 64 * tile + lane; lanes 64..127: the matching up units. Every
-      // warp stages its scaled, rounded accumulator columns in the (consumed) activation area
-      // as G[position][unit] and U[position][unit]; then all 256 threads take 16 units of one
-      // position each, so the SiLU runs on every SM sub-partition and a thread stores 32 B.
-      constexpr int kStride = 68;  // floats a staged row (16-byte aligned, fewer bank conflicts)
+      // M = 64 accumulator: rows 16q..16q+15 sit in lanes 32q..32q+15 of TMEM (lane quarter
+      // q), so quarters 0, 1 hold the 32 gate rows and quarters 2, 3 the 32 matching up rows.
+      // Every warp stages its scaled, rounded columns in the (consumed) activation area as
+      // G[position][unit] and U[position][unit]; then all 256 threads take 8 units of one
+      // position each, so the SiLU runs on every SM sub-partition and a thread stores 16 B.
+      constexpr int kStride = kLatGuUnits + 4;  // floats a staged row (16-byte aligned)
       float* gsm = reinterpret_cast<float*>(smem + kOffAct);
       float* usm = gsm + kLatMaxRows * kStride;
       if (has_cols) {
@@ -449,26 +463,27 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
 #pragma unroll
         for (int c = 0; c < 32; ++c) v[c] = __fmul_rn(rsm[32 * half + c], v[c]);  // folded RMSNorm
         round_bf16_inplace(v);
-        float* dst = (q4 < 2 ? gsm : usm) + 32 * (q4 & 1) + lane;
+        if (lane < 16) {
+          float* dst = (q4 < 2 ? gsm : usm) + 16 * (q4 & 1) + lane;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) dst[(32 * half + c) * kStride] = v[c];
+          for (int c = 0; c < 32; ++c) dst[(32 * half + c) * kStride] = v[c];
+        }
       }
       __syncthreads();
       {
-        const int b = tid >> 2, u0 = (tid & 3) * 16;
+        const int b = tid >> 2, u0 = (tid & 3) * 8;
         if (b < p.n) {
           const float4* g4 = reinterpret_cast<const float4*>(gsm + b * kStride + u0);
           const float4* u4 = reinterpret_cast<const float4*>(usm + b * kStride + u0);
-          uint32_t o[8];
+          uint32_t o[4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
+          for (int k = 0; k < 2; ++k) {
             const float4 g = g4[k], u = u4[k];
             o[2 * k] = pack_bf16x2(swiglu_f32(g.x, u.x), swiglu_f32(g.y, u.y));
             o[2 * k + 1] = pack_bf16x2(swiglu_f32(g.z, u.z), swiglu_f32(g.w, u.w));
           }
-          uint4* dst = reinterpret_cast<uint4*>(p.hidden + static_cast<size_t>(b) * p.h + tile * 64 + u0);
-          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          *reinterpret_cast<uint4*>(p.hidden + static_cast<size_t>(b) * p.h + tile * kLatGuUnits + u0) =
+              make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
       fence_proxy_async_smem();  // these generic accesses precede the next TMA into the area
@@ -557,7 +572,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
 void latency_forward(const LatParams& p, int grid, cudaStream_t s) {
   require(p.maps != nullptr && p.tasks != nullptr && p.max_tasks >= 1 && grid >= 1 && grid <= sm_count() &&
               p.batch >= 1 && p.batch <= kLatMaxRows && p.n % 16 == 0 && p.n >= p.batch && p.n <= kLatMaxRows &&
-              p.d % 128 == 0 && p.d <= kLatMaxD && p.mt == p.d / 128 && p.h % 64 == 0 && p.gt == p.h / 64 &&
+              p.d % 128 == 0 && p.d <= kLatMaxD && p.mt == p.d / 128 && p.h % 64 == 0 && p.gt == p.h / kLatGuUnits &&
               p.depth >= 1 && p.depth <= kFwdMaxDepth && p.kp_in >= 1 && p.kb_in % p.kp_in == 0 &&
               p.kb_in / p.kp_in <= kLatMaxKbSlot && p.kp_dn >= 1 && (p.h / 64) % p.kp_dn == 0 &&
               (p.h / 64) / p.kp_dn <= kLatMaxKbSlot && p.policy_size <= p.policy_storage &&

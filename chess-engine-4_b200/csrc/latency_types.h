@@ -16,6 +16,7 @@ constexpr int kLatWSlotBytes = 64 * 1024;  // one of two weight slots in shared 
 constexpr int kLatMaxKbSlot = kLatWSlotBytes / (128 * 64 * 2);  // 4 k-blocks of a 128-row tile
 constexpr int kLatThreads = 256;
 constexpr int kLatTraceWords = 12;
+constexpr int kLatGuUnits = 32;  // hidden units of a gate_up tile (32 gate + 32 up weight rows)
 
 enum LatTaskType : int { kLatEnd = -1, kLatInput = 0, kLatGateUp = 1, kLatDown = 2, kLatHeads = 3 };
 
@@ -26,7 +27,7 @@ struct LatMaps {
   CUtensorMap x;       // residual stream [rows, d]
   CUtensorMap hidden;  // [rows, h]
   CUtensorMap w_in;    // input.weight [d, in_dim], box 64 x 128
-  CUtensorMap gate_up[kFwdMaxDepth];  // bf16(gate_up.weight * norm.weight) [2h, d], box 64 x 64
+  CUtensorMap gate_up[kFwdMaxDepth];  // bf16(gate_up.weight * norm.weight) [2h, d], box 64 x 32
   CUtensorMap down[kFwdMaxDepth];     // down.weight [d, h], box 64 x 128
   // bf16(final_norm.weight * [policy | wdl | moves-left].weight) [head_cols, d], box 64 x 128
   CUtensorMap heads;
@@ -55,7 +56,7 @@ struct LatParams {
   int kb_in;    // in_dim / 64
   int kp_in;    // K parts of the input GEMM (kb_in / kp_in k-blocks each)
   int kp_dn;    // K parts of each down GEMM
-  int gt;       // gate_up tiles a layer: h / 64
+  int gt;       // gate_up tiles a layer: h / kLatGuUnits
   int ht;       // head tiles: ceil(head_cols / 128)
   int policy_size, policy_storage, head_cols, wdl_probs;
   float eps;

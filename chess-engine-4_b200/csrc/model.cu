@@ -534,7 +534,10 @@ void Model::plan_latency() {
   const int kc_dn = hb % 2 == 0 ? 2 : 1;
   const int kp_dn = hb / kc_dn;
   const int ht = (policy_storage + 64 + 127) / 128;
-  const int layer_ctas = (cfg.depth > 1 ? 2 : 1) * hb + mt * kp_dn + ht;
+  const int gt = h / kLatGuUnits;
+  // Two gate_up sets (even, odd layers); the heads go to the set the last layer leaves idle
+  // when they fit there.
+  const int layer_ctas = 2 * gt + mt * kp_dn + (ht <= gt ? 0 : ht);
   const int grid = std::max(layer_ctas, mt * kp_in);
   if (kp_in == 0 || grid > sms) return;
   lat = true;
@@ -546,7 +549,7 @@ void Model::plan_latency() {
 // Tensor maps and the per-CTA task lists of the small-batch forward (one device buffer).
 void Model::build_latency() {
   const int d = cfg.d_model, h = dense_hidden, depth = cfg.depth;
-  const int mt = d / 128, gt = h / 64, ht = (policy_storage + 64 + 127) / 128;
+  const int mt = d / 128, gt = h / kLatGuUnits, ht = (policy_storage + 64 + 127) / 128;
   LatMaps maps{};
   maps.a_in = make_tmap_bf16(workspace + ws_off.a_in, rows_cap, in_dim, in_dim, 64);
   maps.x = make_tmap_bf16(workspace + ws_off.x, rows_cap, d, d, 64);
@@ -555,7 +558,7 @@ void Model::build_latency() {
   for (int l = 0; l < depth; ++l) {
     const std::string p = "blocks." + std::to_string(l);
     // RMSNorm folded into the weight, as in the persistent forward (built just before).
-    maps.gate_up[l] = make_tmap_bf16(fwd_weights + static_cast<size_t>(l) * 2 * h * d, 2 * h, d, d, 64);
+    maps.gate_up[l] = make_tmap_bf16(fwd_weights + static_cast<size_t>(l) * 2 * h * d, 2 * h, d, d, kLatGuUnits);
     maps.down[l] = make_tmap_bf16(w(p + ".down.weight"), d, h, h, 128);
   }
   maps.heads = make_tmap_bf16(fwd_weights + static_cast<size_t>(depth) * 2 * h * d, policy_storage + 64, d, d, 128);
@@ -566,8 +569,10 @@ void Model::build_latency() {
   for (int m = 0; m < mt; ++m) {
     for (int k = 0; k < lat_kp_in; ++k) lists[lat_grid - n_in + m * lat_kp_in + k].push_back({kLatInput, 0, m, k});
   }
-  const int down0 = (depth > 1 ? 2 : 1) * gt;
-  const int heads0 = down0 + mt * lat_kp_dn;
+  const int down0 = 2 * gt;
+  // Heads on the gate_up set that the last layer does not use (their weights load after its
+  // last gate_up tile), else on CTAs of their own.
+  const int heads0 = ht <= gt ? (depth % 2) * gt : down0 + mt * lat_kp_dn;
   for (int l = 0; l < depth; ++l) {
     for (int j = 0; j < gt; ++j) lists[(l % 2) * gt + j].push_back({kLatGateUp, l, j, 0});
     for (int m = 0; m < mt; ++m) {
@@ -622,7 +627,7 @@ void Model::forward_latency(int layout, void* input, const void* scalars, int ba
   p.kb_in = in_dim / 64;
   p.kp_in = lat_kp_in;
   p.kp_dn = lat_kp_dn;
-  p.gt = dense_hidden / 64;
+  p.gt = dense_hidden / kLatGuUnits;
   p.ht = (policy_storage + 64 + 127) / 128;
   p.policy_size = policy_size;
   p.policy_storage = policy_storage;
