@@ -140,6 +140,21 @@ __device__ __forceinline__ void lat_row_scale(const uint8_t* act, float* rsm, in
   if (q == 0) rsm[r] = rsqrtf(__fdiv_rn(sum, static_cast<float>(d)) + eps);
 }
 
+// This thread's 32 accumulator columns [32 * half, +32) of TMEM lane quarter q: the sum of
+// the two issuers' accumulators (columns 0.. and 64..; the second only when the task had at
+// least two k-blocks, `two`).
+__device__ __forceinline__ void lat_load_acc(uint32_t tmem, int q, int half, bool two, float (&v)[32]) {
+  const uint32_t t = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(32 * half);
+  if (!two) {
+    load_acc32(t, v);
+    return;
+  }
+  float a[32], b[32];
+  load_acc32x2(t, t + 64, a, b);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = a[j] + b[j];
+}
+
 __device__ __forceinline__ void lat_fence_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 __device__ __forceinline__ void lat_red_add(int* ptr, int v) {
@@ -227,16 +242,18 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
   // The leader (lane 0 of the last warp) issues every TMA load and MMA and polls the
   // counters; warps 0..3 compute row scales while it issues a task's MMAs.
   constexpr int kLead = kLatThreads - 32;
+  constexpr int kIssueWarp = kLatThreads / 32 - 2;  // warps 6, 7 issue the MMAs
+  constexpr uint32_t kIssueBarrier = 2;             // named barrier of those two warps
   float* rsm = reinterpret_cast<float*>(smem + kOffRow);
   if (tid == 0) {
     mbar_init(wbar0, 1);
     mbar_init(wbar1, 1);
     for (int g = 0; g < kLatMaxD / 256; ++g) mbar_init(abar0 + 8u * g, 1);
-    mbar_init(mbar, 1);
+    mbar_init(mbar, 2);  // one arrival per MMA issuer
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 64);
+    tmem_alloc(smem_u32(tmem_slot), 128);
     tmem_relinquish();
   }
   __syncwarp();
@@ -348,56 +365,79 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       if (!failed) lat_row_scale(smem + kOffAct, rsm, p.d, p.eps);
       if (tid == 0) lat_stamp(p, tr, 8);
     }
-    // 3. MMAs (one thread): D^T[128 x n] over the task's K range.
-    if (tid == kLead) {
-      bool ok = true, issued = false;
-      const bool both = static_cast<uint32_t>(nkb) * lat_kb_bytes(type) > kLatWSlotBytes;
-      const int first = both ? 0 : alt_use;
-      if (!both) alt_use ^= 1;
-      cur_mask = both ? 3u : (1u << first);
-      if (ok && (cur_mask & 1u)) {
-        ok = mbar_wait(wbar0, landed0 & 1u);
-        if (ok) ++landed0;
-      }
-      if (ok && (cur_mask & 2u)) {
-        ok = mbar_wait(wbar1, landed1 & 1u);
-        if (ok) ++landed1;
-      }
-      if (ok) {
-        lat_stamp(p, tr, 9);
-        tc_fence_after();
-        const uint32_t idesc = idesc_bf16(type == kLatGateUp ? kLatGuRows : 128, p.n);
-        const uint32_t kbb = lat_kb_bytes(type);
-        // Descriptors advance by address / 16 in their low field (every operand lies in the
-        // first 256 KB of shared memory, so the field does not carry).
-        const uint64_t da = sdesc_k128(w_base + static_cast<uint32_t>(first) * kLatWSlotBytes);
-        const uint64_t db = sdesc_k128(act);
-        for (int kb = 0; kb < nkb && ok; ++kb) {
-          if ((kb & 3) == 0) {
-            ok = mbar_wait(abar(kb), (act_par >> (kb >> 2)) & 1u);
-            if (!ok) break;
-            if (kb == 0) lat_stamp(p, tr, 2);
-            if (kb == 4) lat_stamp(p, tr, 7);  // second activation group landed
-          }
-          issued = true;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            umma_bf16(tmem, da + ((kb * kbb + 32u * k) >> 4), db + ((kb * kLatActKb + 32u * k) >> 4), idesc,
-                      (kb | k) != 0 ? 1u : 0u);
-          }
+    // 3. MMAs: D^T[M x n] over the task's K range, issued by two threads (the leader and lane 0
+    // of warp 6), each over half of the k-blocks into its own 64-column accumulator (a
+    // tcgen05.mma of these shapes costs ~60 ns to issue; the epilogue adds the halves).
+    if (warp >= kIssueWarp) {
+      volatile int* mma_go = reinterpret_cast<volatile int*>(smem + kOffBar + 28);
+      if (tid == kLead) {
+        bool ok = true;
+        const bool both = static_cast<uint32_t>(nkb) * lat_kb_bytes(type) > kLatWSlotBytes;
+        const int first = both ? 0 : alt_use;
+        if (!both) alt_use ^= 1;
+        cur_mask = both ? 3u : (1u << first);
+        if (ok && (cur_mask & 1u)) {
+          ok = mbar_wait(wbar0, landed0 & 1u);
+          if (ok) ++landed0;
+        }
+        if (ok && (cur_mask & 2u)) {
+          ok = mbar_wait(wbar1, landed1 & 1u);
+          if (ok) ++landed1;
+        }
+        if (ok) lat_stamp(p, tr, 9);
+        *mma_go = ok ? first : -1;
+        if (!ok) {
+          record_error(p.err, kErrTimeoutMma);
+          failed = true;
         }
       }
-      if (ok) act_pending = false;
-      if (issued) {
-        // Committed also when a later k-block timed out, so that teardown can wait for the
-        // MMAs already issued.
-        umma_commit(mbar);
-        mma_pending = true;
-        lat_stamp(p, tr, 3);
-      }
-      if (!ok) {
-        record_error(p.err, kErrTimeoutMma);
-        failed = true;
+      named_bar_sync(kIssueBarrier, 64);
+      const int first = *mma_go;
+      if (lane == 0) {
+        const bool leader = tid == kLead;
+        const int mid = (nkb + 1) / 2;  // the leader takes k-blocks [0, mid), the other [mid, nkb)
+        const int kb_lo = leader ? 0 : mid, kb_hi = leader ? mid : nkb;
+        bool ok = first >= 0, issued = false;
+        if (ok && kb_lo < kb_hi) {
+          tc_fence_after();
+          const uint32_t idesc = idesc_bf16(type == kLatGateUp ? kLatGuRows : 128, p.n);
+          const uint32_t kbb = lat_kb_bytes(type);
+          // Descriptors advance by address / 16 in their low field (every operand lies in the
+          // first 256 KB of shared memory, so the field does not carry).
+          const uint64_t da = sdesc_k128(w_base + static_cast<uint32_t>(first) * kLatWSlotBytes);
+          const uint64_t db = sdesc_k128(act);
+          const uint32_t acc = tmem + (leader ? 0u : 64u);
+          int waited = -1;
+          for (int kb = kb_lo; kb < kb_hi && ok; ++kb) {
+            if ((kb >> 2) != waited) {
+              waited = kb >> 2;
+              ok = mbar_wait(abar(kb), (act_par >> waited) & 1u);
+              if (!ok) break;
+              if (leader && kb == 0) lat_stamp(p, tr, 2);
+            }
+            issued = true;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              umma_bf16(acc, da + ((kb * kbb + 32u * k) >> 4), db + ((kb * kLatActKb + 32u * k) >> 4), idesc,
+                        (kb != kb_lo || k != 0) ? 1u : 0u);
+            }
+          }
+        }
+        // Each issuer arrives once on the MMA barrier: through a commit when it issued (also
+        // after a later wait timed out, so that the MMAs in flight are waited for), else directly.
+        if (issued) {
+          umma_commit(mbar);
+        } else {
+          mbar_arrive(mbar);
+        }
+        if (leader) {
+          mma_pending = true;
+          lat_stamp(p, tr, 3);
+        }
+        if (first >= 0 && !ok) {
+          record_error(p.err, kErrTimeoutMma);
+          failed = true;
+        }
       }
     }
     if (__syncthreads_or(failed)) break;
@@ -411,6 +451,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     act_par ^= (1u << ((nkb + 3) >> 2)) - 1u;
     if (tid == kLead) {
       mma_pending = false;
+      act_pending = false;  // both issuers waited for every activation group
       busy &= ~cur_mask;  // the slots this task read are free again (refilled after the epilogue)
       lat_stamp(p, tr, 4);
     }
@@ -422,7 +463,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       float* part_base = input ? p.part_in : p.part_dn;
       if (has_cols) {
         float v[32];
-        load_acc32(tmem + (static_cast<uint32_t>(32 * q4) << 16) + static_cast<uint32_t>(32 * half), v);
+        lat_load_acc(tmem, q4, half, nkb >= 2, v);
         float* dst = part_base + (static_cast<size_t>(tile) * kpn + part) * p.n * 128 + 32 * q4 + lane;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -459,7 +500,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       float* usm = gsm + kLatMaxRows * kStride;
       if (has_cols) {
         float v[32];
-        load_acc32(tmem + (static_cast<uint32_t>(32 * q4) << 16) + static_cast<uint32_t>(32 * half), v);
+        lat_load_acc(tmem, q4, half, nkb >= 2, v);
 #pragma unroll
         for (int c = 0; c < 32; ++c) v[c] = __fmul_rn(rsm[32 * half + c], v[c]);  // folded RMSNorm
         round_bf16_inplace(v);
@@ -498,7 +539,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
       // Heads: lane = head column tile * 128 + 32 * (w % 4) + lane.
       if (has_cols) {
         float v[32];
-        load_acc32(tmem + (static_cast<uint32_t>(32 * q4) << 16) + static_cast<uint32_t>(32 * half), v);
+        lat_load_acc(tmem, q4, half, nkb >= 2, v);
         const int c0 = tile * 128 + 32 * q4;  // first head column of this warp
         const int c = c0 + lane;
         const float bias = c < p.head_cols ? __bfloat162float(p.head_bias[c]) : 0.0f;
@@ -564,7 +605,7 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 64);
+  if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
 }  // namespace
