@@ -126,3 +126,23 @@ def test_small_batch_evaluate_through_the_c_abi(tmp_path) -> None:
     assert torch.equal(policy, dev.policy_logits.cpu())
     assert torch.equal(wdl, dev.wdl_logits.cpu())
     assert torch.equal(ml, dev.moves_left.cpu())
+
+
+@pytest.mark.parametrize("hist", [8, 2])
+def test_small_batch_lc0_records_expanded_in_kernel_match_plane_layouts(hist: int) -> None:
+    """lc0 InputPlane records are expanded by the small-batch kernel's input tiles
+    themselves; the other layouts go through the expansion kernel. Both give the same bits
+    (history selection and the rule-50 / 99 included)."""
+
+    from ce4b200 import synthetic
+
+    d, depth, batch = 256, 2, 40
+    weights = synthetic.make_dense_weights(d_model=d, depth=depth, hidden_dim=3 * d, seed=8, history_length=hist)
+    lc0 = synthetic.make_lc0_planes(batch, 13, aux_constant=True)
+    model = dense_model(weights, d=d, depth=depth, ratio=3.0, hist=hist).cuda()
+    a = model(synthetic.lc0_to_dense(lc0).cuda())
+    e = model.forward_lc0(synthetic.lc0_planes_tensor(lc0).cuda(), wdl_probs=False)
+    torch.cuda.synchronize()
+    assert model._native.uses_latency_path(batch)
+    for x, y in ((a.policy_logits, e.policy_logits), (a.wdl_logits, e.wdl_logits), (a.moves_left, e.moves_left)):
+        assert torch.equal(x, y)
