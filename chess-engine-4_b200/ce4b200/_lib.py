@@ -123,6 +123,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ce4b_expert_parallel_plan": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32, ctypes.POINTER(_i32)]),
     "ce4b_model_task_count": (_i32, [_vp, _i32, ctypes.POINTER(_i32)]),
     "ce4b_model_set_latency_path": (_i32, [_vp, _i32]),
+    "ce4b_model_set_direct_io": (_i32, [_vp, _i32]),
     "ce4b_model_uses_latency_path": (_i32, [_vp, _i32, ctypes.POINTER(_i32)]),
     "ce4b_model_set_mxfp8_tap": (_i32, [_vp, ctypes.POINTER(Mxfp8TapStruct)]),
     "ce4b_model_set_routing_tap": (_i32, [_vp, _vp, _i32]),

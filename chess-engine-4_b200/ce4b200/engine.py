@@ -167,6 +167,12 @@ class Engine:
                                                 wdl.data_ptr(), ml.data_ptr()))
         return policy, wdl, ml
 
+    def set_direct_io(self, enabled: bool) -> None:
+        """Copy-free small-batch evaluation of pinned host buffers (on by default): the
+        expansion kernel reads the records and the heads write the outputs in place."""
+
+        _lib.check(self.lib.ce4b_model_set_direct_io(self.handle, 1 if enabled else 0))
+
     def evaluate_async(self, planes: torch.Tensor, out, stream: torch.cuda.Stream) -> None:
         """Enqueues the evaluation on ``stream``; ``planes`` and ``out`` must be pinned and
         stay untouched until the stream reaches this point."""

@@ -329,6 +329,13 @@ int ce4b_model_set_latency_path(ce4b_model* model, int enable) {
   });
 }
 
+int ce4b_model_set_direct_io(ce4b_model* model, int enable) {
+  return guarded([&] {
+    require(model != nullptr && model->impl, "null model");
+    model->impl->direct_io = enable != 0;
+  });
+}
+
 int ce4b_model_uses_latency_path(const ce4b_model* model, int batch, int* uses) {
   return guarded([&] {
     require(model != nullptr && model->impl && uses != nullptr, "null argument");

@@ -25,6 +25,9 @@ constexpr int kExpandPer = 4;
 __global__ void expand_lc0_kernel(const ce4b_input_plane* __restrict__ planes, bf16* __restrict__ out,
                                   int batch, int history) {
   static_assert(sizeof(ce4b_input_plane) == 16, "InputPlane is 16 bytes");
+  // The forward kernel after it may start its prologue now; it waits for this grid's
+  // completion before reading the planes.
+  grid_launch_dependents();
   const int sel = selected_planes(history);
   const int hp = history * kPlanesPerHistory;
   const int nchunk = sel * 8;
@@ -66,6 +69,7 @@ __global__ void expand_lc0_kernel(const ce4b_input_plane* __restrict__ planes, b
 template <typename T>
 __global__ void expand_dense_kernel(T* __restrict__ planes, bf16* __restrict__ out, int batch,
                                     int history, int write_back) {
+  grid_launch_dependents();
   const int sel = selected_planes(history);
   const int hp = history * kPlanesPerHistory;
   for (int64_t b = blockIdx.x; b < batch; b += gridDim.x)
@@ -112,6 +116,7 @@ __global__ void expand_dense_kernel(T* __restrict__ planes, bf16* __restrict__ o
 template <typename S>
 __global__ void expand_packed_kernel(const uint8_t* __restrict__ packed, const S* __restrict__ scalars,
                                      bf16* __restrict__ out, int batch, int history) {
+  grid_launch_dependents();
   const int sel = selected_planes(history);
   const int hp = history * kPlanesPerHistory;
   for (int64_t b = blockIdx.x; b < batch; b += gridDim.x)

@@ -161,6 +161,12 @@ __device__ __forceinline__ void lat_red_add(int* ptr, int v) {
   asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ int lat_atom_add(int* ptr, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+  return old;
+}
+
 // All threads' global stores of this task, then one increment of `counter` (release). The
 // stores are generic; a reader that loads them with TMA issues fence.proxy.async.global
 // after acquiring the counter, which orders them before its async-proxy reads.
@@ -301,6 +307,9 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
     tma_prefetch_desc(&maps->hidden);
     prefetch();
   }
+  // Everything above reads only what finalize wrote (weights, maps, task lists), so with a
+  // programmatic launch it overlaps the plane expansion; the tasks read its output.
+  grid_dependency_wait();
 
   const int q4 = warp & 3;     // TMEM lane quarter of this warp
   const int half = warp >> 2;  // accumulator columns [32 * half, +32)
@@ -606,6 +615,15 @@ __global__ void __launch_bounds__(kLatThreads, 1) latency_forward_kernel(const _
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, 128);
+  // The last CTA out zeroes the counters for the next launch (every CTA's counter accesses
+  // precede its arrival here), so no reset runs before the kernel.
+  if (tid == 0) {
+    const int exit_idx = 2 + 2 * p.mt;
+    lat_fence_gpu();
+    if (lat_atom_add(p.cnt + exit_idx, 1) == static_cast<int>(gridDim.x) - 1) {
+      for (int i = 0; i <= exit_idx; ++i) reinterpret_cast<volatile int*>(p.cnt)[i] = 0;
+    }
+  }
 }
 
 }  // namespace
@@ -641,10 +659,36 @@ void latency_forward(const LatParams& p, int grid, cudaStream_t s) {
   cfg.dynamicSmemBytes = kLatSmemBytes;
   cfg.stream = s;
   // Cooperative: every CTA is resident at once (CTAs wait on counters other CTAs publish).
-  cudaLaunchAttribute attr[1];
+  // Programmatic: the prologue and the first weight loads may run under the expansion
+  // kernel before it (the kernel waits for it before its tasks). If the driver refuses the
+  // pair of attributes, the launch is repeated cooperative only, and remembered per device.
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
+  static std::mutex pdl_mu;
+  static std::set<int> pdl_refused;
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  bool pdl = false;
+  {
+    std::lock_guard<std::mutex> lock(pdl_mu);
+    pdl = !pdl_refused.count(dev);
+  }
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  check_cuda(cudaStreamIsCapturing(s, &capture), "query stream capture");
+  if (pdl) {
+    cfg.numAttrs = 2;
+    const cudaError_t st = cudaLaunchKernelEx(&cfg, latency_forward_kernel, p);
+    if (st == cudaSuccess) return;
+    // A refusal under stream capture invalidates the capture: report it as it is.
+    if (capture != cudaStreamCaptureStatusNone) check_cuda(st, "small-batch forward launch");
+    (void)cudaGetLastError();
+    std::lock_guard<std::mutex> lock(pdl_mu);
+    pdl_refused.insert(dev);
+  }
   cfg.numAttrs = 1;
   check_cuda(cudaLaunchKernelEx(&cfg, latency_forward_kernel, p), "small-batch forward launch");
 }

@@ -44,7 +44,8 @@ struct LatParams {
   float* part_in;         // [d / 128][kp_in][n][128] FP32 partial sums of the input GEMM
   float* part_dn;         // [d / 128][kp_dn][n][128] of each layer's down GEMM
   int* cnt;               // [0] x slices ready, [1] hidden tiles ready, [2 + m] input and
-                          // [2 + mt + m] down partial tiles of 128-row block m
+                          // [2 + mt + m] down partial tiles of 128-row block m, [2 + 2 mt]
+                          // CTAs finished (zero at launch; the last CTA zeroes them all)
   int* err;
   float* policy;
   float* wdl;

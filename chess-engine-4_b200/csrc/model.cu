@@ -45,7 +45,7 @@ std::string shape_str(const std::vector<int64_t>& s) {
 Model::~Model() {
   if (device >= 0) cudaSetDevice(device);
   disable_expert_parallel();
-  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  graphs_clear();
   if (fwd_dev) cudaFree(fwd_dev);
   if (fwd_weights) cudaFree(fwd_weights);
   if (lat_dev) cudaFree(lat_dev);
@@ -143,11 +143,12 @@ void Model::plan_workspace() {
   }
   if (lat) {
     // FP32 partial tiles [d / 128][K parts][64 positions][128] of the input and down GEMMs,
-    // and the counters (x ready, hidden ready, one per 128-row block for each GEMM).
+    // and the counters (x ready, hidden ready, one per 128-row block for each GEMM, CTAs
+    // finished).
     const size_t mt = static_cast<size_t>(d / 128);
     ws_off.lat_part_in = take(mt * lat_kp_in * kLatMaxRows * 128 * 4);
     ws_off.lat_part_dn = take(mt * lat_kp_dn * kLatMaxRows * 128 * 4);
-    lat_sync_bytes = (2 + 2 * mt) * 4;
+    lat_sync_bytes = (3 + 2 * mt) * 4;  // + the exit counter (the last CTA out zeroes all)
     ws_off.lat_sync = take(lat_sync_bytes);
   }
   if (cfg.arch == CE4B_ARCH_MOE64A2) {
@@ -332,8 +333,7 @@ void Model::finalize() {
   }
   if (lat) build_latency();
   if (mx) quantize_weights();
-  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
-  graphs.clear();
+  graphs_clear();
   finalized = true;
 }
 
@@ -598,8 +598,9 @@ void Model::build_latency() {
 void Model::forward_latency(int layout, void* input, const void* scalars, int batch, float* policy,
                             float* wdl, float* moves_left, int wdl_probs, int write_back, cudaStream_t s) {
   const int d = cfg.d_model;
+  // The counters are zero: from the workspace reset at create, then from the last CTA of
+  // each launch.
   auto* sync = reinterpret_cast<int*>(workspace + ws_off.lat_sync);
-  check_cuda(cudaMemsetAsync(sync, 0, lat_sync_bytes, s), "reset small-batch counters");
   expand_input(layout, input, scalars, batch, cfg.history_length,
                reinterpret_cast<bf16*>(workspace + ws_off.a_in), write_back, s);
   trace("expand_planes", s);
@@ -760,6 +761,39 @@ void Model::trace(const char* label, cudaStream_t s) {
   trace_labels.emplace_back(label);
 }
 
+cudaGraphExec_t Model::capture_evaluate(const ce4b_input_plane* planes, int batch, float* pol,
+                                        float* wdl, float* ml) {
+  const std::vector<cudaEvent_t> saved = std::move(trace_events);
+  trace_events.clear();
+  cudaGraphExec_t exec = nullptr;
+  try {
+    check_cuda(cudaStreamWaitEvent(stream, forward_done, 0), "wait previous forward");
+    forward(CE4B_INPUT_LC0, const_cast<ce4b_input_plane*>(planes), nullptr, batch, pol, wdl, ml, 1, 0,
+            nullptr, stream);
+    check_cuda(cudaStreamSynchronize(stream), "warm-up forward");
+    check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      forward(CE4B_INPUT_LC0, const_cast<ce4b_input_plane*>(planes), nullptr, batch, pol, wdl, ml, 1, 0,
+              nullptr, stream);
+    } catch (...) {
+      cudaGraph_t g = nullptr;
+      cudaStreamEndCapture(stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    cudaGraph_t graph = nullptr;
+    check_cuda(cudaStreamEndCapture(stream, &graph), "end capture");
+    const cudaError_t st = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    check_cuda(st, "instantiate graph");
+  } catch (...) {
+    trace_events = saved;
+    throw;
+  }
+  trace_events = saved;
+  return exec;
+}
+
 cudaGraphExec_t Model::evaluate_graph(int batch, int slot) {
   IoSlot& io_slot = io[slot];
   auto* planes = reinterpret_cast<ce4b_input_plane*>(workspace + io_slot.planes);
@@ -769,37 +803,53 @@ cudaGraphExec_t Model::evaluate_graph(int batch, int slot) {
   const int key = batch * kIoSlots + slot;
   auto it = graphs.find(key);
   if (it != graphs.end()) return it->second;
-  // First use of this batch size and slot: run once outside a capture (kernel
-  // attributes), then capture the forward into a graph on the internal stream. Blocks.
-  const std::vector<cudaEvent_t> saved = std::move(trace_events);
-  trace_events.clear();
-  try {
-    check_cuda(cudaStreamWaitEvent(stream, forward_done, 0), "wait previous forward");
-    check_cuda(cudaStreamWaitEvent(stream, io_slot.free, 0), "wait I/O slot");
-    forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
-    check_cuda(cudaStreamSynchronize(stream), "warm-up forward");
-    check_cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
-    try {
-      forward(CE4B_INPUT_LC0, planes, nullptr, batch, pol, wdl, ml, 1, 0, nullptr, stream);
-    } catch (...) {
-      cudaGraph_t g = nullptr;
-      cudaStreamEndCapture(stream, &g);
-      if (g) cudaGraphDestroy(g);
-      throw;
+  // First use of this batch size and slot (the slot's earlier copies are done first).
+  check_cuda(cudaStreamWaitEvent(stream, io_slot.free, 0), "wait I/O slot");
+  return graphs.emplace(key, capture_evaluate(planes, batch, pol, wdl, ml)).first->second;
+}
+
+namespace {
+
+// The device address of host buffer [ptr, ptr + bytes) when it is pinned and mapped for the
+// current device over its whole extent (its first and last byte resolve to device
+// addresses the same distance apart), else nullptr.
+void* mapped_view(const void* ptr, size_t bytes) {
+  auto view = [](const void* p) -> char* {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return nullptr;
     }
-    cudaGraph_t graph = nullptr;
-    check_cuda(cudaStreamEndCapture(stream, &graph), "end capture");
-    cudaGraphExec_t exec = nullptr;
-    const cudaError_t st = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    check_cuda(st, "instantiate graph");
-    it = graphs.emplace(key, exec).first;
-  } catch (...) {
-    trace_events = saved;
-    throw;
+    return a.type == cudaMemoryTypeHost ? static_cast<char*>(a.devicePointer) : nullptr;
+  };
+  if (ptr == nullptr || bytes == 0) return nullptr;
+  char* first = view(ptr);
+  char* last = view(static_cast<const char*>(ptr) + bytes - 1);
+  if (first == nullptr || last == nullptr || last - first != static_cast<ptrdiff_t>(bytes - 1)) return nullptr;
+  return first;
+}
+
+}  // namespace
+
+cudaGraphExec_t Model::direct_graph(const ce4b_input_plane* host_planes, int batch, float* host_policy,
+                                    float* host_wdl, float* host_moves_left) {
+  if (!latency_path(batch)) return nullptr;
+  const size_t b = static_cast<size_t>(batch);
+  auto* planes = static_cast<ce4b_input_plane*>(mapped_view(host_planes, b * kInputPlanes * sizeof(ce4b_input_plane)));
+  auto* pol = static_cast<float*>(mapped_view(host_policy, b * policy_size * 4));
+  auto* wdl = static_cast<float*>(mapped_view(host_wdl, b * 3 * 4));
+  auto* ml = static_cast<float*>(mapped_view(host_moves_left, b * 4));
+  if (planes == nullptr || pol == nullptr || wdl == nullptr || ml == nullptr) return nullptr;
+  const std::array<uintptr_t, 5> key{static_cast<uintptr_t>(batch), reinterpret_cast<uintptr_t>(planes),
+                                     reinterpret_cast<uintptr_t>(pol), reinterpret_cast<uintptr_t>(wdl),
+                                     reinterpret_cast<uintptr_t>(ml)};
+  auto it = direct_graphs.find(key);
+  if (it != direct_graphs.end()) return it->second;
+  if (direct_graphs.size() >= kDirectGraphs) {
+    for (auto& kv : direct_graphs) cudaGraphExecDestroy(kv.second);
+    direct_graphs.clear();
   }
-  trace_events = saved;
-  return it->second;
+  return direct_graphs.emplace(key, capture_evaluate(planes, batch, pol, wdl, ml)).first->second;
 }
 
 void Model::enqueue_evaluate_legal(const ce4b_input_plane* host_planes, int batch,
@@ -870,6 +920,15 @@ void Model::enqueue_evaluate(const ce4b_input_plane* host_planes, int batch, flo
   require(batch >= 1 && batch <= max_batch, "batch size exceeds model capacity");
   require(host_planes && host_policy && host_wdl && host_moves_left, "null host buffer");
   check_cuda(cudaSetDevice(device), "cudaSetDevice");
+  if (direct_io) {
+    cudaGraphExec_t direct = direct_graph(host_planes, batch, host_policy, host_wdl, host_moves_left);
+    if (direct != nullptr) {
+      check_cuda(cudaStreamWaitEvent(s, forward_done, 0), "wait previous forward");
+      check_cuda(cudaGraphLaunch(direct, s), "launch graph");
+      check_cuda(cudaEventRecord(forward_done, s), "record forward");
+      return;
+    }
+  }
   const int slot = static_cast<int>(io_next % kIoSlots);
   IoSlot& io_slot = io[slot];
   auto* planes = reinterpret_cast<ce4b_input_plane*>(workspace + io_slot.planes);

@@ -2,6 +2,8 @@
 #pragma once
 
 #include <algorithm>
+#include <array>
+#include <cstdint>
 #include <map>
 #include <memory>
 #include <string>
@@ -158,6 +160,21 @@ struct Model {
   unsigned io_next = 0;
   cudaEvent_t forward_done = nullptr;
   std::map<int, cudaGraphExec_t> graphs;  // key: batch * kIoSlots + slot
+  // Small-batch evaluations whose host buffers are pinned and mapped (device-accessible)
+  // run without copies: the expansion kernel reads the records from host memory and the
+  // heads write policy, WDL and moves-left into the caller's buffers. One graph per
+  // (batch, buffers), at most kDirectGraphs of them (the set is dropped when full).
+  static constexpr size_t kDirectGraphs = 16;
+  bool direct_io = true;  // ce4b_model_set_direct_io
+  std::map<std::array<uintptr_t, 5>, cudaGraphExec_t> direct_graphs;
+  // Captures forward() of an lc0 batch with the given device-visible pointers on the
+  // internal stream (run once outside the capture first, for kernel attributes). Blocks.
+  cudaGraphExec_t capture_evaluate(const ce4b_input_plane* planes, int batch, float* policy,
+                                   float* wdl, float* moves_left);
+  // The direct graph for these host buffers, or nullptr when they are not all pinned and
+  // mapped over their whole extent or the batch does not take the small-batch forward.
+  cudaGraphExec_t direct_graph(const ce4b_input_plane* host_planes, int batch, float* host_policy,
+                               float* host_wdl, float* host_moves_left);
   // Optional per-kernel trace: an event is recorded after each kernel of forward().
   std::vector<cudaEvent_t> trace_events;
   std::vector<std::string> trace_labels;
@@ -225,6 +242,8 @@ struct Model {
   void graphs_clear() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     graphs.clear();
+    for (auto& kv : direct_graphs) cudaGraphExecDestroy(kv.second);
+    direct_graphs.clear();
   }
   void moe_layer(const Layer& L, int moe_index, const bf16* next_norm, int batch,
                  int32_t* tokens_per_expert, cudaStream_t s);

@@ -141,14 +141,25 @@ int ce4b_model_forward(ce4b_model* model, int input_layout, void* input_dev,
 
 /* Host-buffer evaluation, blocking: H2D of the planes, forward (CUDA graph per batch
  * size), D2H of policy [B, policy_size], WDL probabilities [B, 3], moves-left [B].
- * Mirrors Model::Evaluate (kernels/src/inference/runtime.cu:532-564). */
+ * Mirrors Model::Evaluate (kernels/src/inference/runtime.cu:532-564).
+ * Batches that take the small-batch forward skip the copies when all four host buffers are
+ * pinned and mapped for the model's device over their whole extent (cudaHostAlloc, or
+ * cudaHostRegister with mapping; e.g. torch pin_memory): the expansion kernel reads the
+ * records from host memory and the heads write the outputs into the caller's buffers
+ * (one CUDA graph per batch size and buffer set, built on first use, which blocks).
+ * Results are identical either way. Other buffers take the copy path. */
 int ce4b_model_evaluate(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
                         float* host_policy, float* host_wdl, float* host_moves_left);
 
+/* Turns the copy-free evaluation of pinned host buffers above on (default) or off
+ * (enable = 0: every evaluation copies through device buffers). */
+int ce4b_model_set_direct_io(ce4b_model* model, int enable);
+
 /* Asynchronous form of ce4b_model_evaluate on `stream`: enqueues the H2D copy, the
- * graph and the D2H copies and returns. Host buffers must stay valid (and should be
- * pinned) until the stream reaches that point. The first call for a batch size builds
- * its graphs and blocks.
+ * graph and the D2H copies (or, for pinned buffers of a small batch, the copy-free graph)
+ * and returns. Host buffers must stay valid and untouched (and should be pinned) until the
+ * stream reaches that point. The first call for a batch size (and, copy-free, for a
+ * buffer set) builds its graph and blocks.
  * The model owns two device I/O slots used in turn. Consecutive calls on different
  * streams overlap: a call's H2D copy and the previous call's D2H copies run while a
  * forward computes. Forwards of one model never overlap one another (each waits for the

@@ -107,32 +107,48 @@ def test_small_batch_forward_is_deterministic_and_agrees_with_persistent() -> No
 
 def test_small_batch_evaluate_through_the_c_abi(tmp_path) -> None:
     """lc0 InputPlane records through ce4b_model_evaluate (graph-captured forward, host
-    buffers) at the latency batch equal the device forward of the same records."""
+    buffers) at small batches equal the device forward of the same records, through the
+    copy path (pageable buffers, or direct I/O off) and through the copy-free path (pinned
+    buffers: the kernels read the records and write the outputs in host memory)."""
 
-    from ce4b200 import DenseChessNet, DenseChessNetConfig, Engine, export_model, synthetic
+    from ce4b200 import DenseChessNet, DenseChessNetConfig, Engine, _lib, export_model, synthetic
 
-    d, depth, batch = 512, 3, 64
+    d, depth = 512, 3
     weights = synthetic.make_dense_weights(d_model=d, depth=depth, hidden_dim=3 * d, seed=6)
     model = DenseChessNet(DenseChessNetConfig(d_model=d, depth=depth, expansion_ratio=3.0, precision="bf16"))
     synthetic.load_into(model, weights)
     path = tmp_path / "m.safetensors"
     export_model(model, path)
     engine = Engine.load(path, gpu=0, max_batch=256)
-    lc0 = synthetic.lc0_planes_tensor(synthetic.make_lc0_planes(batch, 7))
-    for _ in range(2):
-        policy, wdl, ml = engine.evaluate(lc0)
-    dev = model.cuda().forward_lc0(lc0.cuda())
-    torch.cuda.synchronize()
-    assert torch.equal(policy, dev.policy_logits.cpu())
-    assert torch.equal(wdl, dev.wdl_logits.cpu())
-    assert torch.equal(ml, dev.moves_left.cpu())
+    dm = model.cuda()
+    for batch in (64, 23):
+        lc0 = synthetic.lc0_planes_tensor(synthetic.make_lc0_planes(batch, 7 + batch))
+        dev = dm.forward_lc0(lc0.cuda())
+        torch.cuda.synchronize()
+        expect = (dev.policy_logits.cpu(), dev.wdl_logits.cpu(), dev.moves_left.cpu())
+        pinned_in = lc0.pin_memory()
+        runs = []
+        for direct in (True, False):
+            engine.set_direct_io(direct)
+            runs.append(engine.evaluate(lc0))  # pageable: copies
+            for _ in range(2):
+                out = engine.outputs(batch, pin=True)
+                runs.append(engine.evaluate(pinned_in, out))  # pinned: copy-free when direct
+            out = engine.outputs(batch, pin=True)
+            for _ in range(3):  # the same buffers again (cached graph), then reset outputs
+                for t in out:
+                    t.fill_(float("nan"))
+                runs.append(engine.evaluate(pinned_in, out))
+        for got in runs:
+            for x, y in zip(got, expect):
+                assert torch.equal(x, y)
+    assert _lib.check_device_error(0) == 0
 
 
 @pytest.mark.parametrize("hist", [8, 2])
 def test_small_batch_lc0_records_expanded_in_kernel_match_plane_layouts(hist: int) -> None:
-    """lc0 InputPlane records are expanded by the small-batch kernel's input tiles
-    themselves; the other layouts go through the expansion kernel. Both give the same bits
-    (history selection and the rule-50 / 99 included)."""
+    """lc0 InputPlane records and dense planes of the same positions give the same bits at
+    a small batch (history selection and the rule-50 / 99 included)."""
 
     from ce4b200 import synthetic
 
