@@ -461,12 +461,14 @@ void Model::moe_layer_ep(const Layer& L, int moe_index, const bf16* next_norm, i
   check_cuda(cudaGetLastError(), "ep_publish_meta launch");
   ep_plan_kernel<<<1, 32, 0, s>>>(dv);
   check_cuda(cudaGetLastError(), "ep_plan launch");
+  trace("ep_counts_plan", s);
   const int copy_grid = std::max(1, std::min(4 * sm_count(), (batch * 2 * (d / 8) + 255) / 256));
   ep_push_rows_kernel<<<copy_grid, 256, 0, s>>>(dv, xperm, pprob, expert_start);
   check_cuda(cudaGetLastError(), "ep_push_rows launch");
+  trace("ep_push_rows", s);
   ep_wait_kernel<<<1, 32, 0, s>>>(dv, kPhaseRows);
   check_cuda(cudaGetLastError(), "ep_wait launch");
-  trace("moe_dispatch_exchange", s);
+  trace("ep_wait_rows", s);
 
   auto* ep_p = reinterpret_cast<float*>(ep_buf + ep_off.p);
   gemm_grouped_swiglu(tm_ep_x, L.tm_gate_up, tm_ep_h, dv.tiles, dv.num_tiles, he, d, s);
@@ -476,9 +478,10 @@ void Model::moe_layer_ep(const Layer& L, int moe_index, const bf16* next_norm, i
 
   ep_push_results_kernel<<<copy_grid, 256, 0, s>>>(dv, reinterpret_cast<const bf16*>(ep_buf + ep_off.y));
   check_cuda(cudaGetLastError(), "ep_push_results launch");
+  trace("ep_push_results", s);
   ep_wait_kernel<<<1, 32, 0, s>>>(dv, kPhaseResults);
   check_cuda(cudaGetLastError(), "ep_wait launch");
-  trace("moe_combine_exchange", s);
+  trace("ep_wait_results", s);
   moe_combine_norm(x, reinterpret_cast<const bf16*>(ep_buf + ep_off.ret), route_pos, next_norm, n, batch, d,
                    cfg.rms_norm_eps, s);
   trace("moe_combine_rmsnorm", s);
