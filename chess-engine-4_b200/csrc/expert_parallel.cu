@@ -95,8 +95,9 @@ __device__ __forceinline__ bool wait_flags(const EpDev& dv, int phase, unsigned 
   return true;
 }
 
-// 2. Counts into every rank's inbox, then the meta flags. One CTA of 64 threads.
-__global__ void ep_publish_meta_kernel(EpDev dv, const int* __restrict__ counts) {
+// 2 + 3. Counts into every rank's inbox and the meta flags, then (thread 0) the device-side
+// plan once every rank's counts are in. One CTA of 64 threads.
+__global__ void ep_counts_plan_kernel(EpDev dv, const int* __restrict__ counts) {
   __shared__ unsigned epoch_s;
   const int e = threadIdx.x;
   if (e == 0) epoch_s = *dv.epoch + 1u;
@@ -106,19 +107,13 @@ __global__ void ep_publish_meta_kernel(EpDev dv, const int* __restrict__ counts)
   for (int r = 0; r < dv.world; ++r) {
     reinterpret_cast<volatile int*>(dv.peer[r] + dv.off_meta)[dv.rank * kExperts + e] = c;
   }
-  fence_acq_rel_sys();
+  // The barrier orders every thread's count stores before thread 0's system-scope fence,
+  // which orders them before the flags.
   __syncthreads();
-  if (e == 0) {
-    *dv.epoch = epoch;
-    fence_acq_rel_sys();
-    for (int r = 0; r < dv.world; ++r) st_release_sys(flag_ptr(dv, r, kPhaseMeta, dv.rank), epoch);
-  }
-}
-
-// 3. Device-side plan (one thread) once every rank's counts are in.
-__global__ void ep_plan_kernel(EpDev dv) {
-  if (threadIdx.x != 0) return;
-  const unsigned epoch = *dv.epoch;
+  if (e != 0) return;
+  *dv.epoch = epoch;
+  fence_acq_rel_sys();
+  for (int r = 0; r < dv.world; ++r) st_release_sys(flag_ptr(dv, r, kPhaseMeta, dv.rank), epoch);
   if (!wait_flags(dv, kPhaseMeta, epoch)) {
     record_error(dv.err, kErrTimeoutPeer);
     *dv.num_tiles = 0;
@@ -163,6 +158,7 @@ __global__ void ep_plan_kernel(EpDev dv) {
   *dv.num_tiles = nt;
 }
 
+
 // Copies `rows` rows of d BF16 (and optionally one float each) with 16-byte stores,
 // grid-strided.
 __device__ __forceinline__ void copy_rows(bf16* dst, const bf16* src, float* dst_p, const float* src_p, int rows,
@@ -181,12 +177,12 @@ __device__ __forceinline__ void copy_rows(bf16* dst, const bf16* src, float* dst
   }
 }
 
-// The last CTA to finish raises the phase's flag on the given ranks (every thread fenced its
-// own stores at system scope before the count).
+// The last CTA to finish raises the phase's flag on the given ranks. The barrier orders the
+// CTA's stores before thread 0's system-scope fence, which orders them before its count.
 __device__ __forceinline__ void finish_push(const EpDev& dv, int counter, int phase, bool to_all) {
-  fence_acq_rel_sys();
   __syncthreads();
   if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
     const int old = atomicAdd(dv.done + counter, 1);
     if (old == static_cast<int>(gridDim.x) - 1) {
       dv.done[counter] = 0;
@@ -457,10 +453,8 @@ void Model::moe_layer_ep(const Layer& L, int moe_index, const bf16* next_norm, i
                                cudaMemcpyDeviceToDevice, s),
                "copy expert counts");
   }
-  ep_publish_meta_kernel<<<1, kExperts, 0, s>>>(dv, counts);
-  check_cuda(cudaGetLastError(), "ep_publish_meta launch");
-  ep_plan_kernel<<<1, 32, 0, s>>>(dv);
-  check_cuda(cudaGetLastError(), "ep_plan launch");
+  ep_counts_plan_kernel<<<1, kExperts, 0, s>>>(dv, counts);
+  check_cuda(cudaGetLastError(), "ep_counts_plan launch");
   trace("ep_counts_plan", s);
   const int copy_grid = std::max(1, std::min(4 * sm_count(), (batch * 2 * (d / 8) + 255) / 256));
   ep_push_rows_kernel<<<copy_grid, 256, 0, s>>>(dv, xperm, pprob, expert_start);
