@@ -178,11 +178,13 @@ __device__ __forceinline__ void copy_rows(bf16* dst, const bf16* src, float* dst
 }
 
 // The last CTA to finish raises the phase's flag on the given ranks. The barrier orders the
-// CTA's stores before thread 0's system-scope fence, which orders them before its count.
+// CTA's stores before thread 0's GPU-scope fence and count; the last CTA's system-scope fence
+// then orders every CTA's stores (they happen before it) before the flags, so one system
+// fence a push is paid instead of one a CTA.
 __device__ __forceinline__ void finish_push(const EpDev& dv, int counter, int phase, bool to_all) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    fence_acq_rel_sys();
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     const int old = atomicAdd(dv.done + counter, 1);
     if (old == static_cast<int>(gridDim.x) - 1) {
       dv.done[counter] = 0;
