@@ -162,3 +162,41 @@ def test_small_batch_lc0_records_expanded_in_kernel_match_plane_layouts(hist: in
     assert model._native.uses_latency_path(batch)
     for x, y in ((a.policy_logits, e.policy_logits), (a.wdl_logits, e.wdl_logits), (a.moves_left, e.moves_left)):
         assert torch.equal(x, y)
+
+
+def test_small_batch_async_copy_free_and_copy_calls_interleave(tmp_path) -> None:
+    """Small-batch evaluate_async calls on two streams, alternating the copy-free path
+    (pinned buffers, kernels reading and writing host memory) and the copy path, give the
+    blocking evaluate's results: the forwards share the model's workspace and are ordered
+    across streams whichever path a call takes."""
+
+    from ce4b200 import DenseChessNet, DenseChessNetConfig, Engine, _lib, export_model, synthetic
+
+    d, depth = 256, 2
+    weights = synthetic.make_dense_weights(d_model=d, depth=depth, hidden_dim=3 * d, seed=21)
+    model = DenseChessNet(DenseChessNetConfig(d_model=d, depth=depth, expansion_ratio=3.0, precision="bf16"))
+    synthetic.load_into(model, weights)
+    path = tmp_path / "m.safetensors"
+    export_model(model, path)
+    engine = Engine.load(path, gpu=0, max_batch=256)
+    sizes = [64, 48, 64, 17, 64, 30, 1, 64]
+    batches = [synthetic.lc0_planes_tensor(synthetic.make_lc0_planes(b, 60 + i)).pin_memory()
+               for i, b in enumerate(sizes)]
+    expected = [engine.evaluate(p) for p in batches]  # pageable outputs: copy path
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [engine.outputs(int(p.shape[0]), pin=True) for p in batches]
+    for rep in range(2):
+        for o in outs:
+            for t in o:
+                t.fill_(float("nan"))
+        for i, (p, o) in enumerate(zip(batches, outs)):
+            engine.set_direct_io(i % 2 == rep)
+            engine.evaluate_async(p, o, streams[i % 2])
+        for s in streams:
+            s.synchronize()
+        for got, exp in zip(outs, expected):
+            for x, y in zip(got, exp):
+                assert torch.equal(x, y)
+    engine.set_direct_io(True)
+    assert _lib.check_device_error(0) == 0
+    engine.close()
