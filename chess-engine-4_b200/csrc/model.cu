@@ -810,9 +810,26 @@ cudaGraphExec_t Model::evaluate_graph(int batch, int slot) {
 
 namespace {
 
+using PointerAttributeFn = CUresult (*)(void*, CUpointer_attribute, CUdeviceptr);
+
+PointerAttributeFn pointer_attribute_fn() {
+  static PointerAttributeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuPointerGetAttribute", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PointerAttributeFn>(p);
+    }
+  });
+  return fn;
+}
+
 // The device address of host buffer [ptr, ptr + bytes) when it is pinned and mapped for the
-// current device over its whole extent (its first and last byte resolve to device
-// addresses the same distance apart), else nullptr.
+// current device over its whole extent, else nullptr: its first and last byte must both be
+// mapped, lie in one CUDA allocation or registration (the same process-unique buffer id, so
+// no unmapped hole can sit between them) and resolve to device addresses bytes - 1 apart.
 void* mapped_view(const void* ptr, size_t bytes) {
   auto view = [](const void* p) -> char* {
     cudaPointerAttributes a{};
@@ -822,10 +839,18 @@ void* mapped_view(const void* ptr, size_t bytes) {
     }
     return a.type == cudaMemoryTypeHost ? static_cast<char*>(a.devicePointer) : nullptr;
   };
+  auto buffer_id = [](const void* p, unsigned long long* id) {
+    const PointerAttributeFn fn = pointer_attribute_fn();
+    return fn != nullptr &&
+           fn(id, CU_POINTER_ATTRIBUTE_BUFFER_ID, reinterpret_cast<CUdeviceptr>(p)) == CUDA_SUCCESS;
+  };
   if (ptr == nullptr || bytes == 0) return nullptr;
+  const void* end = static_cast<const char*>(ptr) + bytes - 1;
   char* first = view(ptr);
-  char* last = view(static_cast<const char*>(ptr) + bytes - 1);
+  char* last = view(end);
   if (first == nullptr || last == nullptr || last - first != static_cast<ptrdiff_t>(bytes - 1)) return nullptr;
+  unsigned long long id_first = 0, id_last = 0;
+  if (!buffer_id(ptr, &id_first) || !buffer_id(end, &id_last) || id_first != id_last) return nullptr;
   return first;
 }
 
