@@ -145,9 +145,9 @@ int ce4b_model_forward(ce4b_model* model, int input_layout, void* input_dev,
  * Batches that take the small-batch forward skip the copies when all four host buffers are
  * pinned and mapped for the model's device over their whole extent, each inside one
  * cudaHostAlloc allocation or cudaHostRegister registration (e.g. torch pin_memory): the
- * expansion kernel reads the
- * records from host memory and the heads write the outputs into the caller's buffers
- * (one CUDA graph per batch size and buffer set, built on first use, which blocks).
+ * expansion kernel reads the records from host memory and the heads write the outputs
+ * into the caller's buffers (one CUDA graph per batch size and buffer set, built on first
+ * use, which blocks).
  * Results are identical either way. Other buffers take the copy path. */
 int ce4b_model_evaluate(ce4b_model* model, const ce4b_input_plane* host_planes, int batch,
                         float* host_policy, float* host_wdl, float* host_moves_left);
