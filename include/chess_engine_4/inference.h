@@ -78,7 +78,9 @@ class Model {
   const ModelInfo& info() const { return info_; }
 
   // planes: batch_size * 112 records; outputs sized batch_size * {policy_size, 3, 1}.
-  // Not thread-safe (serialise calls on one model, as lc0 does with its mutex).
+  // Not thread-safe (serialise calls on one model, as lc0 does with its mutex). Spans over
+  // pinned, mapped host memory (cudaHostAlloc / cudaHostRegister) let small batches run
+  // without copies (see ce4b_model_evaluate).
   void Evaluate(std::span<const InputPlane> planes, int batch_size, Outputs outputs) {
     if (batch_size < 1 || batch_size > info_.maximum_batch_size) {
       throw std::runtime_error("ce4b200: batch size out of range");
