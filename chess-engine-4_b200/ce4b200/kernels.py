@@ -129,16 +129,20 @@ def dense_block_forward(
 
     Same arguments and checks as the reference operator
     (src/chess_engine_4/kernels/dense.py:141-160, 357-392), except that any expansion
-    ratio whose hidden width is a multiple of 64 is accepted (the reference custom path
-    requires ratio 4).
+    ratio whose hidden width is a multiple of 64 (128 for MXFP8) is accepted (the
+    reference custom path requires ratio 4).
+
+    ``precision="mxfp8"`` follows the reference's recipe step by step (dense.py:395-407):
+    the RMSNorm output and both weights are quantised per call (``quantize_mxfp8``), the
+    gate_up product is a block-scaled GEMM with a BF16 output, SwiGLU runs in BF16, the
+    hidden activations and the down weight are quantised and multiplied the same way, and
+    the residual is added last; every step is one of this library's kernels.
     """
 
     _check_bf16_matrix("x", x)
     d_model = x.shape[1]
     if precision not in ("bf16", "mxfp8"):
         raise ValueError(f"custom dense kernel does not support precision={precision!r}")
-    if precision != "bf16":
-        raise ValueError("dense_block_forward: only precision='bf16' is available")
     _check_bf16_vector("norm_weight", norm_weight, d_model)
     _check_bf16_matrix("gate_up_weight", gate_up_weight)
     _check_bf16_matrix("down_weight", down_weight)
@@ -147,6 +151,15 @@ def dense_block_forward(
         raise ValueError(f"gate_up_weight must have shape [{2 * hidden_dim}, {d_model}]")
     if tuple(down_weight.shape) != (d_model, hidden_dim):
         raise ValueError(f"down_weight must have shape [{d_model}, {hidden_dim}]")
+    if precision == "mxfp8":
+        for name, t in (("x", x), ("gate_up_weight", gate_up_weight), ("down_weight", down_weight)):
+            if any(size % MXFP8_TILE_SIZE for size in t.shape):
+                raise ValueError(f"{name} dimensions must be multiples of {MXFP8_TILE_SIZE}")
+        normalized = rmsnorm_forward(x, norm_weight, eps)
+        gate_up = mxfp8_gemm(quantize_mxfp8(normalized), quantize_mxfp8(gate_up_weight))
+        hidden = swiglu_forward(gate_up)
+        projected = mxfp8_gemm(quantize_mxfp8(hidden), quantize_mxfp8(down_weight))
+        return residual_add(projected, x)
     lib = _lib.library()
     rows = x.shape[0]
     ws_bytes = lib.ce4b_dense_block_workspace_size(rows, d_model, hidden_dim)

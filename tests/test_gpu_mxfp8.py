@@ -52,6 +52,47 @@ def test_mxfp8_gemm_matches_dequantised_product(m: int, n: int, k: int) -> None:
     torch.testing.assert_close(c.float().cpu(), ref, atol=1e-3 * float(ref.abs().max()), rtol=8e-3)
 
 
+@pytest.mark.parametrize("rows,d", [(256, 256), (384, 512)])
+def test_dense_block_forward_mxfp8_follows_the_reference_recipe(rows: int, d: int) -> None:
+    """kernels.dense_block_forward(precision="mxfp8") against the reference's recipe
+    restated on the CPU with the oracle quantiser (src/chess_engine_4/kernels/dense.py:
+    395-407): RMSNorm, per-call quantisation of the normalised rows and both weights,
+    block-scaled gate_up GEMM to BF16, SwiGLU, quantised hidden times quantised down weight
+    to BF16, residual. x ~ N(0, 1) BF16 with seed 2026 and ratio 4, as the reference's
+    dense kernel harness draws them (kernels/dense_benchmark.py)."""
+
+    from ce4b200 import kernels
+    from oracle import mxfp8
+
+    h = 4 * d
+    g = torch.Generator().manual_seed(2026)
+    x = torch.randn(rows, d, generator=g).bfloat16()
+    nw = (1 + 0.1 * torch.randn(d, generator=g)).bfloat16()
+    wgu = (torch.randn(2 * h, d, generator=g) / d**0.5).bfloat16()
+    wd = (torch.randn(d, h, generator=g) / h**0.5).bfloat16()
+    out = kernels.dense_block_forward(x.cuda(), nw.cuda(), wgu.cuda(), wd.cuda(), precision="mxfp8")
+    torch.cuda.synchronize()
+
+    def mx(t: torch.Tensor) -> torch.Tensor:
+        return mxfp8.dequantize(*mxfp8.quantize(t.bfloat16())).double()
+
+    xf = x.float()
+    n = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * nw.float()).bfloat16()
+    gu = (mx(n) @ mx(wgu).T).float().bfloat16().float()
+    gate, up = gu[:, :h], gu[:, h:]
+    hidden = (gate / (1 + torch.exp(-gate)) * up).bfloat16()
+    proj = (mx(hidden) @ mx(wd).T).float().bfloat16().float()
+    ref = (xf + proj).bfloat16().float()
+    got = out.float().cpu()
+    err = (got - ref).abs()
+    print(f"dense block MXFP8 {rows}x{d}: max {float(err.max()):.4g}, within 1e-2: "
+          f"{float((err <= 1e-2).float().mean()):.4f}")
+    # The restatement quantises the same BF16 values the same way; only FP32 accumulation
+    # order, the SFU SiLU and the rare E4M3 code those move across a rounding boundary differ.
+    assert float((err <= 1e-2).float().mean()) >= 0.99
+    torch.testing.assert_close(got, ref, atol=6e-2, rtol=2e-2)
+
+
 @pytest.mark.parametrize("d,depth,ratio,batch", [(256, 2, 3.0, 256), (512, 12, 3.0, 1024), (512, 2, 3.0, 2048)])
 def test_mxfp8_model_matches_oracle(d: int, depth: int, ratio: float, batch: int) -> None:
     from ce4b200 import DenseChessNet, DenseChessNetConfig, synthetic
