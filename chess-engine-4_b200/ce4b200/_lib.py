@@ -152,6 +152,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp],
     ),
     "ce4b_quantize_mxfp8": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
+    "ce4b_quantize_mxfp8_transpose": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp]),
     "ce4b_mxfp8_gemm": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "ce4b_dense_block_forward_static": (
         _i32,

@@ -220,6 +220,23 @@ def quantize_mxfp8(tensor: torch.Tensor) -> Mxfp8Tensor:
     return Mxfp8Tensor(values=values, scales=scales)
 
 
+def quantize_mxfp8_transpose(tensor: torch.Tensor) -> Mxfp8Tensor:
+    """MXFP8 quantisation of ``tensor.T`` without materialising the BF16 transpose
+    (kernels/dense.py:63-84): values [cols, rows], scales [cols/128, rows/128, 32, 16]."""
+
+    _check_mx_matrix("tensor", tensor)
+    rows, cols = tensor.shape
+    values = torch.empty(cols, rows, dtype=torch.float8_e4m3fn, device=tensor.device)
+    scales = torch.empty(cols // 128, rows // 128, 32, 16, dtype=torch.uint8, device=tensor.device)
+    with torch.cuda.device(tensor.device):
+        _lib.check(
+            _lib.library().ce4b_quantize_mxfp8_transpose(
+                tensor.data_ptr(), values.data_ptr(), scales.data_ptr(), rows, cols, _stream(tensor)
+            )
+        )
+    return Mxfp8Tensor(values=values, scales=scales)
+
+
 def mxfp8_gemm(left: Mxfp8Tensor, right: Mxfp8Tensor) -> torch.Tensor:
     """``dequant(left) @ dequant(right).T`` in BF16 on block-scaled tcgen05 MMAs
     (replaces kernels/dense.py:87-113; any output width divisible by 128)."""

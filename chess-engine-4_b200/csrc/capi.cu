@@ -567,6 +567,16 @@ int ce4b_quantize_mxfp8(const void* x_dev, void* codes_dev, void* scales_dev, in
   });
 }
 
+int ce4b_quantize_mxfp8_transpose(const void* x_dev, void* codes_dev, void* scales_dev, int rows,
+                                  int cols, void* stream) {
+  return guarded([&] {
+    require(x_dev && codes_dev && scales_dev, "null pointer");
+    require(rows >= 128 && cols >= 128, "MXFP8 tensors need at least 128 rows and columns");
+    mx_quantize_transpose(static_cast<const bf16*>(x_dev), static_cast<uint8_t*>(codes_dev),
+                          static_cast<uint8_t*>(scales_dev), rows, cols, as_stream(stream));
+  });
+}
+
 int ce4b_mxfp8_gemm(const void* a_codes_dev, const void* a_scales_dev, const void* b_codes_dev,
                     const void* b_scales_dev, void* c_dev, int m, int n, int k, void* stream) {
   return guarded([&] {

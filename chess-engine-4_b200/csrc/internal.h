@@ -123,6 +123,9 @@ void bf16_to_f32(const bf16* in, float* out, int n, cudaStream_t s);
 // BF16 [rows, cols] -> E4M3 codes [rows, cols] + E8M0 scales [rows/128][cols/128][512].
 void mx_quantize(const bf16* x, uint8_t* codes, uint8_t* scales, int rows, int cols,
                  cudaStream_t s);
+// The same for the transpose: codes [cols, rows] + scales [cols/128][rows/128][512].
+void mx_quantize_transpose(const bf16* x, uint8_t* codes, uint8_t* scales, int rows, int cols,
+                           cudaStream_t s);
 // 2-D byte (E4M3 code) tensor map, 128-byte swizzle, box = 128 codes x box_rows.
 CUtensorMap make_tmap_u8(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_bytes,
                          uint32_t box_rows);

@@ -398,6 +398,13 @@ int ce4b_moe_forward(const void* x_dev, const void* gate_up_weight_dev,
 int ce4b_quantize_mxfp8(const void* x_dev, void* codes_dev, void* scales_dev, int rows, int cols,
                         void* stream);
 
+/* The quantisation of the transpose of a BF16 [rows, cols] matrix without materialising it:
+ * codes [cols, rows] and scales [cols/128, rows/128, 32, 16], equal to ce4b_quantize_mxfp8 of
+ * the transposed matrix. Replaces quantize_mxfp8_transpose
+ * (src/chess_engine_4/kernels/dense.py:63-84). */
+int ce4b_quantize_mxfp8_transpose(const void* x_dev, void* codes_dev, void* scales_dev, int rows,
+                                  int cols, void* stream);
+
 /* C[M,N] BF16 = sum over 32-element K blocks of (A codes * 2^(sa-127)) (B codes *
  * 2^(sb-127)), FP32 accumulate: A, B E4M3 codes [M,K], [N,K] with scales in the
  * ce4b_quantize_mxfp8 layout; M, N, K multiples of 128. Block-scaled tcgen05 MMA

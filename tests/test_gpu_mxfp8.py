@@ -33,6 +33,22 @@ def test_quantizer_bit_exact(rows: int, cols: int) -> None:
     assert torch.equal(q.scales.cpu(), ref_scales)
 
 
+@pytest.mark.parametrize("rows,cols", [(128, 128), (128, 384), (384, 1536), (512, 128)])
+def test_transposed_quantizer_bit_exact(rows: int, cols: int) -> None:
+    """quantize_mxfp8_transpose(x) equals the quantisation of x.T (kernels/dense.py:63-84)."""
+
+    from ce4b200 import kernels
+    from oracle import mxfp8
+
+    x = _sample(rows, cols, 7 * rows + cols)
+    q = kernels.quantize_mxfp8_transpose(x.cuda())
+    torch.cuda.synchronize()
+    ref_codes, ref_scales = mxfp8.quantize(x.T.contiguous())
+    assert q.values.shape == (cols, rows) and q.scales.shape == (cols // 128, rows // 128, 32, 16)
+    assert torch.equal(q.values.view(torch.uint8).cpu(), ref_codes)
+    assert torch.equal(q.scales.cpu(), ref_scales)
+
+
 @pytest.mark.parametrize("m,n,k", [(128, 128, 128), (256, 384, 512), (4096, 3072, 512), (512, 512, 1536)])
 def test_mxfp8_gemm_matches_dequantised_product(m: int, n: int, k: int) -> None:
     from ce4b200 import kernels
