@@ -19,13 +19,25 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("d,depth,batch,repeats", [(256, 2, 700, 1), (768, 4, 4096, 3)])
-def test_expert_parallel_forward_equals_single_gpu(d: int, depth: int, batch: int, repeats: int) -> None:
+def _gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize(
+    "world,d,depth,batch,repeats",
+    [
+        pytest.param(2, 256, 2, 700, 1),
+        pytest.param(2, 768, 4, 4096, 3),
+        # 8 experts a GPU, the expert split the c3 configuration names.
+        pytest.param(8, 768, 4, 2048, 2, marks=pytest.mark.skipif(_gpus() < 8, reason="needs 8 GPUs")),
+    ],
+)
+def test_expert_parallel_forward_equals_single_gpu(world: int, d: int, depth: int, batch: int, repeats: int) -> None:
     from ce4b200 import Moe64A2ChessNet, Moe64A2ChessNetConfig, _lib, replicas, synthetic
     from dist_worker import collect, ep_forward_worker
 
-    world = 2
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
     unique_id = _lib.nccl_unique_id()
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
